@@ -1,0 +1,428 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 W8A8 linear hot path (BASELINE.json configs 1 and 2).
+
+A step is one pass of the prefill linear set of a 35-layer Gemma E2B-class decoder over
+one prompt of M = 3658 tokens (config 1): per layer the qkv (1536->2560), o (2048->1536),
+gate_up (1536->12288) and down (6144->1536) W8A8 GEMMs, plus the PLE model projection
+(1536->8960), each int8 x int8 -> exact int32 as the reference's mm_i8 / torch._int_mm
+produce it.  Weights are random N(0, 0.02) quantised per channel and activations random
+N(0, 1) quantised per token, seeded per layer, distinct buffers per layer (synthetic data:
+no checkpoint is available).  The step is captured once into a CUDA graph and replayed.
+
+`value` is whole-job TOPS with inputs resident in HBM; `e2e` is the same metric through
+the reference-facing API with host buffers (pinned int8 activations copied in, int32
+results copied out every step, as the reference's CPU glue consumes them).  The decode
+weight-only GEMV chain (config 2: the same 140 layer weights + the 262144-wide LM head
+with the softcap fused) is reported beside it in GB/s.
+
+With torchrun (N > 1) every rank runs its own prompt (weak scaling, no collective on the
+data path); time is the max over ranks.  `--impl reference` times the reference's own
+CPU implementation of the path (its `cpu-int8` backend: torch._int_mm) on the host cores.
+
+usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+LAYERS = 35
+M_TOKENS = 3658
+LAYER_SHAPES = [("qkv", 2560, 1536), ("o", 1536, 2048), ("gate_up", 12288, 1536), ("down", 1536, 6144)]
+PLE_SHAPE = ("ple_model", 8960, 1536)
+VOCAB, HIDDEN, SOFTCAP = 262144, 1536, 30.0
+INT8_PER_BF16 = 2.0  # dense int8 tensor rate / dense bf16 rate on B200 (4.5 / 2.25 PFLOP/s nominal)
+NOMINAL_INT8_TOPS = 4500.0
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def macs_per_token():
+    return LAYERS * sum(n * k for _, n, k in LAYER_SHAPES) + PLE_SHAPE[1] * PLE_SHAPE[2]
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ----------------------------------------------------------------------------- setup
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if world == 1 and args.gpus > 1:
+        raise SystemExit("--gpus > 1 needs torchrun (one process per GPU)")
+    return world, rank, local
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]), "source": "measured"}
+    return dict(FALLBACK, source="fallback")
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.proc, self.path = None, None
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            self.fh = os.fdopen(fd, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(index), "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) == 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- workloads
+def build_prefill(w8, dev, m, only=None, seed=0):
+    """Per layer: resident int8 [N,K] weights and int8 [M,K] activations; shared int32 outputs."""
+    shapes = [s for s in LAYER_SHAPES if only in (None, s[0])]
+    calls, weights = [], []
+    outs = {name: torch.empty((m, n), dtype=torch.int32, device=dev) for name, n, _ in shapes + [PLE_SHAPE]}
+    acts = []
+    for layer in range(LAYERS):
+        g = torch.Generator(device=dev).manual_seed(seed * 1000 + layer)
+        per = {}
+        for name, n, k in shapes:
+            wq, _ = w8.quant_rows(torch.randn((n, k), device=dev, generator=g, dtype=torch.bfloat16) * 0.02)
+            xq, _ = w8.quant_rows(torch.randn((m, k), device=dev, generator=g, dtype=torch.bfloat16))
+            calls.append((xq, wq, outs[name], name))
+            per[name] = wq
+            acts.append(xq)
+        weights.append(per)
+    if only in (None, PLE_SHAPE[0]):
+        g = torch.Generator(device=dev).manual_seed(seed * 1000 + 999)
+        name, n, k = PLE_SHAPE
+        wq, _ = w8.quant_rows(torch.randn((n, k), device=dev, generator=g, dtype=torch.bfloat16) * 0.02)
+        xq, _ = w8.quant_rows(torch.randn((m, k), device=dev, generator=g, dtype=torch.bfloat16))
+        calls.append((xq, wq, outs[name], name))
+    torch.cuda.synchronize()
+    ops = sum(2 * xq.shape[0] * wq.shape[0] * wq.shape[1] for xq, wq, _, _ in calls)
+    return {"calls": calls, "weights": weights, "ops": ops, "outs": outs}
+
+
+def capture(fn, stream):
+    """Run fn once eagerly (sets kernel attributes), then capture it into a CUDA graph."""
+    with torch.cuda.stream(stream):
+        fn()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        fn()
+    return graph
+
+
+def timed(replay, steps, warmup, stream, world):
+    """Warm up, then time exactly `steps` replays with CUDA events; max over ranks (ms)."""
+    import torch.distributed as dist
+
+    for _ in range(warmup):
+        replay()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        replay()
+    end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end)
+    torch.cuda.synchronize()
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def e2e_prefill(w8, work, dev, steps, warmup, world):
+    """Host-buffer path: per GEMM, pinned int8 activations -> HBM, GEMM, int32 result -> pinned host."""
+    import torch.distributed as dist
+
+    host_in, host_out = {}, {}
+    for xq, wq, c, name in work["calls"]:
+        if name not in host_in:
+            host_in[name] = xq.cpu().pin_memory()
+            host_out[name] = torch.empty(c.shape, dtype=torch.int32).pin_memory()
+    stream = torch.cuda.current_stream()
+    bi = sum(xq.numel() for xq, _, _, _ in work["calls"])
+    bo = sum(4 * c.numel() for _, _, c, _ in work["calls"])
+
+    def step():
+        for xq, wq, c, name in work["calls"]:
+            xq.copy_(host_in[name], non_blocking=True)
+            w8.mm_i8_nk(xq, wq, c)
+            host_out[name].copy_(c, non_blocking=True)
+        stream.synchronize()  # the results are on the host when the step ends
+
+    for _ in range(warmup):
+        step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms / steps, bi, bo
+
+
+def build_decode(w8, work, dev):
+    """The decode GEMV chain over the prefill's resident weights + an int8 LM head."""
+    g = torch.Generator(device=dev).manual_seed(4242)
+    chain, nbytes = [], 0
+    for per in work["weights"]:
+        for name, n, k in LAYER_SHAPES:
+            wq = per[name]
+            s = (torch.rand((n,), device=dev, generator=g) * 1e-3 + 1e-4).to(torch.bfloat16)
+            x = torch.randn((1, k), device=dev, generator=g).to(torch.bfloat16)
+            y = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
+            chain.append((x, wq, s, y))
+            nbytes += n * k + 2 * n + 2 * k + 2 * n
+    hw, hs = w8.quant_rows(torch.randn((VOCAB, HIDDEN), device=dev, generator=g, dtype=torch.bfloat16) * 0.02)
+    head = (torch.randn((HIDDEN,), device=dev, generator=g).to(torch.bfloat16), hw, hs.to(torch.bfloat16),
+            torch.empty((VOCAB,), dtype=torch.float32, device=dev))
+    nbytes += VOCAB * HIDDEN + 2 * VOCAB + 2 * HIDDEN + 4 * VOCAB
+    torch.cuda.synchronize()
+
+    def step():
+        for x, wq, s, y in chain:
+            w8.int8_linear(x, wq, s, out=y)
+        h, hq, hsc, logits = head
+        w8.lm_head_logits(h, hq, hsc, SOFTCAP, out=logits)
+
+    return step, nbytes, len(chain) + 1, head
+
+
+# ----------------------------------------------------------------------------- CPU reference
+def cpu_reference_step(m, layers, seed=0):
+    """The reference's cpu-int8 prefill GEMMs (torch._int_mm) over `layers` layers; returns ops."""
+    from oracle import cpu_int8
+
+    g = torch.Generator().manual_seed(seed)
+    data = []
+    for _ in range(layers):
+        for _, n, k in LAYER_SHAPES:
+            xq, _ = cpu_int8.quant(torch.randn(m, k, generator=g).to(torch.bfloat16))
+            w_kn = cpu_int8.weight_quant(torch.randn(n, k, generator=g) * 0.02)[2]
+            data.append((xq, w_kn))
+    ops = sum(2 * m * w.shape[1] * w.shape[0] for _, w in data)
+
+    def run():
+        for xq, w_kn in data:
+            cpu_int8.int_mm(xq, w_kn)
+
+    return run, ops
+
+
+def cpu_reference_rate(m, target_s=10.0, max_layers=35):
+    """TOPS of the reference CPU path on a bounded sample of config 1, sized to ~target_s."""
+    from oracle import cpu_int8
+
+    cores = cpu_int8.set_threads()
+    run1, ops1 = cpu_reference_step(m, 1)
+    run1()
+    t = time.perf_counter()
+    run1()
+    per_layer = time.perf_counter() - t
+    reps = max(1, min(int(target_s / max(per_layer, 1e-6)), max_layers))
+    layers = min(reps, max_layers)
+    run, ops = cpu_reference_step(m, layers, seed=1)
+    run()  # warm-up
+    t = time.perf_counter()
+    run()
+    dt = time.perf_counter() - t
+    return {"value": ops / dt / 1e12, "unit": "TOPS", "cores": cores, "kind": "port",
+            "sample": f"{layers} of {LAYERS} layers x 4 GEMMs (torch._int_mm, M={m}), one timed pass of {dt:.2f} s"}
+
+
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    from oracle import cpu_int8
+
+    cores = cpu_int8.set_threads()
+    run1, _ = cpu_reference_step(args.m, 1)
+    run1()
+    t = time.perf_counter()
+    run1()
+    per_layer = time.perf_counter() - t
+    # each step a bounded sample of the layer set so the whole run stays within minutes
+    layers = max(1, min(LAYERS, int(args.ref_step_s / max(per_layer, 1e-6))))
+    run, ops = cpu_reference_step(args.m, layers, seed=1)
+    for _ in range(args.warmup):
+        run()
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    dt = (time.perf_counter() - t) / args.steps
+    tops = ops / dt / 1e12
+    step_ms_full = dt * 1e3 * macs_per_token() * 2 * args.m / ops  # projected to the full layer set
+    sample = f"{layers} of {LAYERS} layers x 4 GEMMs per step (torch._int_mm, M={args.m}); PLE projection omitted"
+    line = {"metric": "W8A8 GEMM TOPS, prefill linear set @3658 tok (config 1)", "value": tops, "unit": "TOPS",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "ms_full_layer_set": step_ms_full, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"config 1: 35-layer prefill linear set, M={args.m} (sampled)",
+                       "parallelism": "cpu"},
+            "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--m", type=int, default=M_TOKENS, help="tokens per prompt (rows of every GEMM)")
+    ap.add_argument("--only", default=None, help="profile one projection shape only (qkv/o/gate_up/down/ple_model)")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--decode-steps", type=int, default=200)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-step-s", type=float, default=4.0, help="CPU seconds per reference-arm step")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    world, rank, local = dist_setup(args)
+
+    if args.impl == "reference":
+        run_reference_arm(args, world, rank)
+        return
+
+    import importlib
+    import torch.distributed as dist
+
+    w8 = importlib.import_module("gemma-npu_b200")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        pk = peaks()
+        work = build_prefill(w8, dev, args.m, only=args.only, seed=rank)
+        stream = torch.cuda.Stream(device=dev)
+
+        def prefill_step():
+            for xq, wq, c, _ in work["calls"]:
+                w8.mm_i8_nk(xq, wq, c)
+
+        graph = capture(prefill_step, stream)
+        sampler = ClockSampler(local) if rank == 0 else None
+        ms = timed(lambda: graph.replay(), args.steps, args.warmup, stream, world)
+        clocks = sampler.stop() if sampler else None
+        ms_step = ms / args.steps
+        tops_rank = work["ops"] / (ms_step * 1e-3) / 1e12
+        value = world * tops_rank  # each rank processed one prompt per step
+        int8_peak = INT8_PER_BF16 * pk["bf16_tflops"]
+        line = {
+            "metric": "W8A8 GEMM TOPS, prefill linear set @3658 tok (config 1)"
+            if args.only is None else f"W8A8 GEMM TOPS, {args.only} @M={args.m}",
+            "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic (seeded N(0,1) activations / N(0,0.02) weights, W8A8-quantised)",
+            "config": {"workload": f"config 1: 35 layers x (qkv, o, gate_up, down) + PLE model projection, "
+                                   f"M={args.m} tokens per rank", "m_tokens": args.m,
+                       "gemms_per_step": len(work["calls"]), "parallelism": f"dp{world} (one prompt per GPU)",
+                       "l2": "no flush: every step streams 1.24 GB of weights, 1.45 GB of activations and "
+                             "9.3 GB of int32 outputs (>> 126 MB L2)"},
+            "pct_int8_peak": 100.0 * tops_rank / int8_peak,
+            "pct_int8_nominal": 100.0 * tops_rank / NOMINAL_INT8_TOPS,
+            "gpu_launches": args.steps * len(work["calls"]),
+            "roofline": {"bound": "tensor", "achieved": tops_rank, "peak": int8_peak, "unit": "TOP/s",
+                         "frac": tops_rank / int8_peak, "traffic": None,
+                         "peak_note": f"2 x {pk['source']} dense bf16 {pk['bf16_tflops']} TFLOP/s (B200 int8 = 2x bf16)"},
+            "clocks": clocks,
+        }
+        del graph
+        if not args.no_e2e and args.only is None:
+            e_ms, bi, bo = e2e_prefill(w8, work, dev, args.e2e_steps, 1, world)
+            line["e2e"] = {"value": world * work["ops"] / (e_ms * 1e-3) / 1e12, "unit": "TOPS",
+                           "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo, "ms_per_step": e_ms,
+                           "steps": args.e2e_steps,
+                           "path": "gemma_npu_b200.mm_i8_nk per GEMM: pinned int8 activations H2D, int32 results D2H"}
+        if not args.no_decode and args.only is None:
+            step, nbytes, launches, _ = build_decode(w8, work, dev)
+            dgraph = capture(step, stream)
+            dms = timed(lambda: dgraph.replay(), args.decode_steps, args.warmup, stream, world)
+            per = dms / args.decode_steps
+            gbs = nbytes / (per * 1e-3) / 1e9
+            line["decode_gemv"] = {
+                "metric": "int8 GEMV GB/s, decode chain (config 2: 140 layer GEMVs + LM head 262144x1536, softcap)",
+                "value": world * gbs, "unit": "GB/s", "ms_per_token": per, "bytes_per_token": nbytes,
+                "launches_per_token": launches,
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                             "frac": gbs / pk["hbm_gbs"], "traffic": None,
+                             "peak_note": f"{pk['source']} HBM copy bandwidth"}}
+            del dgraph
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_reference_rate(args.m)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,229 @@
+// Weight-only int8 GEMV for decode and the LM head (sm_100a).
+//
+// Reference behaviour replaced: cpu_int8_linear (gemma_npu.py:155-156), i.e.
+// torch._weight_int8pack_mm(x_bf16 [T,K], w int8 [N,K], s bf16 [N]) -> bf16 [T,N]:
+//     y[t,n] = bf16(float(s[n]) * sum_k float(x[t,k]) * float(w[n,k]))
+// and, for the LM head, Int8Head.forward (gemma_npu.py:170-172) followed by the final
+// logit softcap of the prefill (pipeline.py:335-338): cap * tanh(float(y) / cap).
+//
+// The kernel is HBM-bound: every weight byte is read once with 16-byte non-allocating
+// loads, coalesced across the warp.  The activation row is converted to fp32 once per
+// thread and kept in registers: lane l of the warp owning K-slice `sl` multiplies the
+// 16 consecutive k of chunk c, k = ((sl*J + c)*32 + l)*16 .. +15, of every weight row it
+// visits.  S warps ("a team") split K; the team's partial sums meet in shared memory.
+// int8 -> fp32 uses the exponent trick: byte b (offset to b+128) is placed in the
+// mantissa of 2^23 with one PRMT and the bias removed with one FADD, exactly.
+#include "common.cuh"
+
+namespace w8 {
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// acc += sum over the 4 signed bytes of `word` times x[0..3].
+__device__ __forceinline__ float dot4_i8(uint32_t word, const float* x, float acc) {
+  const uint32_t u = word ^ 0x80808080u;  // b + 128 in each byte
+  constexpr float kBias = 8388736.0f;     // 2^23 + 128
+  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - kBias;
+  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - kBias;
+  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - kBias;
+  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - kBias;
+  acc = fmaf(f0, x[0], acc);
+  acc = fmaf(f1, x[1], acc);
+  acc = fmaf(f2, x[2], acc);
+  acc = fmaf(f3, x[3], acc);
+  return acc;
+}
+
+// Output of one row: bf16 of the scaled sum, optionally softcapped to fp32.
+template <bool LOGITS>
+__device__ __forceinline__ void write_out(void* y, int64_t idx, float acc, __nv_bfloat16 s,
+                                          float cap) {
+  const __nv_bfloat16 v = __float2bfloat16_rn(__fmul_rn(acc, __bfloat162float(s)));
+  if constexpr (LOGITS) {
+    float f = __bfloat162float(v);
+    if (cap > 0.f) f = __fmul_rn(tanhf(__fdiv_rn(f, cap)), cap);
+    static_cast<float*>(y)[idx] = f;
+  } else {
+    static_cast<__nv_bfloat16*>(y)[idx] = v;
+  }
+}
+
+// J: 16-byte chunks per lane per row; S: warps splitting K; R: rows per team per step.
+template <int J, int S, int R, bool LOGITS>
+__global__ void __launch_bounds__(kGemvThreads)
+    int8_gemv_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                     const int8_t* __restrict__ w, int64_t ldw, const __nv_bfloat16* __restrict__ s,
+                     void* __restrict__ y, int64_t ldy, int t_count, int n, int k, float cap) {
+  static_assert(kGemvWarps % S == 0, "S must divide the CTA's warps");
+  constexpr int kTeams = kGemvWarps / S;
+  __shared__ float red[kTeams][S][R];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int team = warp / S;
+  const int sl = warp % S;
+
+  for (int t = 0; t < t_count; ++t) {
+    // This lane's slice of the activation row, in fp32.
+    float xr[J][16];
+#pragma unroll
+    for (int c = 0; c < J; ++c) {
+      const int k0 = ((sl * J + c) * 32 + lane) * 16;
+      if (k0 < k) {
+        const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * ldx + k0);
+        const uint4 a = __ldg(p), b = __ldg(p + 1);
+        const uint32_t words[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          xr[c][2 * i] = __uint_as_float(words[i] << 16);
+          xr[c][2 * i + 1] = __uint_as_float(words[i] & 0xFFFF0000u);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) xr[c][i] = 0.f;
+      }
+    }
+
+    const int stride = gridDim.x * kTeams * R;
+    for (int n0 = (blockIdx.x * kTeams + team) * R; n0 < n; n0 += stride) {
+      uint4 wv[R][J];
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int c = 0; c < J; ++c) {
+          const int k0 = ((sl * J + c) * 32 + lane) * 16;
+          const int row = n0 + r;
+          wv[r][c] = (row < n && k0 < k) ? ldg_stream(w + static_cast<int64_t>(row) * ldw + k0)
+                                         : make_uint4(0u, 0u, 0u, 0u);
+        }
+      float acc[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < J; ++c) {
+          a0 = dot4_i8(wv[r][c].x, &xr[c][0], a0);
+          a1 = dot4_i8(wv[r][c].y, &xr[c][4], a1);
+          a0 = dot4_i8(wv[r][c].z, &xr[c][8], a0);
+          a1 = dot4_i8(wv[r][c].w, &xr[c][12], a1);
+        }
+        acc[r] = a0 + a1;
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+
+      if constexpr (S == 1) {
+        if (lane == 0) {
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+            if (n0 + r < n)
+              write_out<LOGITS>(y, static_cast<int64_t>(t) * ldy + n0 + r, acc[r], s[n0 + r], cap);
+        }
+      } else {
+        if (lane == 0) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) red[team][sl][r] = acc[r];
+        }
+        // Team barrier: the S warps of this team only.
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");
+        if (sl == 0 && lane == 0) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            float v = red[team][0][r];
+#pragma unroll
+            for (int q = 1; q < S; ++q) v += red[team][q][r];
+            if (n0 + r < n)
+              write_out<LOGITS>(y, static_cast<int64_t>(t) * ldy + n0 + r, v, s[n0 + r], cap);
+          }
+        }
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");
+      }
+    }
+  }
+}
+
+}  // namespace w8
+
+namespace w8host {
+
+int require_sm100(int* device);
+
+template <int J, int S, int R, bool LOGITS>
+static int launch_gemv(const __nv_bfloat16* x, int64_t ldx, const int8_t* w, int64_t ldw,
+                       const __nv_bfloat16* s, void* y, int64_t ldy, int t, int n, int k, float cap,
+                       cudaStream_t stream) {
+  auto kern = w8::int8_gemv_kernel<J, S, R, LOGITS>;
+  int sms = 0;
+  int st = num_sms(&sms);
+  if (st != W8_OK) return st;
+  int per_sm = 0;
+  W8_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, w8::kGemvThreads, 0));
+  if (per_sm < 1) per_sm = 1;
+  constexpr int rows_per_cta = (w8::kGemvWarps / S) * R;
+  const int64_t need = (static_cast<int64_t>(n) + rows_per_cta - 1) / rows_per_cta;
+  const int64_t cap_blocks = static_cast<int64_t>(sms) * per_sm;
+  const int grid = static_cast<int>(need < cap_blocks ? need : cap_blocks);
+  kern<<<grid, w8::kGemvThreads, 0, stream>>>(x, ldx, w, ldw, s, y, ldy, t, n, k, cap);
+  return cuda_status(cudaGetLastError());
+}
+
+template <bool LOGITS>
+static int gemv_dispatch(const uint16_t* xh, int64_t ldx, const int8_t* w, int64_t ldw,
+                         const uint16_t* sh, void* y, int64_t ldy, int64_t t, int64_t n, int64_t k,
+                         float cap, cudaStream_t stream) {
+  W8_CHECK_ARG(t >= 0 && n >= 0 && k >= 0, "negative size");
+  W8_CHECK_ARG(t < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31), "size beyond int32 range");
+  if (t == 0 || n == 0) return W8_OK;
+  W8_CHECK_ARG(xh != nullptr && w != nullptr && sh != nullptr && y != nullptr, "null pointer");
+  W8_CHECK_ARG(k % 16 == 0, "k = %lld must be a multiple of 16", (long long)k);
+  W8_CHECK_ARG(k <= 16384, "k = %lld exceeds the GEMV limit of 16384", (long long)k);
+  W8_CHECK_ARG(ldw >= k && ldx >= k && ldy >= n, "row pitch too small");
+  W8_CHECK_ALIGN(aligned(w, 16) && ldw % 16 == 0, "w must be 16-byte aligned with ldw %% 16 == 0");
+  W8_CHECK_ALIGN(aligned(xh, 16) && ldx % 8 == 0, "x must be 16-byte aligned with ldx %% 8 == 0");
+  int device = 0;
+  const int st = require_sm100(&device);
+  if (st != W8_OK) return st;
+  if (k == 0) {
+    W8_CUDA_TRY(cudaMemset2DAsync(y, ldy * (LOGITS ? 4 : 2), 0, n * (LOGITS ? 4 : 2), t, stream));
+    return W8_OK;
+  }
+  const auto* x = reinterpret_cast<const __nv_bfloat16*>(xh);
+  const auto* s = reinterpret_cast<const __nv_bfloat16*>(sh);
+  const int ti = static_cast<int>(t), ni = static_cast<int>(n), ki = static_cast<int>(k);
+  // Smallest (S, J) whose slice covers K: x stays within 64 fp32 registers per lane.
+  if (k <= 512) return launch_gemv<1, 1, 4, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
+  if (k <= 1024) return launch_gemv<2, 1, 4, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
+  if (k <= 1536) return launch_gemv<3, 1, 4, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
+  if (k <= 2048) return launch_gemv<4, 1, 2, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
+  if (k <= 3072) return launch_gemv<3, 2, 4, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
+  if (k <= 4096) return launch_gemv<4, 2, 2, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
+  if (k <= 6144) return launch_gemv<3, 4, 4, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
+  if (k <= 8192) return launch_gemv<4, 4, 2, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
+  if (k <= 12288) return launch_gemv<3, 8, 4, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
+  return launch_gemv<4, 8, 2, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
+}
+
+}  // namespace w8host
+
+extern "C" int w8_int8_linear_bf16(const uint16_t* x, int64_t ldx, const int8_t* w, int64_t ldw,
+                                   const uint16_t* s, uint16_t* y, int64_t ldy, int64_t t,
+                                   int64_t n, int64_t k, w8_stream_t stream) {
+  return w8host::gemv_dispatch<false>(x, ldx, w, ldw, s, y, ldy, t, n, k, 0.f,
+                                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int w8_lm_head_f32(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap,
+                              float* logits, int64_t n, int64_t k, w8_stream_t stream) {
+  return w8host::gemv_dispatch<true>(x, k, w, k, s, logits, n, 1, n, k, cap,
+                                     reinterpret_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,237 @@
+// Per-row symmetric int8 quantisation and int32 -> bf16 dequantisation.
+//
+// quant: reference _quant (pipeline.py:49-52) / _quant_rows (gemma_npu.py:37-42) and the
+// per-output-channel weight quant of NPUGemm (gemma_npu.py:68-69) and Int8Head
+// (gemma_npu.py:165-166):
+//     s = max(absmax(row), 1e-8) / 127          (fp32, IEEE divide)
+//     q = clamp(round_half_even(x / s), -127, 127)
+// Both divisions are correctly rounded (__fdiv_rn) and the rounding is rintf, so the
+// output is bit-identical to torch's CPU result on the same fp32/bf16 input.
+//
+// dequant: reference _deq (pipeline.py:55-57) / _dequant (gemma_npu.py:45-47):
+//     y = bf16((float(acc) * sx[row]) * sw[col])
+//
+// Both are HBM-bound streaming kernels: one CTA per row for quant (the row stays in
+// registers between the absmax pass and the quantise pass), a grid-stride 16-byte
+// vectorised loop for dequant.
+#include "common.cuh"
+
+namespace w8 {
+
+constexpr int kQuantThreads = 128;
+constexpr int kQuantMaxVecs = 8;  // vectors per thread kept in registers
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+
+__device__ __forceinline__ int8_t quant_one(float v, float s) {
+  float q = rintf(__fdiv_rn(v, s));
+  q = fminf(fmaxf(q, -127.f), 127.f);
+  return static_cast<int8_t>(static_cast<int>(q));
+}
+
+// VEC elements of T per 16-byte vector (VEC == 1: unaligned scalar path).
+template <typename T, int VEC>
+struct alignas(VEC * sizeof(T) >= 16 ? 16 : alignof(T)) Vec {
+  T v[VEC];
+};
+
+template <typename T, int VEC>
+__device__ __forceinline__ Vec<T, VEC> load_vec(const T* p) {
+  Vec<T, VEC> r;
+  if constexpr (VEC * sizeof(T) == 16) {
+    *reinterpret_cast<uint4*>(r.v) = __ldg(reinterpret_cast<const uint4*>(p));
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) r.v[i] = p[i];
+  }
+  return r;
+}
+
+__device__ __forceinline__ uint32_t pack4(const int8_t* q) {
+  return static_cast<uint32_t>(static_cast<uint8_t>(q[0])) |
+         (static_cast<uint32_t>(static_cast<uint8_t>(q[1])) << 8) |
+         (static_cast<uint32_t>(static_cast<uint8_t>(q[2])) << 16) |
+         (static_cast<uint32_t>(static_cast<uint8_t>(q[3])) << 24);
+}
+
+template <int VEC>
+__device__ __forceinline__ void store_q(int8_t* p, const int8_t (&q)[VEC]) {
+  if constexpr (VEC == 8) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack4(q), pack4(q + 4));
+  } else if constexpr (VEC == 4) {
+    *reinterpret_cast<uint32_t*>(p) = pack4(q);
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) p[i] = q[i];
+  }
+}
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(kQuantThreads)
+    quant_rows_kernel(const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q, int64_t ldq,
+                      float* __restrict__ s, int m, int k) {
+  __shared__ float red[kQuantThreads / 32];
+  const int row = blockIdx.x;
+  if (row >= m) return;
+  const T* xr = x + static_cast<int64_t>(row) * ldx;
+  int8_t* qr = q + static_cast<int64_t>(row) * ldq;
+  const int nvec = k / VEC;
+
+  Vec<T, VEC> held[kQuantMaxVecs];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < kQuantMaxVecs; ++i) {
+    const int vi = threadIdx.x + i * kQuantThreads;
+    if (vi < nvec) {
+      held[i] = load_vec<T, VEC>(xr + static_cast<int64_t>(vi) * VEC);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) amax = fmaxf(amax, fabsf(to_f32(held[i].v[e])));
+    }
+  }
+  // Rows longer than the register window: stream the rest (read again in pass 2).
+  for (int vi = threadIdx.x + kQuantMaxVecs * kQuantThreads; vi < nvec; vi += kQuantThreads) {
+    const Vec<T, VEC> v = load_vec<T, VEC>(xr + static_cast<int64_t>(vi) * VEC);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) amax = fmaxf(amax, fabsf(to_f32(v.v[e])));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, red[w]);
+  const float sc = __fdiv_rn(fmaxf(amax, 1e-8f), 127.f);
+  if (threadIdx.x == 0) s[row] = sc;
+
+#pragma unroll
+  for (int i = 0; i < kQuantMaxVecs; ++i) {
+    const int vi = threadIdx.x + i * kQuantThreads;
+    if (vi < nvec) {
+      int8_t out[VEC];
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) out[e] = quant_one(to_f32(held[i].v[e]), sc);
+      store_q<VEC>(qr + static_cast<int64_t>(vi) * VEC, out);
+    }
+  }
+  for (int vi = threadIdx.x + kQuantMaxVecs * kQuantThreads; vi < nvec; vi += kQuantThreads) {
+    const Vec<T, VEC> v = load_vec<T, VEC>(xr + static_cast<int64_t>(vi) * VEC);
+    int8_t out[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) out[e] = quant_one(to_f32(v.v[e]), sc);
+    store_q<VEC>(qr + static_cast<int64_t>(vi) * VEC, out);
+  }
+}
+
+// y = bf16((float(acc) * sx[row]) * sw[col]); 4 columns per thread step when aligned.
+template <int VEC>
+__global__ void __launch_bounds__(256)
+    dequant_kernel(const int32_t* __restrict__ acc, int64_t ldacc, const float* __restrict__ sx,
+                   const float* __restrict__ sw, __nv_bfloat16* __restrict__ y, int64_t ldy, int m,
+                   int n) {
+  const int64_t nv = n / VEC;
+  const int64_t total = static_cast<int64_t>(m) * nv;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(i / nv);
+    const int col = static_cast<int>(i - static_cast<int64_t>(row) * nv) * VEC;
+    const float sr = __ldg(sx + row);
+    const int32_t* a = acc + static_cast<int64_t>(row) * ldacc + col;
+    __nv_bfloat16* o = y + static_cast<int64_t>(row) * ldy + col;
+    if constexpr (VEC == 4) {
+      const int4 v = __ldg(reinterpret_cast<const int4*>(a));
+      const float4 w = __ldg(reinterpret_cast<const float4*>(sw + col));
+      __nv_bfloat162 p0 = __floats2bfloat162_rn(__fmul_rn(__fmul_rn(__int2float_rn(v.x), sr), w.x),
+                                                __fmul_rn(__fmul_rn(__int2float_rn(v.y), sr), w.y));
+      __nv_bfloat162 p1 = __floats2bfloat162_rn(__fmul_rn(__fmul_rn(__int2float_rn(v.z), sr), w.z),
+                                                __fmul_rn(__fmul_rn(__int2float_rn(v.w), sr), w.w));
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&p0);
+      pk.y = *reinterpret_cast<uint32_t*>(&p1);
+      *reinterpret_cast<uint2*>(o) = pk;
+    } else {
+      o[0] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(__int2float_rn(__ldg(a)), sr), __ldg(sw + col)));
+    }
+  }
+}
+
+}  // namespace w8
+
+namespace w8host {
+
+int require_sm100(int* device);
+
+template <typename T>
+static int quant_rows(const T* x, int64_t ldx, int8_t* q, int64_t ldq, float* s, int64_t m,
+                      int64_t k, cudaStream_t stream) {
+  W8_CHECK_ARG(m >= 0 && k >= 0, "negative size");
+  W8_CHECK_ARG(m < (1ll << 31) && k < (1ll << 31), "size beyond int32 range");
+  if (m == 0) return W8_OK;
+  W8_CHECK_ARG(x != nullptr && q != nullptr && s != nullptr, "null pointer");
+  W8_CHECK_ARG(ldx >= k && ldq >= k, "row pitch smaller than k");
+  int device = 0;
+  const int st = require_sm100(&device);
+  if (st != W8_OK) return st;
+  constexpr int VEC = 16 / static_cast<int>(sizeof(T));
+  const bool vec_ok = aligned(x, 16) && (ldx * sizeof(T)) % 16 == 0 && k % VEC == 0 &&
+                      aligned(q, VEC) && ldq % VEC == 0;
+  const dim3 grid(static_cast<unsigned>(m));
+  if (vec_ok)
+    w8::quant_rows_kernel<T, VEC><<<grid, w8::kQuantThreads, 0, stream>>>(
+        x, ldx, q, ldq, s, static_cast<int>(m), static_cast<int>(k));
+  else
+    w8::quant_rows_kernel<T, 1><<<grid, w8::kQuantThreads, 0, stream>>>(
+        x, ldx, q, ldq, s, static_cast<int>(m), static_cast<int>(k));
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace w8host
+
+extern "C" int w8_quant_rows_bf16(const uint16_t* x, int64_t ldx, int8_t* q, int64_t ldq, float* s,
+                                  int64_t m, int64_t k, w8_stream_t stream) {
+  return w8host::quant_rows(reinterpret_cast<const __nv_bfloat16*>(x), ldx, q, ldq, s, m, k,
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int w8_quant_rows_f32(const float* x, int64_t ldx, int8_t* q, int64_t ldq, float* s,
+                                 int64_t m, int64_t k, w8_stream_t stream) {
+  return w8host::quant_rows(x, ldx, q, ldq, s, m, k, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int w8_dequant_bf16(const int32_t* acc, int64_t ldacc, const float* sx, const float* sw,
+                               uint16_t* y, int64_t ldy, int64_t m, int64_t n, w8_stream_t stream) {
+  W8_CHECK_ARG(m >= 0 && n >= 0, "negative size");
+  W8_CHECK_ARG(m < (1ll << 31) && n < (1ll << 31), "size beyond int32 range");
+  if (m == 0 || n == 0) return W8_OK;
+  W8_CHECK_ARG(acc != nullptr && sx != nullptr && sw != nullptr && y != nullptr, "null pointer");
+  W8_CHECK_ARG(ldacc >= n && ldy >= n, "row pitch smaller than n");
+  int device = 0;
+  const int st = w8host::require_sm100(&device);
+  if (st != W8_OK) return st;
+  int sms = 0;
+  const int st2 = w8host::num_sms(&sms);
+  if (st2 != W8_OK) return st2;
+  const bool vec_ok = w8host::aligned(acc, 16) && ldacc % 4 == 0 && w8host::aligned(sw, 16) &&
+                      w8host::aligned(y, 8) && ldy % 4 == 0 && n % 4 == 0;
+  const int64_t work = m * (vec_ok ? n / 4 : n);
+  int64_t blocks = (work + 255) / 256;
+  if (blocks > static_cast<int64_t>(sms) * 16) blocks = static_cast<int64_t>(sms) * 16;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  auto* out = reinterpret_cast<__nv_bfloat16*>(y);
+  if (vec_ok)
+    w8::dequant_kernel<4><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        acc, ldacc, sx, sw, out, ldy, static_cast<int>(m), static_cast<int>(n));
+  else
+    w8::dequant_kernel<1><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        acc, ldacc, sx, sw, out, ldy, static_cast<int>(m), static_cast<int>(n));
+  return w8host::cuda_status(cudaGetLastError());
+}

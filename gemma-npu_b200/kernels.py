@@ -1,0 +1,219 @@
+"""Torch-facing wrappers of the sm_100a W8A8 kernels.
+
+B200 counterpart of the reference's kernel module `npu_kernels.py` plus the
+quant/dequant glue of `pipeline.py` / `gemma_npu.py`:
+
+    mm_i8(a, b, c) -> c          npu_kernels.py:59-64   (int8 [M,K] @ int8 [K,N] -> int32)
+    use_device()                 npu_kernels.py:25-26   (use_npu: per-thread device selection)
+    quant_rows(x) -> (q, s)      pipeline.py:49-52, gemma_npu.py:37-42
+    dequant(acc, sx, sw)         pipeline.py:55-57, gemma_npu.py:45-47
+    int8_linear(x, wq, sw)       gemma_npu.py:155-156   (torch._weight_int8pack_mm)
+
+Every function validates dtype/shape/layout on the host, passes raw device
+pointers and torch's current CUDA stream to the C ABI, and raises a W8Error
+subclass on a non-zero status.  Inputs must already live on a CUDA device:
+nothing here copies to or from the host, and nothing falls back to the CPU.
+Unlike the reference kernel, no shape needs padding to the tile (M, N any;
+K a multiple of 16).
+"""
+import torch
+
+from . import _lib
+from ._lib import W8_B_KN, W8_B_NK
+
+# Tile of the tcgen05 GEMM (rows x columns x K per pipeline stage).  Informational:
+# callers need not pad to it (the reference's BLOCK_M = BLOCK_N = 512, BLOCK_K = 128).
+BLOCK_M = 128
+BLOCK_N = 256
+BLOCK_K = 128
+
+
+def use_device(device=None):
+    """Select the CUDA device for the calling thread (the reference's use_npu()).
+
+    CUDA's current device is per thread, like Triton's active driver in the
+    reference: a worker thread that launches GEMMs calls this first.
+    """
+    if device is None:
+        device = torch.cuda.current_device()
+    torch.cuda.set_device(device)
+
+
+def _stream(t):
+    return ctypes_ptr(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def ctypes_ptr(v):
+    return v if v else None
+
+
+def _need(cond, msg):
+    if not cond:
+        raise ValueError(msg)
+
+
+def _check_matrix(t, name, dtype):
+    _need(isinstance(t, torch.Tensor), f"{name} must be a tensor")
+    _need(t.is_cuda, f"{name} must be on a CUDA device (got {t.device}); there is no CPU path")
+    _need(t.dtype == dtype, f"{name} must be {dtype} (got {t.dtype})")
+    _need(t.dim() == 2, f"{name} must be 2-D (got shape {tuple(t.shape)})")
+    _need(t.stride(1) == 1 or t.shape[1] <= 1, f"{name} must be row-major with unit column stride")
+
+
+def _ld(t):
+    return t.stride(0) if t.shape[0] > 1 else max(t.shape[1], t.stride(0))
+
+
+def _check_vector(t, name, dtype, n):
+    _need(isinstance(t, torch.Tensor) and t.is_cuda, f"{name} must be a CUDA tensor")
+    _need(t.dtype == dtype, f"{name} must be {dtype} (got {t.dtype})")
+    _need(t.dim() == 1 and t.shape[0] == n, f"{name} must have shape ({n},) (got {tuple(t.shape)})")
+    _need(t.is_contiguous(), f"{name} must be contiguous")
+
+
+def mm_i8(a, b, c):
+    """c[M,N] (int32) = a[M,K] (int8) @ b[K,N] (int8), exact; writes into c and returns it.
+
+    Same contract as the reference's mm_i8 (npu_kernels.py:59-64) without its
+    multiple-of-512 precondition.  b is the reference layout [K,N]; see
+    mm_i8_nk for the resident [N,K] layout.
+    """
+    _check_matrix(a, "a", torch.int8)
+    _check_matrix(b, "b", torch.int8)
+    _check_matrix(c, "c", torch.int32)
+    M, K = a.shape
+    _need(b.shape[0] == K, f"inner sizes differ: a {tuple(a.shape)}, b {tuple(b.shape)}")
+    N = b.shape[1]
+    _need(tuple(c.shape) == (M, N), f"c must be ({M}, {N}) (got {tuple(c.shape)})")
+    _need(a.device == b.device == c.device, "a, b, c must be on one device")
+    _lib.call("w8_mm_i8", a.data_ptr(), _ld(a), b.data_ptr(), _ld(b), W8_B_KN, c.data_ptr(), _ld(c),
+              M, N, K, _stream(a))
+    return c
+
+
+def mm_i8_nk(a, w, c):
+    """c[M,N] (int32) = a[M,K] @ w[N,K]^T: the GEMM over a resident K-major weight."""
+    _check_matrix(a, "a", torch.int8)
+    _check_matrix(w, "w", torch.int8)
+    _check_matrix(c, "c", torch.int32)
+    M, K = a.shape
+    N = w.shape[0]
+    _need(w.shape[1] == K, f"inner sizes differ: a {tuple(a.shape)}, w {tuple(w.shape)}")
+    _need(tuple(c.shape) == (M, N), f"c must be ({M}, {N}) (got {tuple(c.shape)})")
+    _need(a.device == w.device == c.device, "a, w, c must be on one device")
+    _lib.call("w8_mm_i8", a.data_ptr(), _ld(a), w.data_ptr(), _ld(w), W8_B_NK, c.data_ptr(), _ld(c),
+              M, N, K, _stream(a))
+    return c
+
+
+def gemm_dequant(a, w, sx, sw, out=None):
+    """bf16 [M,N] = dequant(a @ w^T) with the dequant fused into the GEMM epilogue.
+
+    a int8 [M,K] with per-row scales sx fp32 [M]; w int8 [N,K] with per-channel
+    scales sw fp32 [N].  Bit-identical to dequant(mm_i8_nk(a, w, c), sx, sw).
+    """
+    _check_matrix(a, "a", torch.int8)
+    _check_matrix(w, "w", torch.int8)
+    M, K = a.shape
+    N = w.shape[0]
+    _need(w.shape[1] == K, f"inner sizes differ: a {tuple(a.shape)}, w {tuple(w.shape)}")
+    _check_vector(sx, "sx", torch.float32, M)
+    _check_vector(sw, "sw", torch.float32, N)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    _check_matrix(out, "out", torch.bfloat16)
+    _need(tuple(out.shape) == (M, N), f"out must be ({M}, {N})")
+    _lib.call("w8_gemm_dequant_bf16", a.data_ptr(), _ld(a), w.data_ptr(), _ld(w), W8_B_NK,
+              sx.data_ptr(), sw.data_ptr(), out.data_ptr(), _ld(out), M, N, K, _stream(a))
+    return out
+
+
+def quant_rows(x, q=None, s=None):
+    """Per-row symmetric int8 quant of a bf16 or fp32 [T,K] tensor -> (q int8 [T,K], s fp32 [T]).
+
+    The reference's _quant (pipeline.py:49-52) / _quant_rows (gemma_npu.py:37-42):
+    s = max(absmax, 1e-8) / 127, q = clamp(round(x / s), -127, 127), bit-identical.
+    """
+    _need(isinstance(x, torch.Tensor) and x.is_cuda, "x must be a CUDA tensor; there is no CPU path")
+    _need(x.dim() == 2 and (x.stride(1) == 1 or x.shape[1] <= 1), "x must be 2-D row-major")
+    T, K = x.shape
+    if q is None:
+        q = torch.empty((T, K), dtype=torch.int8, device=x.device)
+    if s is None:
+        s = torch.empty((T,), dtype=torch.float32, device=x.device)
+    _check_matrix(q, "q", torch.int8)
+    _need(tuple(q.shape) == (T, K), f"q must be ({T}, {K})")
+    _check_vector(s, "s", torch.float32, T)
+    if x.dtype == torch.bfloat16:
+        fn = "w8_quant_rows_bf16"
+    elif x.dtype == torch.float32:
+        fn = "w8_quant_rows_f32"
+    else:
+        raise ValueError(f"x must be bfloat16 or float32 (got {x.dtype})")
+    _lib.call(fn, x.data_ptr(), _ld(x), q.data_ptr(), _ld(q), s.data_ptr(), T, K, _stream(x))
+    return q, s
+
+
+def dequant(acc, sx, sw, dtype=torch.bfloat16, out=None):
+    """bf16 [T,N] = (float(acc) * sx[:,None]) * sw[None,:] (the reference's _deq, pipeline.py:55-57)."""
+    _need(dtype == torch.bfloat16, "only bfloat16 output is implemented (the reference's dtype)")
+    _check_matrix(acc, "acc", torch.int32)
+    T, N = acc.shape
+    _check_vector(sx, "sx", torch.float32, T)
+    _check_vector(sw, "sw", torch.float32, N)
+    if out is None:
+        out = torch.empty((T, N), dtype=torch.bfloat16, device=acc.device)
+    _check_matrix(out, "out", torch.bfloat16)
+    _lib.call("w8_dequant_bf16", acc.data_ptr(), _ld(acc), sx.data_ptr(), sw.data_ptr(), out.data_ptr(),
+              _ld(out), T, N, _stream(acc))
+    return out
+
+
+def int8_linear(x2d, wq, sw, out=None):
+    """bf16 [T,N] = (x2d @ wq^T) * sw: the weight-only int8 GEMV of decode.
+
+    The reference's cpu_int8_linear (gemma_npu.py:155-156), i.e.
+    torch._weight_int8pack_mm(x_bf16, wq [N,K] int8, sw [N] bf16), with fp32
+    accumulation on the GPU.
+    """
+    _need(isinstance(x2d, torch.Tensor) and x2d.is_cuda, "x2d must be a CUDA tensor; there is no CPU path")
+    if x2d.dtype != torch.bfloat16:
+        x2d = x2d.to(torch.bfloat16)
+    if x2d.stride(-1) != 1 or x2d.data_ptr() % 16 or (x2d.shape[0] > 1 and x2d.stride(0) % 8):
+        x2d = x2d.contiguous()
+    _check_matrix(x2d, "x2d", torch.bfloat16)
+    _check_matrix(wq, "wq", torch.int8)
+    T, K = x2d.shape
+    N = wq.shape[0]
+    _need(wq.shape[1] == K, f"inner sizes differ: x {tuple(x2d.shape)}, wq {tuple(wq.shape)}")
+    _check_vector(sw, "sw", torch.bfloat16, N)
+    if out is None:
+        out = torch.empty((T, N), dtype=torch.bfloat16, device=x2d.device)
+    _check_matrix(out, "out", torch.bfloat16)
+    _lib.call("w8_int8_linear_bf16", x2d.data_ptr(), _ld(x2d), wq.data_ptr(), _ld(wq), sw.data_ptr(),
+              out.data_ptr(), _ld(out), T, N, K, _stream(x2d))
+    return out
+
+
+def lm_head_logits(x, wq, sw, cap=0.0, out=None):
+    """fp32 [N] logits of one token: cap * tanh(bf16(x @ wq^T * sw) / cap) (cap <= 0: no softcap).
+
+    Int8Head.forward (gemma_npu.py:170-172) followed by the final logit softcap
+    (pipeline.py:335-338), fused into the GEMV.
+    """
+    _need(isinstance(x, torch.Tensor) and x.is_cuda, "x must be a CUDA tensor")
+    x = x.reshape(-1)
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    x = x.contiguous()
+    _check_matrix(wq, "wq", torch.int8)
+    N, K = wq.shape
+    _need(x.shape[0] == K, f"x must have {K} elements (got {x.shape[0]})")
+    _need(wq.is_contiguous(), "wq must be contiguous [N, K]")
+    _check_vector(sw, "sw", torch.bfloat16, N)
+    if out is None:
+        out = torch.empty((N,), dtype=torch.float32, device=x.device)
+    _check_vector(out, "out", torch.float32, N)
+    _lib.call("w8_lm_head_f32", x.data_ptr(), wq.data_ptr(), sw.data_ptr(), float(cap or 0.0),
+              out.data_ptr(), N, K, _stream(x))
+    return out

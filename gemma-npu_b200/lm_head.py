@@ -1,0 +1,64 @@
+"""Column-sharded LM head across GPUs: local int8 GEMV + NCCL all-gather of the logits.
+
+The reference computes the whole 262144-wide LM head on one CPU
+(Int8Head, gemma_npu.py:159-172; softcap pipeline.py:335-338).  Here rank g of a
+G-rank process group holds rows [g*V/G, (g+1)*V/G) of the [V, K] head weight
+(V/G a whole number of rows, padded up when V % G != 0), computes its slice of
+the softcapped fp32 logits with the fused GEMV, and an all-gather over
+NVLink/NVSwitch assembles the full [V] vector on every rank.  One process per
+GPU; the process group is torch.distributed's (NCCL on GPUs).
+"""
+import torch
+import torch.distributed as dist
+
+from . import kernels
+from .gemm import quantize_weight
+
+
+def shard_rows(vocab, world, rank):
+    """Row range [r0, r1) of the head weight owned by `rank`; shards are ceil(V/G) rows."""
+    per = -(-vocab // world)
+    r0 = min(rank * per, vocab)
+    return r0, min(r0 + per, vocab), per
+
+
+def gather_logits(local, full, vocab, group=None):
+    """All-gather equal-length per-rank logit slices into `full` and return its first `vocab`.
+
+    `local` is this rank's [per] slice (a short last shard zero-padded), `full` a
+    [world * per] buffer on the same device; rank order is shard order.
+    """
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return local[:vocab]
+    dist.all_gather_into_tensor(full, local, group=group)
+    return full[:vocab]
+
+
+class ShardedInt8Head:
+    """The int8 LM head split by output rows over the ranks of a process group."""
+
+    def __init__(self, weight, group=None, device=None, cap=0.0):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.vocab, self.hidden = weight.shape
+        self.r0, self.r1, self.per = shard_rows(self.vocab, self.world, self.rank)
+        self.cap = float(cap or 0.0)
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        self.wq, sw = quantize_weight(weight[self.r0: self.r1], self.device)
+        self.sw = sw.to(torch.bfloat16)
+        # Gather target: world x per slots (the last shard may be short: its tail is zero).
+        self.full = torch.empty(self.world * self.per, dtype=torch.float32, device=self.device)
+        self.local = torch.zeros(self.per, dtype=torch.float32, device=self.device)
+
+    def local_logits(self, h):
+        """This rank's softcapped fp32 logits [r1 - r0] of one hidden row."""
+        n = self.r1 - self.r0
+        if n > 0:
+            kernels.lm_head_logits(h, self.wq, self.sw, self.cap, out=self.local[:n])
+        return self.local
+
+    def __call__(self, h):
+        """Full fp32 logits [V] of one hidden row on every rank."""
+        return gather_logits(self.local_logits(h), self.full, self.vocab, self.group)

@@ -1,0 +1,114 @@
+/*
+ * w8a8_b200.h -- C ABI of the B200 (sm_100a) W8A8 linear hot path.
+ *
+ * Drop-in boundary for the int8 linear layers of the Gemma E2B NPU pipeline
+ * (AyaSakura-comp/gemma-npu).  Every entry point takes plain device pointers,
+ * element strides and sizes, is ordered on the given CUDA stream (NULL = the
+ * legacy default stream), and returns W8_OK (0) or a W8_ERR_* status.  Nothing
+ * here allocates per call, and no torch type crosses the boundary.  On a
+ * non-zero status, w8_last_error() holds a one-line description.
+ *
+ * Device-side waits are bounded: a kernel whose pipeline stalls records
+ * W8_ERR_DEVICE_TIMEOUT, which w8_device_status() reports after a sync.
+ *
+ * Reference interfaces replaced (file:line within the reference project):
+ *   w8_mm_i8                npu_kernels.py:59-64 (mm_i8) + :40-56 (matmul_i8_k)
+ *   w8_gemm_dequant_bf16    gemma_npu.py:127-150 (NPUGemm.matmul launch + _dequant)
+ *   w8_quant_rows_bf16/f32  pipeline.py:49-52 (_quant), gemma_npu.py:37-42 (_quant_rows),
+ *                           gemma_npu.py:68-69 (NPUGemm weight quant), :165-166 (Int8Head)
+ *   w8_dequant_bf16         pipeline.py:55-57 (_deq), gemma_npu.py:45-47 (_dequant)
+ *   w8_int8_linear_bf16     gemma_npu.py:155-156 (cpu_int8_linear = torch._weight_int8pack_mm)
+ *   w8_lm_head_f32          gemma_npu.py:170-172 (Int8Head.forward) + pipeline.py:335-338 (softcap)
+ */
+#ifndef W8A8_B200_H
+#define W8A8_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t. */
+typedef struct CUstream_st* w8_stream_t;
+
+/* Status codes. */
+#define W8_OK 0
+#define W8_ERR_INVALID_ARG 1    /* bad size, stride, pointer or layout code            */
+#define W8_ERR_ALIGNMENT 2      /* pointer or row pitch misses the TMA/vector alignment */
+#define W8_ERR_UNSUPPORTED 3    /* no sm_100 device, or a shape outside the kernels' limits */
+#define W8_ERR_CUDA 4           /* a CUDA runtime/driver call failed                     */
+#define W8_ERR_DEVICE_TIMEOUT 5 /* a bounded device-side wait gave up (reported by w8_device_status) */
+
+/* Layout of the B (weight) operand of the GEMMs. */
+#define W8_B_KN 0 /* B is [K, N] row-major: the reference's mm_i8 layout (npu_kernels.py:59-60) */
+#define W8_B_NK 1 /* B is [N, K] row-major (K-major): the resident weight layout, shared with the GEMV */
+
+/* ---- diagnostics ------------------------------------------------------- */
+const char* w8_status_string(int status);
+/* Text of the last host-side error on this thread ("" if none). */
+const char* w8_last_error(void);
+/* Sticky device-side status (W8_OK or W8_ERR_DEVICE_TIMEOUT) of the current device;
+ * synchronises the device first.  clear != 0 resets it to W8_OK. */
+int w8_device_status(int clear);
+/* ABI version: (major << 16) | minor. */
+int w8_abi_version(void);
+
+/* ---- prefill GEMMs (tcgen05 kind::i8, int32 accumulators in TMEM) ----- */
+
+/* C[M,N] (int32) = A[M,K] (int8) @ B (int8), exact int32 accumulation.
+ * Replaces mm_i8 (npu_kernels.py:59-64) / matmul_i8_k (npu_kernels.py:40-56).
+ * Unlike the reference, M and N need no padding to 512 and K none to 128:
+ * K % 16 == 0; lda, ldb multiples of 16 (bytes == elements); ldc % 4 == 0;
+ * a, b, c 16-byte aligned.  b_layout is W8_B_KN ([K,N], ldb >= N) or
+ * W8_B_NK ([N,K], ldb >= K). */
+int w8_mm_i8(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
+             int32_t* c, int64_t ldc, int64_t m, int64_t n, int64_t k, w8_stream_t stream);
+
+/* Y[M,N] (bf16) = bf16((float(A@B) * sx[m]) * sw[n]) with the dequant fused
+ * into the GEMM epilogue.  Bit-identical to mm_i8 followed by _deq.
+ * Replaces NPUGemm.matmul's launches + _dequant (gemma_npu.py:127-150).
+ * Same constraints as w8_mm_i8; ldy % 8 == 0. */
+int w8_gemm_dequant_bf16(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
+                         const float* sx, const float* sw, uint16_t* y, int64_t ldy,
+                         int64_t m, int64_t n, int64_t k, w8_stream_t stream);
+
+/* ---- quantisation ------------------------------------------------------ */
+
+/* Per-row symmetric int8: s[r] = max(absmax(x[r,:]), 1e-8) / 127 (fp32, IEEE divide),
+ * q[r,k] = clamp(round_half_even(x[r,k] / s[r]), -127, 127).
+ * Replaces _quant (pipeline.py:49-52) and _quant_rows (gemma_npu.py:37-42); on a
+ * weight [N,K] it is the per-output-channel quant of NPUGemm (gemma_npu.py:68-69). */
+int w8_quant_rows_bf16(const uint16_t* x, int64_t ldx, int8_t* q, int64_t ldq, float* s,
+                       int64_t m, int64_t k, w8_stream_t stream);
+int w8_quant_rows_f32(const float* x, int64_t ldx, int8_t* q, int64_t ldq, float* s,
+                      int64_t m, int64_t k, w8_stream_t stream);
+
+/* Y[M,N] (bf16) = bf16((float(acc) * sx[m]) * sw[n]).
+ * Replaces _deq (pipeline.py:55-57) / _dequant (gemma_npu.py:45-47). */
+int w8_dequant_bf16(const int32_t* acc, int64_t ldacc, const float* sx, const float* sw,
+                    uint16_t* y, int64_t ldy, int64_t m, int64_t n, w8_stream_t stream);
+
+/* ---- decode: weight-only int8 GEMV / LM head -------------------------- */
+
+/* y[t,n] (bf16) = bf16(float(s[n]) * sum_k float(x[t,k]) * w[n,k]), fp32 accumulation.
+ * x bf16 [T,K], w int8 [N,K] row-major, s bf16 [N].  K % 16 == 0, ldw % 16 == 0,
+ * ldx % 8 == 0, 16-byte aligned x and w.
+ * Replaces cpu_int8_linear (gemma_npu.py:155-156), i.e. torch._weight_int8pack_mm. */
+int w8_int8_linear_bf16(const uint16_t* x, int64_t ldx, const int8_t* w, int64_t ldw,
+                        const uint16_t* s, uint16_t* y, int64_t ldy, int64_t t, int64_t n,
+                        int64_t k, w8_stream_t stream);
+
+/* LM head for one token: logits[n] (fp32) = cap * tanh(float(bf16(y[n])) / cap) with
+ * y as w8_int8_linear_bf16 computes it for t = 1 (cap <= 0: logits = float(y)).
+ * w is [N,K] with row pitch K; for a column-sharded head pass the shard's rows.
+ * Replaces Int8Head.forward (gemma_npu.py:170-172) + final_logit_softcapping
+ * (pipeline.py:335-338). */
+int w8_lm_head_f32(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap,
+                   float* logits, int64_t n, int64_t k, w8_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* W8A8_B200_H */

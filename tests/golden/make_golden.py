@@ -1,0 +1,112 @@
+"""Generate the golden vectors of the W8A8 path by running the REFERENCE's own code.
+
+Imports `pipeline.py` and `gemma_npu.py` from a checkout of AyaSakura-comp/gemma-npu
+(default: the REFERENCE environment variable, else ../reference next to the
+repository) and records, on seeded inputs:
+
+  quant     pipeline._quant (pipeline.py:49-52)            bf16 rows -> int8 + fp32 scale
+  quant_c   gemma_npu._quant_rows (gemma_npu.py:37-42)     the torch.compile'd twin
+  wquant    gemma_npu.Int8Head.__init__ (gemma_npu.py:164-167) = NPUGemm's weight quant (:68-69)
+  int_mm    torch._int_mm as the cpu-int8 GEMM calls it (pipeline.py:237) and the exactness
+            check of shape_bench.py:25-31 (randint(-128, 128) operands)
+  deq       pipeline._deq (pipeline.py:55-57) and gemma_npu._dequant (gemma_npu.py:45-47)
+  gemv      gemma_npu.cpu_int8_linear (gemma_npu.py:155-156), T = 1 and T = 3
+  head      gemma_npu.Int8Head.forward + the softcap of pipeline.py:335-338
+
+The weight of the GEMM, GEMV and head cases is the one stored in wquant.npz
+(q [N,K] int8, s bf16 [N]); the GEMM's B operand is its transpose.  The outputs
+are small .npz files beside this script; the tests read only those,
+so neither the reference nor this script is needed where the tests run.
+
+usage: python tests/golden/make_golden.py [REFERENCE_DIR]
+"""
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def bf16_bits(t):
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def main(ref_dir):
+    sys.path.insert(0, ref_dir)
+    import gemma_npu  # noqa: E402  (reference)
+    import pipeline  # noqa: E402  (reference)
+
+    torch.manual_seed(0)
+    out = {}
+
+    # ---- activation quant: N(0,1) rows as the pipeline's bf16 activations, plus edge rows
+    x = torch.randn(48, 1536).to(torch.bfloat16)
+    x[0] = 0                                            # all-zero row: scale floor 1e-8 / 127
+    x[1] = torch.linspace(-3, 3, 1536).to(torch.bfloat16)
+    x[2, :] = 1e-12                                     # tiny row below the scale floor
+    x[3] = (torch.arange(1536) % 255 - 127).to(torch.bfloat16)  # exact-integer row (absmax 127)
+    x[4] = torch.randn(1536).to(torch.bfloat16) * 3e4   # large magnitudes
+    x[5, ::2] = 0.5
+    x[5, 1::2] = -254.0                                  # ties at x/s = +-0.25 / -127
+    q, s = pipeline._quant(x)
+    out["quant"] = dict(x=bf16_bits(x), q=q.numpy(), s=s.numpy())
+    try:
+        qc, sc = gemma_npu._quant_rows(x)
+        out["quant_c"] = dict(x=bf16_bits(x), q=qc.numpy(), s=sc.numpy())
+    except Exception as e:  # torch.compile needs a working C++ toolchain
+        print("skipping gemma_npu._quant_rows:", type(e).__name__, e)
+
+    # ---- weight quant through the reference's Int8Head on an nn.Linear (N(0, 0.02), bf16)
+    lin = torch.nn.Linear(1536, 384, bias=False)
+    with torch.no_grad():
+        lin.weight.normal_(0, 0.02)
+        lin.weight[7] = 0
+    lin = lin.to(torch.bfloat16)
+    head = gemma_npu.Int8Head(lin)
+    out["wquant"] = dict(w=bf16_bits(lin.weight.detach()), q=head.wq.numpy(), s=bf16_bits(head.sw))
+    w32 = lin.weight.detach().float()
+    sw32 = w32.abs().amax(dim=1).clamp(min=1e-8) / 127   # gemma_npu.py:68 (fp32 scales of NPUGemm)
+    out["wquant"]["s_f32"] = sw32.numpy()
+
+    # ---- int32 GEMM: quantised activations x quantised weights, and full-range random int8
+    xq, sx = pipeline._quant(torch.randn(40, 1536).to(torch.bfloat16))
+    wq = head.wq                                          # [N, K]
+    w_kn = wq.t().contiguous()                            # the w_kn layout of gemma_npu.py:76
+    acc = torch._int_mm(xq, w_kn)
+    out["int_mm"] = dict(a=xq.numpy(), c=acc.numpy())  # b = wquant.q transposed
+    a = torch.randint(-128, 128, (72, 256), dtype=torch.int8)
+    b = torch.randint(-128, 128, (256, 160), dtype=torch.int8)
+    out["int_mm_full"] = dict(a=a.numpy(), b=b.numpy(), c=torch._int_mm(a, b).numpy())
+    assert torch.equal(torch._int_mm(a, b), a.int() @ b.int())
+
+    # ---- dequant
+    y = pipeline._deq(acc, sx, sw32)
+    out["deq"] = dict(acc=acc.numpy(), sx=sx.numpy(), sw=sw32.numpy(), y=bf16_bits(y))
+    try:
+        yc = gemma_npu._dequant(acc, sx, sw32, torch.bfloat16)
+        out["deq_c"] = dict(acc=acc.numpy(), sx=sx.numpy(), sw=sw32.numpy(), y=bf16_bits(yc))
+    except Exception as e:
+        print("skipping gemma_npu._dequant:", type(e).__name__, e)
+
+    # ---- decode GEMV and LM head (+ softcap 30.0, Gemma's final_logit_softcapping)
+    for t in (1, 3):
+        xv = torch.randn(t, 1536).to(torch.bfloat16)
+        yv = gemma_npu.cpu_int8_linear(xv, head.wq, head.sw)
+        out[f"gemv_t{t}"] = dict(x=bf16_bits(xv), y=bf16_bits(yv))  # w, s = wquant.q, wquant.s
+    h = torch.randn(1, 1, 1536).to(torch.bfloat16)
+    logits = head(h)[0, -1].float()
+    cap = 30.0
+    logits = torch.tanh(logits / cap) * cap
+    out["head"] = dict(h=bf16_bits(h.reshape(-1)), cap=np.float32(cap), logits=logits.numpy())
+
+    for name, arrays in out.items():
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)
+        print("wrote", name, {k: getattr(v, "shape", ()) for k, v in arrays.items()})
+
+
+if __name__ == "__main__":
+    default = os.environ.get("REFERENCE", os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))),
+                                                       "reference"))
+    main(sys.argv[1] if len(sys.argv) > 1 else default)
