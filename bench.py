@@ -161,18 +161,19 @@ def timed(replay, steps, warmup, stream, world):
     """Warm up, then time exactly `steps` replays with CUDA events; max over ranks (ms)."""
     import torch.distributed as dist
 
-    for _ in range(warmup):
-        replay()
-    stream.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(steps):
-        replay()
-    end.record(stream)
-    end.synchronize()
+    with torch.cuda.stream(stream):  # replays and events on the same stream
+        for _ in range(warmup):
+            replay()
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            replay()
+        end.record(stream)
+        end.synchronize()
     ms = start.elapsed_time(end)
     torch.cuda.synchronize()
     if world > 1:
@@ -274,20 +275,24 @@ def cpu_reference_rate(m, target_s=10.0, max_layers=35):
     from oracle import cpu_int8
 
     cores = cpu_int8.set_threads()
-    run1, ops1 = cpu_reference_step(m, 1)
+    run1, _ = cpu_reference_step(m, 1)
     run1()
     t = time.perf_counter()
     run1()
     per_layer = time.perf_counter() - t
-    reps = max(1, min(int(target_s / max(per_layer, 1e-6)), max_layers))
-    layers = min(reps, max_layers)
+    layers = max(1, min(int(target_s / 4 / max(per_layer, 1e-6)), max_layers))
     run, ops = cpu_reference_step(m, layers, seed=1)
     run()  # warm-up
-    t = time.perf_counter()
-    run()
-    dt = time.perf_counter() - t
+    times = []
+    t_end = time.perf_counter() + target_s
+    while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 50):
+        t = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t)
+    dt = statistics.median(times)
     return {"value": ops / dt / 1e12, "unit": "TOPS", "cores": cores, "kind": "port",
-            "sample": f"{layers} of {LAYERS} layers x 4 GEMMs (torch._int_mm, M={m}), one timed pass of {dt:.2f} s"}
+            "sample": f"{layers} of {LAYERS} layers x 4 GEMMs (torch._int_mm, M={m}); median of {len(times)} "
+                      f"passes, {sum(times):.1f} s of CPU time"}
 
 
 def run_reference_arm(args, world, rank):

@@ -47,6 +47,8 @@ struct GemmArgs {
   int64_t ldo;
   const float* sx;
   const float* sw;
+  int vec_out;  // output base 16-byte aligned and row pitch a multiple of 16 bytes
+  int vec_sw;   // sw 16-byte aligned
 };
 
 constexpr uint32_t tmem_cols_for(int c) {
@@ -72,7 +74,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0
   if (row >= a.m) return;
   if constexpr (EPI == kEpiI32) {
     int32_t* dst = static_cast<int32_t*>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
-    if (col0 + 32 <= a.n) {
+    if (a.vec_out && col0 + 32 <= a.n) {
       int4* d4 = reinterpret_cast<int4*>(dst);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
@@ -88,7 +90,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0
     // the operation order of _deq (pipeline.py:57).
     __nv_bfloat16* dst =
         static_cast<__nv_bfloat16*>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
-    if (col0 + 32 <= a.n) {
+    if (a.vec_out && a.vec_sw && col0 + 32 <= a.n) {
       const float4* sw4 = reinterpret_cast<const float4*>(a.sw + col0);
       uint32_t packed[16];
 #pragma unroll
@@ -374,12 +376,8 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   if (m == 0 || n == 0) return W8_OK;
   W8_CHECK_ARG(out != nullptr, "null output pointer");
   W8_CHECK_ARG(ldo >= n, "output row pitch %lld < n %lld", (long long)ldo, (long long)n);
-  W8_CHECK_ALIGN(aligned(out, 16) && (ldo * out_elem) % 16 == 0,
-                 "output must be 16-byte aligned with a row pitch that is a multiple of 16 bytes");
-  if (epi == w8::kEpiBf16) {
-    W8_CHECK_ARG(sx != nullptr && sw != nullptr, "null scale pointer");
-    W8_CHECK_ALIGN(aligned(sw, 16), "sw must be 16-byte aligned");
-  }
+  W8_CHECK_ALIGN(aligned(out, out_elem), "output must be aligned to its element size");
+  if (epi == w8::kEpiBf16) W8_CHECK_ARG(sx != nullptr && sw != nullptr, "null scale pointer");
   int device = 0;
   int st = require_sm100(&device);
   if (st != W8_OK) return st;
@@ -420,6 +418,8 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   args.ldo = ldo;
   args.sx = sx;
   args.sw = sw;
+  args.vec_out = aligned(out, 16) && (ldo * out_elem) % 16 == 0;
+  args.vec_sw = sw != nullptr && aligned(sw, 16);
 
   const bool mn = b_layout == W8_B_KN;
   if (epi == w8::kEpiI32)

@@ -59,16 +59,18 @@ int w8_abi_version(void);
 /* C[M,N] (int32) = A[M,K] (int8) @ B (int8), exact int32 accumulation.
  * Replaces mm_i8 (npu_kernels.py:59-64) / matmul_i8_k (npu_kernels.py:40-56).
  * Unlike the reference, M and N need no padding to 512 and K none to 128:
- * K % 16 == 0; lda, ldb multiples of 16 (bytes == elements); ldc % 4 == 0;
- * a, b, c 16-byte aligned.  b_layout is W8_B_KN ([K,N], ldb >= N) or
- * W8_B_NK ([N,K], ldb >= K). */
+ * K % 16 == 0; lda, ldb multiples of 16 (bytes == elements); a, b 16-byte
+ * aligned (TMA).  C may have any row pitch ldc >= N (16-byte vector stores
+ * when c is 16-byte aligned and ldc % 4 == 0, element stores otherwise).
+ * b_layout is W8_B_KN ([K,N], ldb >= N) or W8_B_NK ([N,K], ldb >= K). */
 int w8_mm_i8(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
              int32_t* c, int64_t ldc, int64_t m, int64_t n, int64_t k, w8_stream_t stream);
 
 /* Y[M,N] (bf16) = bf16((float(A@B) * sx[m]) * sw[n]) with the dequant fused
  * into the GEMM epilogue.  Bit-identical to mm_i8 followed by _deq.
  * Replaces NPUGemm.matmul's launches + _dequant (gemma_npu.py:127-150).
- * Same constraints as w8_mm_i8; ldy % 8 == 0. */
+ * Same constraints as w8_mm_i8 (y any pitch ldy >= N; vector stores when
+ * y is 16-byte aligned and ldy % 8 == 0). */
 int w8_gemm_dequant_bf16(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
                          const float* sx, const float* sw, uint16_t* y, int64_t ldy,
                          int64_t m, int64_t n, int64_t k, w8_stream_t stream);

@@ -96,12 +96,30 @@ def test_extreme_values_no_overflow(cuda):
     k = 16384
     a = torch.full((130, k), -128, dtype=torch.int8, device=cuda)
     a[1::2] = 127
-    w = torch.full((300, k), -128, dtype=torch.int8, device=cuda)
+    w = torch.full((304, k), -128, dtype=torch.int8, device=cuda)
     w[::3] = 127
-    c = torch.empty((130, 300), dtype=torch.int32, device=cuda)
+    c = torch.empty((130, 304), dtype=torch.int32, device=cuda)
     w8.mm_i8_nk(a, w, c)
     assert torch.equal(c, torch._int_mm(a, w.t().contiguous()))
     assert int(c[0, 1]) == k * 128 * 128
+    assert int(c[1, 0]) == k * 127 * 127 and int(c[1, 1]) == -k * 127 * 128
+
+
+@pytest.mark.parametrize("n", [300, 301, 37])
+def test_any_output_pitch(cuda, n):
+    # contiguous C with N % 4 != 0: row starts are not 16-byte aligned -> element stores
+    gen = torch.Generator().manual_seed(n)
+    a = torch.randint(-128, 128, (70, 64), dtype=torch.int8, generator=gen)
+    w = torch.randint(-128, 128, (n, 64), dtype=torch.int8, generator=gen)
+    c = torch.empty((70, n), dtype=torch.int32, device=cuda)
+    w8.mm_i8_nk(a.to(cuda), w.to(cuda), c)
+    np.testing.assert_array_equal(c.cpu().numpy(), ref.int_mm(a.numpy(), w.numpy().T))
+    sx = torch.rand(70) * 0.01
+    sw = torch.rand(n) * 0.01
+    y = torch.empty((70, n), dtype=torch.bfloat16, device=cuda)
+    w8.gemm_dequant(a.to(cuda), w.to(cuda), sx.to(cuda), sw.to(cuda), out=y)
+    want = ref.dequant(ref.int_mm(a.numpy(), w.numpy().T), sx.numpy(), sw.numpy())
+    np.testing.assert_array_equal(y.cpu().view(torch.int16).numpy().view(np.uint16), want)
 
 
 def test_k_zero_gives_zeros(cuda):

@@ -30,7 +30,7 @@ def swapped(cuda):
         for p in m.parameters():
             p.normal_(0, 0.02)
     lm = m.model.language_model
-    before = [torch.cat([l.weight.detach().clone() for l in linears]) for _, _, linears in g8.layer_groups(lm)]
+    before = [torch.cat([l.weight.detach().clone() for l in linears]) for _, _, linears in g8.layer_groups(lm)[0]]
     head_w = m.lm_head.weight.detach().clone()
     gemms = w8.to_b200(m, device=cuda)
     return m, gemms, before, head_w
