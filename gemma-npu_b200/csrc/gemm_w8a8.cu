@@ -23,6 +23,7 @@
 // No cluster launch and no multicast: every CTA issues its own TMA loads.
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -49,7 +50,11 @@ struct GemmArgs {
   const float* sw;
   int vec_out;  // output base 16-byte aligned and row pitch a multiple of 16 bytes
   int vec_sw;   // sw 16-byte aligned
+  int tma_out;  // the output tensor map is valid: epilogue stores go through TMA
 };
+
+constexpr int kEpiBufBytes = 32 * 128;  // one 32-row x 128-byte store box
+constexpr int kEpiBufs = 2;             // per epilogue warp: fill one while TMA drains the other
 
 constexpr uint32_t tmem_cols_for(int c) {
   return c <= 32 ? 32u : c <= 64 ? 64u : c <= 128 ? 128u : c <= 256 ? 256u : 512u;
@@ -60,7 +65,8 @@ struct GemmSmem {
   static constexpr int kA = kBM * kBK;
   static constexpr int kB = BN * kBK;
   static constexpr int kStage = kA + kB;
-  static constexpr int kBarOff = STAGES * kStage;
+  static constexpr int kEpiOff = STAGES * kStage;  // epilogue store staging, 1024-aligned
+  static constexpr int kBarOff = kEpiOff + kEpiWarps * kEpiBufs * kEpiBufBytes;
   static constexpr int kNumBars = 2 * STAGES + 5;  // full[S], empty[S], tfull[2], tempty[2], done
   static constexpr int kTotal = kBarOff + kNumBars * 8 + 16;
   static constexpr int kAlloc = kTotal + 1024;  // slack to align the ring to 1024 B
@@ -122,10 +128,39 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0
   }
 }
 
+// 32 int32 accumulators of columns col0.. -> 16 words of packed bf16 pairs,
+// bf16((float(acc) * sx[row]) * sw[col]) with _deq's operation order.
+__device__ __forceinline__ void dequant_pack(const GemmArgs& a, int col0, const uint32_t (&r)[32],
+                                             float sxr, uint32_t* out) {
+  float w[32];
+  if (a.vec_sw && col0 + 32 <= a.n) {
+    const float4* sw4 = reinterpret_cast<const float4*>(a.sw + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 t = __ldg(sw4 + j);
+      w[4 * j] = t.x;
+      w[4 * j + 1] = t.y;
+      w[4 * j + 2] = t.z;
+      w[4 * j + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) w[j] = col0 + j < a.n ? __ldg(a.sw + col0 + j) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float v0 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[2 * j])), sxr), w[2 * j]);
+    const float v1 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[2 * j + 1])), sxr), w[2 * j + 1]);
+    __nv_bfloat162 p = __floats2bfloat162_rn(v0, v1);
+    out[j] = *reinterpret_cast<uint32_t*>(&p);
+  }
+}
+
 template <int BN, int STAGES, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tm_a,
-                     const __grid_constant__ CUtensorMap tm_b, const GemmArgs args) {
+                     const __grid_constant__ CUtensorMap tm_b,
+                     const __grid_constant__ CUtensorMap tm_c, const GemmArgs args) {
   using L = GemmSmem<BN, STAGES>;
   static_assert(!B_MN || BN % 128 == 0, "MN-major B is loaded in 128-column boxes");
   extern __shared__ uint8_t smem_raw[];
@@ -159,6 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     prefetch_tmap(&tm_a);
     prefetch_tmap(&tm_b);
+    if (args.tma_out) prefetch_tmap(&tm_c);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
@@ -257,6 +293,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    // This warp's two store-staging boxes (32 rows x 128 B, 128-byte swizzled like TMA).
+    const uint32_t stage_base = base + L::kEpiOff + (warp - 2) * kEpiBufs * kEpiBufBytes;
+    uint32_t sbuf = 0;  // running box counter: box parity selects the buffer
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -266,22 +305,66 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int mb = tile % args.m_tiles;
       const int nb = tile / args.m_tiles;
-      const int row = mb * kBM + quarter * 32 + lane;
+      const int row0 = mb * kBM + quarter * 32;
+      const int row = row0 + lane;
       float sxr = 0.f;
       if constexpr (EPI == kEpiBf16) sxr = row < args.m ? __ldg(args.sx + row) : 0.f;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-      const int n_chunks = min(BN, args.n - nb * BN + 31) / 32;  // skip chunks wholly past N
+      const int n_cols = min(BN, args.n - nb * BN);  // columns of this tile inside N
+      if (args.tma_out) {
+        // One store box = 32 rows x 128 bytes: 32 int32 or 64 bf16 columns.
+        constexpr int kCols = EPI == kEpiI32 ? 32 : 64;
+        const int n_chunks = (n_cols + kCols - 1) / kCols;
 #pragma unroll 1
-      for (int c = 0; c < n_chunks; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
-        tmem_wait_ld();
-        store_chunk<EPI>(args, row, nb * BN + c * 32, r, sxr);
+        for (int c = 0; c < n_chunks; ++c) {
+          uint32_t v[32];  // this thread's 128-byte slice of its row
+          if constexpr (EPI == kEpiI32) {
+            tmem_ld_32x32b_x32(taddr + c * 32, v);
+            tmem_wait_ld();
+          } else {
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(taddr + c * 64, r0);
+            tmem_ld_32x32b_x32(taddr + c * 64 + 32, r1);
+            tmem_wait_ld();
+            const int col0 = nb * BN + c * 64;
+            dequant_pack(args, col0, r0, sxr, v);
+            dequant_pack(args, col0 + 32, r1, sxr, v + 16);
+          }
+          if (c == n_chunks - 1) {  // the accumulator is in registers: hand TMEM back
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(acc));
+          }
+          const uint32_t buf = stage_base + (sbuf & 1u) * kEpiBufBytes;
+          ++sbuf;
+          if (lane == 0) bulk_wait_group_read<kEpiBufs - 1>();  // the box last stored from buf is read
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            st_shared_v4(buf + lane * 128 + ((j ^ (lane & 7)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                         v[4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tm_c, buf, nb * BN + c * kCols, row0);
+            bulk_commit_group();
+          }
+        }
+      } else {
+        const int n_chunks = (n_cols + 31) / 32;
+#pragma unroll 1
+        for (int c = 0; c < n_chunks; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          tmem_wait_ld();
+          store_chunk<EPI>(args, row, nb * BN + c * 32, r, sxr);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty_bar(acc));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(tempty_bar(acc));
     }
+    if (lane == 0) bulk_wait_group<0>();  // every store of this warp has landed
   }
 
   tc_fence_before();
@@ -319,9 +402,9 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D int8 tensor [outer, inner] with row pitch `pitch` bytes, 128-byte swizzled boxes.
-static int encode_i8_2d(CUtensorMap* map, const void* ptr, int64_t inner, int64_t outer,
-                        int64_t pitch, uint32_t box_inner, uint32_t box_outer) {
+// 2-D tensor [outer, inner] with row pitch `pitch` bytes, 128-byte swizzled boxes.
+static int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* ptr, int64_t inner,
+                     int64_t outer, int64_t pitch, uint32_t box_inner, uint32_t box_outer) {
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) {
     set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -331,10 +414,9 @@ static int encode_i8_2d(CUtensorMap* map, const void* ptr, int64_t inner, int64_
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims,
-                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = enc(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed with CUresult %d (inner %lld, outer %lld, pitch %lld)",
               static_cast<int>(r), static_cast<long long>(inner), static_cast<long long>(outer),
@@ -347,7 +429,7 @@ static int encode_i8_2d(CUtensorMap* map, const void* ptr, int64_t inner, int64_
 int require_sm100(int* device);
 
 template <int BN, int STAGES, bool B_MN, int EPI>
-static int launch_gemm(int device, const CUtensorMap& ta, const CUtensorMap& tb,
+static int launch_gemm(int device, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                        const w8::GemmArgs& args, cudaStream_t stream) {
   using L = w8::GemmSmem<BN, STAGES>;
   auto kern = w8::gemm_w8a8_kernel<BN, STAGES, B_MN, EPI>;
@@ -362,7 +444,7 @@ static int launch_gemm(int device, const CUtensorMap& ta, const CUtensorMap& tb,
   if (st != W8_OK) return st;
   const int tiles = args.m_tiles * args.n_tiles;
   const int grid = tiles < sms ? tiles : sms;
-  kern<<<grid, w8::kThreads, L::kAlloc, stream>>>(ta, tb, args);
+  kern<<<grid, w8::kThreads, L::kAlloc, stream>>>(ta, tb, tc, args);
   return cuda_status(cudaGetLastError());
 }
 
@@ -398,13 +480,13 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
 
   constexpr int BN = 256;
   constexpr int STAGES = 4;
-  CUtensorMap ta, tb;
-  st = encode_i8_2d(&ta, a, k, m, lda, w8::kBK, w8::kBM);
+  CUtensorMap ta, tb, tc;
+  st = encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, m, lda, w8::kBK, w8::kBM);
   if (st != W8_OK) return st;
   if (b_layout == W8_B_NK)
-    st = encode_i8_2d(&tb, b, k, n, ldb, w8::kBK, BN);
+    st = encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, k, n, ldb, w8::kBK, BN);
   else
-    st = encode_i8_2d(&tb, b, n, k, ldb, 128, w8::kBK);
+    st = encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, n, k, ldb, 128, w8::kBK);
   if (st != W8_OK) return st;
 
   w8::GemmArgs args;
@@ -420,13 +502,24 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   args.sw = sw;
   args.vec_out = aligned(out, 16) && (ldo * out_elem) % 16 == 0;
   args.vec_sw = sw != nullptr && aligned(sw, 16);
+  // Output through TMA when the tensor map can address it (16-byte base and pitch);
+  // one box is 32 rows x 128 bytes.  Otherwise the epilogue stores directly.
+  memset(&tc, 0, sizeof(tc));
+  args.tma_out = 0;
+  if (args.vec_out) {
+    const bool i32 = epi == w8::kEpiI32;
+    st = encode_2d(&tc, i32 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, n, m,
+                   ldo * out_elem, i32 ? 32 : 64, 32);
+    if (st != W8_OK) return st;
+    args.tma_out = 1;
+  }
 
   const bool mn = b_layout == W8_B_KN;
   if (epi == w8::kEpiI32)
-    return mn ? launch_gemm<BN, STAGES, true, w8::kEpiI32>(device, ta, tb, args, stream)
-              : launch_gemm<BN, STAGES, false, w8::kEpiI32>(device, ta, tb, args, stream);
-  return mn ? launch_gemm<BN, STAGES, true, w8::kEpiBf16>(device, ta, tb, args, stream)
-            : launch_gemm<BN, STAGES, false, w8::kEpiBf16>(device, ta, tb, args, stream);
+    return mn ? launch_gemm<BN, STAGES, true, w8::kEpiI32>(device, ta, tb, tc, args, stream)
+              : launch_gemm<BN, STAGES, false, w8::kEpiI32>(device, ta, tb, tc, args, stream);
+  return mn ? launch_gemm<BN, STAGES, true, w8::kEpiBf16>(device, ta, tb, tc, args, stream)
+            : launch_gemm<BN, STAGES, false, w8::kEpiBf16>(device, ta, tb, tc, args, stream);
 }
 
 // Read (and optionally clear) the GEMM kernels' sticky device status.
