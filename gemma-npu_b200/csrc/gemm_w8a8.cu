@@ -6,21 +6,43 @@
 // and, in the bf16 variant, the _dequant that follows it (gemma_npu.py:45-47,149-150;
 // pipeline.py:55-57).
 //
-// Structure (one persistent CTA per SM, 6 warps):
-//   warp 0      TMA producer: A [128 x 128B] and B [BN x 128B] boxes into a STAGES-deep
-//               ring of 128-byte-swizzled shared-memory stages (mbarrier full/empty).
-//   warp 1      TMEM owner + MMA issuer: one thread issues 4 x tcgen05.mma (K = 32 each)
-//               per stage into a double-buffered int32 accumulator in TMEM
-//               (2 x BN columns), commits free the stage and publish finished tiles.
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w owns TMEM lanes
-//               32*(w%4)..+31 = tile rows), optional dequant, vector stores to HBM;
-//               the buffer is handed back to the MMA warp so the epilogue of tile i
-//               overlaps the main loop of tile i+1.
+// Two persistent, warp-specialised kernels (6 warps per CTA, one CTA per SM):
+//
+//   gemm_pair_kernel  (M > 128) a cluster of two CTAs on two SMs computes 256 x 256
+//       tiles with tcgen05.mma.cta_group::2: each CTA stages its 128 rows of A and its
+//       128 columns of B (K-blocks of 128 bytes, 128-byte swizzle, 6-stage ring) and
+//       holds its 128 output rows in its own TMEM.  Per SM this halves the B operand
+//       traffic of a 128 x 256 tile.
+//   gemm_single_kernel (M <= 128) one CTA computes 128 x 256 tiles (cta_group::1,
+//       4-stage ring), so a short prompt does not waste half of every pair.
+//
+// Roles in both: warp 0 issues the TMA loads; warp 1 owns TMEM and one of its threads
+// issues the MMAs (in the pair kernel only the even CTA's) into a double-buffered
+// int32 accumulator (2 x 256 TMEM columns); warps 2..5 are the epilogue: tcgen05.ld of
+// the accumulator (warp w owns TMEM lanes 32*(w%4)..+31), optional dequant, staging in
+// 128-byte-swizzled shared memory and TMA bulk tensor stores of 32-row x 128-byte
+// boxes.  The accumulator is handed back as soon as it is in registers, so the
+// epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Work schedule ("workers" = CTA pairs or CTAs, as many as are co-resident):
+//   data-parallel  worker w computes whole tiles w, w + W, w + 2W, ...
+//   stream-K       (int32 output, when whole tiles would leave a ragged last wave)
+//                  the (tile, K-block) units are cut into W equal contiguous ranges;
+//                  a tile split between workers is finished exactly: the worker that
+//                  owns its last K-block (the first thing that worker computes) stores
+//                  its partial sum, and every other contributor adds its partial into C
+//                  with a TMA reduce-add once a per-tile counter in the caller's
+//                  workspace says the store has landed.  The last contributor resets
+//                  the counter, so the workspace is all-zero again after every launch
+//                  (and every replay of a captured graph).  int32 addition is exact
+//                  and order-independent: the result is bit-identical to one pass.
+//
 // B may be K-major ([N,K], the resident layout shared with the decode GEMV) or
-// MN-major ([K,N], the reference's mm_i8 layout); the instruction descriptor's
-// B-major bit and the shared-memory descriptor strides absorb the difference.
-// Tails in M, N and K are handled by TMA zero fill (loads) and masked stores.
-// No cluster launch and no multicast: every CTA issues its own TMA loads.
+// MN-major ([K,N], the reference's mm_i8 layout); the instruction descriptor's B-major
+// bit and the shared-memory descriptor strides absorb the difference.  Tails in M, N
+// and K are handled by TMA zero fill (loads) and TMA clipping (stores).  No load uses
+// cluster multicast: every CTA issues its own TMA loads.  Every wait is bounded (see
+// common.cuh); all workers are co-resident, so a stream-K wait always ends.
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -33,11 +55,13 @@ namespace w8 {
 // Sticky device-side error word of the GEMM kernels (bounded-wait timeouts).
 __device__ int g_gemm_status = 0;
 
-constexpr int kBM = 128;      // tile rows = TMEM lanes
+constexpr int kBM = 128;      // rows per CTA = TMEM lanes
+constexpr int kBN = 256;      // columns per tile = accumulator columns
 constexpr int kBK = 128;      // K elements (= bytes) per stage: one 128-byte swizzle row
 constexpr int kUmmaK = 32;    // K of one tcgen05.mma kind::i8
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr uint32_t kTmemCols = 2 * kBN;  // two accumulators of 256 int32 columns
 
 enum EpiKind : int { kEpiI32 = 0, kEpiBf16 = 1 };
 
@@ -48,32 +72,80 @@ struct GemmArgs {
   int64_t ldo;
   const float* sx;
   const float* sw;
-  int vec_out;  // output base 16-byte aligned and row pitch a multiple of 16 bytes
-  int vec_sw;   // sw 16-byte aligned
-  int tma_out;  // the output tensor map is valid: epilogue stores go through TMA
+  int vec_out;       // output base 16-byte aligned and row pitch a multiple of 16 bytes
+  int vec_sw;        // sw 16-byte aligned
+  int tma_out;       // the output tensor map is valid: epilogue stores go through TMA
+  int stream_k;      // 1: stream-K schedule (int32 + TMA output + flags only)
+  uint32_t* flags;   // stream-K: one zero-initialised counter per tile
 };
 
 constexpr int kEpiBufBytes = 32 * 128;  // one 32-row x 128-byte store box
 constexpr int kEpiBufs = 2;             // per epilogue warp: fill one while TMA drains the other
 
-constexpr uint32_t tmem_cols_for(int c) {
-  return c <= 32 ? 32u : c <= 64 ? 64u : c <= 128 ? 128u : c <= 256 ? 256u : 512u;
-}
-
-template <int BN, int STAGES>
-struct GemmSmem {
-  static constexpr int kA = kBM * kBK;
-  static constexpr int kB = BN * kBK;
-  static constexpr int kStage = kA + kB;
-  static constexpr int kEpiOff = STAGES * kStage;  // epilogue store staging, 1024-aligned
+// Shared-memory plan of one CTA: the operand ring, the epilogue staging boxes, barriers.
+template <int STAGES, int A_BYTES, int B_BYTES>
+struct Smem {
+  static constexpr int kA = A_BYTES;
+  static constexpr int kStage = A_BYTES + B_BYTES;
+  static constexpr int kEpiOff = STAGES * kStage;  // 1024-aligned
   static constexpr int kBarOff = kEpiOff + kEpiWarps * kEpiBufs * kEpiBufBytes;
   static constexpr int kNumBars = 2 * STAGES + 5;  // full[S], empty[S], tfull[2], tempty[2], done
   static constexpr int kTotal = kBarOff + kNumBars * 8 + 16;
   static constexpr int kAlloc = kTotal + 1024;  // slack to align the ring to 1024 B
-  static constexpr uint32_t kTmemCols = tmem_cols_for(2 * BN);
+  static_assert(kStage % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(kAlloc <= 232448, "shared memory budget of one CTA exceeded");
 };
+constexpr int kPairStages = 6;
+constexpr int kSingleStages = 4;
+using PairSmem = Smem<kPairStages, kBM * kBK, 128 * kBK>;     // A half + B half per CTA
+using SingleSmem = Smem<kSingleStages, kBM * kBK, kBN * kBK>;  // A + whole B tile
 
+// ---------------------------------------------------------------- schedule
+struct Segment {
+  int tile, kb0, kb1;  // K-blocks [kb0, kb1) of one output tile
+  int contributors;    // workers that contribute to this tile (1 = whole tile here)
+};
+
+// The segments one worker computes, in order; every role of the worker walks the same list.
+struct Schedule {
+  int64_t u, u_end, units;  // stream-K cursor over (tile, K-block) units
+  int tile, workers;        // data-parallel cursor
+  bool sk;
+
+  __device__ Schedule(const GemmArgs& a, int worker, int nworkers) {
+    sk = a.stream_k != 0;
+    workers = nworkers;
+    units = static_cast<int64_t>(a.m_tiles) * a.n_tiles * a.k_blocks;
+    u = units * worker / nworkers;
+    u_end = units * (worker + 1) / nworkers;
+    tile = worker;
+  }
+  // Worker that owns unit x (the largest w with floor(w * units / workers) <= x).
+  __device__ int owner(int64_t x) const { return static_cast<int>(((x + 1) * workers - 1) / units); }
+
+  __device__ bool next(const GemmArgs& a, Segment& s) {
+    if (!sk) {
+      if (tile >= a.m_tiles * a.n_tiles) return false;
+      s.tile = tile;
+      s.kb0 = 0;
+      s.kb1 = a.k_blocks;
+      s.contributors = 1;
+      tile += workers;
+      return true;
+    }
+    if (u >= u_end) return false;
+    s.tile = static_cast<int>(u / a.k_blocks);
+    s.kb0 = static_cast<int>(u - static_cast<int64_t>(s.tile) * a.k_blocks);
+    const int64_t left = u_end - u;
+    s.kb1 = left < a.k_blocks - s.kb0 ? s.kb0 + static_cast<int>(left) : a.k_blocks;
+    u += s.kb1 - s.kb0;
+    const int64_t first = static_cast<int64_t>(s.tile) * a.k_blocks;
+    s.contributors = owner(first + a.k_blocks - 1) - owner(first) + 1;
+    return true;
+  }
+};
+
+// ---------------------------------------------------------------- epilogue
 template <int EPI>
 __device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0,
                                             const uint32_t (&r)[32], float sxr) {
@@ -96,34 +168,12 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0
     // the operation order of _deq (pipeline.py:57).
     __nv_bfloat16* dst =
         static_cast<__nv_bfloat16*>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
-    if (a.vec_out && a.vec_sw && col0 + 32 <= a.n) {
-      const float4* sw4 = reinterpret_cast<const float4*>(a.sw + col0);
-      uint32_t packed[16];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 w = __ldg(sw4 + j);
-        const float v0 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[4 * j + 0])), sxr), w.x);
-        const float v1 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[4 * j + 1])), sxr), w.y);
-        const float v2 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[4 * j + 2])), sxr), w.z);
-        const float v3 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[4 * j + 3])), sxr), w.w);
-        __nv_bfloat162 p0 = __floats2bfloat162_rn(v0, v1);
-        __nv_bfloat162 p1 = __floats2bfloat162_rn(v2, v3);
-        packed[2 * j] = *reinterpret_cast<uint32_t*>(&p0);
-        packed[2 * j + 1] = *reinterpret_cast<uint32_t*>(&p1);
-      }
-      int4* d4 = reinterpret_cast<int4*>(dst);
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        d4[j] = make_int4(static_cast<int>(packed[4 * j]), static_cast<int>(packed[4 * j + 1]),
-                          static_cast<int>(packed[4 * j + 2]), static_cast<int>(packed[4 * j + 3]));
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (col0 + j >= a.n) continue;
-        const float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), sxr),
-                                  __ldg(a.sw + col0 + j));
-        dst[j] = __float2bfloat16_rn(v);
-      }
+    for (int j = 0; j < 32; ++j) {
+      if (col0 + j >= a.n) continue;
+      const float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), sxr),
+                                __ldg(a.sw + col0 + j));
+      dst[j] = __float2bfloat16_rn(v);
     }
   }
 }
@@ -156,13 +206,116 @@ __device__ __forceinline__ void dequant_pack(const GemmArgs& a, int col0, const 
   }
 }
 
-template <int BN, int STAGES, bool B_MN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
-    gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tm_a,
-                     const __grid_constant__ CUtensorMap tm_b,
+// Drain one 32-row slice of a finished accumulator (called by one whole epilogue warp).
+// `taddr` addresses the warp's TMEM lanes at the accumulator's first column; rows
+// row0.. and columns col_base.. of the output.  `release` hands the accumulator back to
+// the MMA issuer once its last columns are in registers.  With `reduce`, the boxes are
+// added into C (TMA reduce-add) instead of stored.
+template <int EPI, typename Release>
+__device__ __forceinline__ void epilogue_rows(const GemmArgs& args, const CUtensorMap* tm_c,
+                                              uint32_t taddr, int row0, int col_base, float sxr,
+                                              uint32_t stage_base, uint32_t& sbuf, int lane,
+                                              bool reduce, Release release) {
+  const int n_cols = min(kBN, args.n - col_base);  // columns of this tile inside N
+  const int row = row0 + lane;
+  if (args.tma_out) {
+    // One store box = 32 rows x 128 bytes: 32 int32 or 64 bf16 columns.
+    constexpr int kCols = EPI == kEpiI32 ? 32 : 64;
+    const int n_chunks = (n_cols + kCols - 1) / kCols;
+#pragma unroll 1
+    for (int c = 0; c < n_chunks; ++c) {
+      uint32_t v[32];  // this thread's 128-byte slice of its row
+      if constexpr (EPI == kEpiI32) {
+        tmem_ld_32x32b_x32(taddr + c * 32, v);
+        tmem_wait_ld();
+      } else {
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(taddr + c * 64, r0);
+        tmem_ld_32x32b_x32(taddr + c * 64 + 32, r1);
+        tmem_wait_ld();
+        const int col0 = col_base + c * 64;
+        dequant_pack(args, col0, r0, sxr, v);
+        dequant_pack(args, col0 + 32, r1, sxr, v + 16);
+      }
+      if (c == n_chunks - 1) {  // the accumulator is in registers: hand TMEM back
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) release();
+      }
+      const uint32_t buf = stage_base + (sbuf & 1u) * kEpiBufBytes;
+      ++sbuf;
+      if (lane == 0) bulk_wait_group_read<kEpiBufs - 1>();  // the box last stored from buf is read
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        st_shared_v4(buf + lane * 128 + ((j ^ (lane & 7)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                     v[4 * j + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (reduce)
+          tma_reduce_add_2d(tm_c, buf, col_base + c * kCols, row0);
+        else
+          tma_store_2d(tm_c, buf, col_base + c * kCols, row0);
+        bulk_commit_group();
+      }
+    }
+  } else {
+    const int n_chunks = (n_cols + 31) / 32;
+#pragma unroll 1
+    for (int c = 0; c < n_chunks; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + c * 32, r);
+      tmem_wait_ld();
+      store_chunk<EPI>(args, row, col_base + c * 32, r, sxr);
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) release();
+  }
+}
+
+// One epilogue warp's part of a segment: for a stream-K tile split between workers,
+// the owner of the last K-block stores and signals; the others wait, then add.
+// `warps_per_contrib` epilogue warps make up one contributor.
+template <int EPI, typename Release>
+__device__ __forceinline__ void epilogue_segment(const GemmArgs& args, const CUtensorMap* tm_c,
+                                                 const Segment& s, uint32_t taddr, int row0,
+                                                 int col_base, float sxr, uint32_t stage_base,
+                                                 uint32_t& sbuf, int lane, int warps_per_contrib,
+                                                 Release release) {
+  const bool split = s.contributors > 1;
+  const bool tail = s.kb1 == args.k_blocks;  // owns the tile's last K-block: stores first
+  uint32_t* flag = split ? args.flags + s.tile : nullptr;
+  if (split && !tail) {
+    bool ok = true;
+    if (lane == 0) {
+      ok = wait_counter_bounded(flag, static_cast<uint32_t>(warps_per_contrib), &g_gemm_status);
+      fence_proxy_async_global();
+    }
+    __syncwarp();
+    (void)ok;  // on a timeout the sum is wrong and the status says so; the launch still ends
+  }
+  epilogue_rows<EPI>(args, tm_c, taddr, row0, col_base, sxr, stage_base, sbuf, lane, split && !tail,
+                     release);
+  if (split && lane == 0) {
+    bulk_wait_group<0>();  // this warp's boxes have landed in C
+    __threadfence();
+    const uint32_t total = static_cast<uint32_t>(warps_per_contrib * s.contributors);
+    if (atomicAdd(flag, 1u) == total - 1) atomicExch(flag, 0u);  // last one: reset for the next launch
+  }
+  __syncwarp();
+}
+
+// =====================================================================================
+// 256 x 256 tiles on a CTA pair (tcgen05 cta_group::2)
+// =====================================================================================
+template <bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                      const __grid_constant__ CUtensorMap tm_c, const GemmArgs args) {
-  using L = GemmSmem<BN, STAGES>;
-  static_assert(!B_MN || BN % 128 == 0, "MN-major B is loaded in 128-column boxes");
+  using L = PairSmem;
+  constexpr int STAGES = kPairStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // swizzle atoms need 1024-byte alignment
@@ -179,6 +332,193 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = the CTA that issues the MMAs
+  const uint32_t peer = rank ^ 1u;
+  pdl_launch_dependents();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);   // leader: one arrive.expect_tx + both CTAs' TMA bytes
+      mbar_init(empty_bar(s), 1);  // both: one MMA commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);               // both: one MMA commit
+      mbar_init(tempty_bar(a), 2 * kEpiWarps);  // leader: the epilogue warps of both CTAs
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tm_a);
+    prefetch_tmap(&tm_b);
+    if (args.tma_out) prefetch_tmap(&tm_c);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  pdl_wait();  // the previous kernel's writes (our A, B) are visible from here on
+  const uint32_t tmem_base = *tmem_slot;
+  const int worker = blockIdx.x >> 1;
+  const int workers = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs): this CTA's A rows and B columns
+      Schedule sched(args, worker, workers);
+      Segment sg;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      while (ok && sched.next(args, sg)) {
+        const int mb = sg.tile % args.m_tiles;
+        const int nb = sg.tile / args.m_tiles;
+        const int a_row = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int b_col = nb * kBN + static_cast<int>(rank) * 128;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+          if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, &g_gemm_status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + stage * L::kStage;
+          const uint32_t sb = sa + L::kA;
+          const uint32_t fb = mapa_shared(full_bar(stage), 0);  // the leader's full barrier
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * L::kStage);
+          tma_load_2d_pair(sa, &tm_a, fb, kb * kBK, a_row);
+          if constexpr (B_MN)
+            tma_load_2d_pair(sb, &tm_b, fb, b_col, kb * kBK);
+          else
+            tma_load_2d_pair(sb, &tm_b, fb, kb * kBK, b_col);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Every copy issued here was consumed by the leader's MMA (it waited on the full
+      // barrier that counts both CTAs' bytes) unless a wait gave up; either way the
+      // closing cluster barrier keeps both CTAs resident until the end.
+    }
+  } else if (warp == 1) {
+    if (rank == 0 && lane == 0) {
+      // ---------------- MMA issuer (leader CTA only)
+      constexpr uint32_t idesc = idesc_i8(2 * kBM, kBN, B_MN);
+      const uint32_t empty_peer0 = mapa_shared(empty_bar(0), peer);
+      const uint32_t tfull_peer0 = mapa_shared(tfull_bar(0), peer);
+      Schedule sched(args, worker, workers);
+      Segment sg;
+      int stage = 0, local = 0;
+      uint32_t phase = 0;
+      bool ok = true, issued = false;
+      while (ok && sched.next(args, sg)) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        ++local;
+        if (!mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, &g_gemm_status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * kBN;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+          if (!mbar_wait_bounded(full_bar(stage), phase, abort_flag, &g_gemm_status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + stage * L::kStage;
+          const uint32_t sb = sa + L::kA;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            const uint64_t ad = smem_desc_sw128(sa + k * kUmmaK, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(sb + k * kUmmaK * 128, 128 * kBK, 1024)
+                                     : smem_desc_sw128(sb + k * kUmmaK, 16, 1024);
+            mma_i8_pair(d, ad, bd, idesc, (kb > sg.kb0 || k > 0) ? 1u : 0u);
+          }
+          issued = true;
+          mma_commit_pair(empty_bar(stage));           // our stage is free ...
+          mma_commit_pair(empty_peer0 + 8u * stage);   // ... and the peer's
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(tfull_bar(acc));
+        mma_commit_pair(tfull_peer0 + 8u * acc);
+      }
+      // Every MMA must retire before either CTA releases its TMEM.
+      if (issued) {
+        mma_commit_pair(done_bar);
+        mbar_wait_bounded(done_bar, 0, nullptr, &g_gemm_status);
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows of every 256 x 256 tile
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t stage_base = base + L::kEpiOff + (warp - 2) * kEpiBufs * kEpiBufBytes;
+    const uint32_t tempty_leader0 = mapa_shared(tempty_bar(0), 0);
+    Schedule sched(args, worker, workers);
+    Segment sg;
+    uint32_t sbuf = 0;
+    int local = 0;
+    while (sched.next(args, sg)) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      ++local;
+      const bool ok = mbar_wait_bounded(tfull_bar(acc), acc_phase, abort_flag, &g_gemm_status);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int mb = sg.tile % args.m_tiles;
+      const int nb = sg.tile / args.m_tiles;
+      const int row0 = mb * 2 * kBM + static_cast<int>(rank) * kBM + quarter * 32;
+      float sxr = 0.f;
+      if constexpr (EPI == kEpiBf16) sxr = row0 + lane < args.m ? __ldg(args.sx + row0 + lane) : 0.f;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
+      epilogue_segment<EPI>(args, &tm_c, sg, taddr, row0, nb * kBN, sxr, stage_base, sbuf, lane,
+                            2 * kEpiWarps, [&] { mbar_arrive_cluster(tempty_leader0 + 8u * acc); });
+    }
+    if (lane == 0) bulk_wait_group<0>();  // every store of this warp has landed
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still touch its barriers or TMEM
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+// =====================================================================================
+// 128 x 256 tiles on one CTA (tcgen05 cta_group::1), for M <= 128
+// =====================================================================================
+template <bool B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_single_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                       const __grid_constant__ CUtensorMap tm_c, const GemmArgs args) {
+  using L = SingleSmem;
+  constexpr int STAGES = kSingleStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw);
+  const uint32_t bar0 = base + L::kBarOff;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBarOff + L::kNumBars * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+  const uint32_t done_bar = bar0 + 8u * (2 * STAGES + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -197,25 +537,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (args.tma_out) prefetch_tmap(&tm_c);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // the previous kernel's writes (our A, B) are visible from here on
   const uint32_t tmem_base = *tmem_slot;
-  const int num_tiles = args.m_tiles * args.n_tiles;
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
+      Schedule sched(args, blockIdx.x, gridDim.x);
+      Segment sg;
       int stage = 0;
       uint32_t phase = 0, issued_mask = 0, last_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int mb = tile % args.m_tiles;
-        const int nb = tile / args.m_tiles;
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+      while (ok && sched.next(args, sg)) {
+        const int mb = sg.tile % args.m_tiles;
+        const int nb = sg.tile / args.m_tiles;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, &g_gemm_status)) {
             ok = false;
             break;
@@ -226,10 +568,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(sa, &tm_a, full_bar(stage), kb * kBK, mb * kBM);
           if constexpr (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 128; ++j)
-              tma_load_2d(sb + j * 128 * kBK, &tm_b, full_bar(stage), nb * BN + j * 128, kb * kBK);
+            for (int j = 0; j < kBN / 128; ++j)
+              tma_load_2d(sb + j * 128 * kBK, &tm_b, full_bar(stage), nb * kBN + j * 128, kb * kBK);
           } else {
-            tma_load_2d(sb, &tm_b, full_bar(stage), kb * kBK, nb * BN);
+            tma_load_2d(sb, &tm_b, full_bar(stage), kb * kBK, nb * kBN);
           }
           issued_mask |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
@@ -241,25 +583,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Our copies still in flight must land before the CTA may exit.
       for (int s = 0; s < STAGES; ++s)
-        if (issued_mask & (1u << s)) mbar_wait_bounded(full_bar(s), (last_phase >> s) & 1u, nullptr, &g_gemm_status);
+        if (issued_mask & (1u << s))
+          mbar_wait_bounded(full_bar(s), (last_phase >> s) & 1u, nullptr, &g_gemm_status);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
-      constexpr uint32_t idesc = idesc_i8(kBM, BN, B_MN);
+      constexpr uint32_t idesc = idesc_i8(kBM, kBN, B_MN);
+      Schedule sched(args, blockIdx.x, gridDim.x);
+      Segment sg;
       int stage = 0, local = 0;
       uint32_t phase = 0;
       bool ok = true, issued = false;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      while (ok && sched.next(args, sg)) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
+        ++local;
         if (!mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, &g_gemm_status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem_base + acc * BN;
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+        const uint32_t d = tmem_base + acc * kBN;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait_bounded(full_bar(stage), phase, abort_flag, &g_gemm_status)) {
             ok = false;
             break;
@@ -272,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t ad = smem_desc_sw128(sa + k * kUmmaK, 16, 1024);
             const uint64_t bd = B_MN ? smem_desc_sw128(sb + k * kUmmaK * 128, 128 * kBK, 1024)
                                      : smem_desc_sw128(sb + k * kUmmaK, 16, 1024);
-            mma_i8(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            mma_i8(d, ad, bd, idesc, (kb > sg.kb0 || k > 0) ? 1u : 0u);
           }
           issued = true;
           mma_commit(empty_bar(stage));
@@ -284,7 +630,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         mma_commit(tfull_bar(acc));
       }
-      // Every MMA this thread issued must retire before the TMEM is released.
       if (issued) {
         mma_commit(done_bar);
         mbar_wait_bounded(done_bar, 0, nullptr, &g_gemm_status);
@@ -292,79 +637,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    // This warp's two store-staging boxes (32 rows x 128 B, 128-byte swizzled like TMA).
+    const int quarter = warp & 3;
     const uint32_t stage_base = base + L::kEpiOff + (warp - 2) * kEpiBufs * kEpiBufBytes;
-    uint32_t sbuf = 0;  // running box counter: box parity selects the buffer
+    Schedule sched(args, blockIdx.x, gridDim.x);
+    Segment sg;
+    uint32_t sbuf = 0;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    while (sched.next(args, sg)) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      ++local;
       const bool ok = mbar_wait_bounded(tfull_bar(acc), acc_phase, abort_flag, &g_gemm_status);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const int mb = tile % args.m_tiles;
-      const int nb = tile / args.m_tiles;
+      const int mb = sg.tile % args.m_tiles;
+      const int nb = sg.tile / args.m_tiles;
       const int row0 = mb * kBM + quarter * 32;
-      const int row = row0 + lane;
       float sxr = 0.f;
-      if constexpr (EPI == kEpiBf16) sxr = row < args.m ? __ldg(args.sx + row) : 0.f;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-      const int n_cols = min(BN, args.n - nb * BN);  // columns of this tile inside N
-      if (args.tma_out) {
-        // One store box = 32 rows x 128 bytes: 32 int32 or 64 bf16 columns.
-        constexpr int kCols = EPI == kEpiI32 ? 32 : 64;
-        const int n_chunks = (n_cols + kCols - 1) / kCols;
-#pragma unroll 1
-        for (int c = 0; c < n_chunks; ++c) {
-          uint32_t v[32];  // this thread's 128-byte slice of its row
-          if constexpr (EPI == kEpiI32) {
-            tmem_ld_32x32b_x32(taddr + c * 32, v);
-            tmem_wait_ld();
-          } else {
-            uint32_t r0[32], r1[32];
-            tmem_ld_32x32b_x32(taddr + c * 64, r0);
-            tmem_ld_32x32b_x32(taddr + c * 64 + 32, r1);
-            tmem_wait_ld();
-            const int col0 = nb * BN + c * 64;
-            dequant_pack(args, col0, r0, sxr, v);
-            dequant_pack(args, col0 + 32, r1, sxr, v + 16);
-          }
-          if (c == n_chunks - 1) {  // the accumulator is in registers: hand TMEM back
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty_bar(acc));
-          }
-          const uint32_t buf = stage_base + (sbuf & 1u) * kEpiBufBytes;
-          ++sbuf;
-          if (lane == 0) bulk_wait_group_read<kEpiBufs - 1>();  // the box last stored from buf is read
-          __syncwarp();
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            st_shared_v4(buf + lane * 128 + ((j ^ (lane & 7)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
-                         v[4 * j + 3]);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tm_c, buf, nb * BN + c * kCols, row0);
-            bulk_commit_group();
-          }
-        }
-      } else {
-        const int n_chunks = (n_cols + 31) / 32;
-#pragma unroll 1
-        for (int c = 0; c < n_chunks; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(taddr + c * 32, r);
-          tmem_wait_ld();
-          store_chunk<EPI>(args, row, nb * BN + c * 32, r, sxr);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(tempty_bar(acc));
-      }
+      if constexpr (EPI == kEpiBf16) sxr = row0 + lane < args.m ? __ldg(args.sx + row0 + lane) : 0.f;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
+      epilogue_segment<EPI>(args, &tm_c, sg, taddr, row0, nb * kBN, sxr, stage_base, sbuf, lane,
+                            kEpiWarps, [&] { mbar_arrive(tempty_bar(acc)); });
     }
-    if (lane == 0) bulk_wait_group<0>();  // every store of this warp has landed
+    if (lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();
@@ -372,7 +667,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, L::kTmemCols);
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -428,38 +723,131 @@ static int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* pt
 
 int require_sm100(int* device);
 
-template <int BN, int STAGES, bool B_MN, int EPI>
-static int launch_gemm(int device, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
-                       const w8::GemmArgs& args, cudaStream_t stream) {
-  using L = w8::GemmSmem<BN, STAGES>;
-  auto kern = w8::gemm_w8a8_kernel<BN, STAGES, B_MN, EPI>;
-  static bool attr_done[64] = {};
+template <typename Kernel>
+static int set_smem_once(int device, Kernel kern, int bytes, bool* done) {
   if (device < 0 || device >= 64) return W8_ERR_UNSUPPORTED;
-  if (!attr_done[device]) {
-    W8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
-    attr_done[device] = true;
+  if (!done[device]) {
+    W8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[device] = true;
   }
-  int sms = 0;
-  const int st = num_sms(&sms);
+  return W8_OK;
+}
+
+// Co-resident CTA pairs of the pair kernel on this device (a GPC with an odd number of
+// SMs leaves one idle), cached per device.
+template <bool B_MN, int EPI>
+static int pair_capacity(int device, int* out) {
+  auto kern = w8::gemm_pair_kernel<B_MN, EPI>;
+  static bool done[64] = {};
+  static int cap[64] = {};
+  int st = set_smem_once(device, kern, w8::PairSmem::kAlloc, done);
   if (st != W8_OK) return st;
-  const int tiles = args.m_tiles * args.n_tiles;
-  const int grid = tiles < sms ? tiles : sms;
-  kern<<<grid, w8::kThreads, L::kAlloc, stream>>>(ta, tb, tc, args);
-  return cuda_status(cudaGetLastError());
+  if (cap[device] == 0) {
+    int sms = 0;
+    st = num_sms(&sms);
+    if (st != W8_OK) return st;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms & ~1, 1, 1);
+    cfg.blockDim = dim3(w8::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = w8::PairSmem::kAlloc;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    W8_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    cap[device] = n > 0 ? n : 1;
+  }
+  *out = cap[device];
+  return W8_OK;
+}
+
+// Launch with programmatic stream serialization: the kernel may be scheduled while the
+// previous kernel on the stream drains; it waits (griddepcontrol.wait) before touching
+// global memory, so only its launch and prologue overlap.
+template <typename Kernel>
+static int launch_pdl(Kernel kern, int grid, int smem, cudaStream_t stream, const CUtensorMap& ta,
+                      const CUtensorMap& tb, const CUtensorMap& tc, const w8::GemmArgs& args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(w8::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, args));
+}
+
+// Stream-K pays off when whole tiles would leave the last wave of workers mostly idle
+// and each tile is long enough (K) that splitting it costs little next to its MMAs.
+static bool want_stream_k(int64_t tiles, int workers, int k_blocks) {
+  if (k_blocks < 24) return false;
+  const int64_t waves = (tiles + workers - 1) / workers;
+  return tiles * 100 < waves * workers * 90;  // whole-tile efficiency below 90 %
+}
+
+template <bool B_MN, int EPI>
+static int launch_pair(int device, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                       w8::GemmArgs args, int64_t flag_words, cudaStream_t stream) {
+  auto kern = w8::gemm_pair_kernel<B_MN, EPI>;
+  int cap = 0;
+  int st = pair_capacity<B_MN, EPI>(device, &cap);
+  if (st != W8_OK) return st;
+  const int64_t tiles = static_cast<int64_t>(args.m_tiles) * args.n_tiles;
+  int workers = static_cast<int>(tiles < cap ? tiles : cap);
+  args.stream_k = 0;
+  if (EPI == w8::kEpiI32 && args.tma_out && args.flags != nullptr && flag_words >= tiles &&
+      want_stream_k(tiles, cap, args.k_blocks)) {
+    const int64_t units = tiles * args.k_blocks;
+    workers = static_cast<int>(units < cap ? units : cap);
+    args.stream_k = 1;
+  }
+  return launch_pdl(kern, 2 * workers, w8::PairSmem::kAlloc, stream, ta, tb, tc, args);
+}
+
+template <bool B_MN, int EPI>
+static int launch_single(int device, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                         w8::GemmArgs args, int64_t flag_words, cudaStream_t stream) {
+  auto kern = w8::gemm_single_kernel<B_MN, EPI>;
+  static bool done[64] = {};
+  int st = set_smem_once(device, kern, w8::SingleSmem::kAlloc, done);
+  if (st != W8_OK) return st;
+  int sms = 0;
+  st = num_sms(&sms);
+  if (st != W8_OK) return st;
+  const int64_t tiles = static_cast<int64_t>(args.m_tiles) * args.n_tiles;
+  int workers = static_cast<int>(tiles < sms ? tiles : sms);
+  args.stream_k = 0;
+  if (EPI == w8::kEpiI32 && args.tma_out && args.flags != nullptr && flag_words >= tiles &&
+      want_stream_k(tiles, sms, args.k_blocks)) {
+    const int64_t units = tiles * args.k_blocks;
+    workers = static_cast<int>(units < sms ? units : sms);
+    args.stream_k = 1;
+  }
+  return launch_pdl(kern, workers, w8::SingleSmem::kAlloc, stream, ta, tb, tc, args);
 }
 
 static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
                        void* out, int64_t ldo, int out_elem, const float* sx, const float* sw,
-                       int64_t m, int64_t n, int64_t k, cudaStream_t stream, int epi) {
+                       int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
+                       cudaStream_t stream, int epi) {
   W8_CHECK_ARG(m >= 0 && n >= 0 && k >= 0, "negative size (m=%lld n=%lld k=%lld)", (long long)m,
                (long long)n, (long long)k);
   W8_CHECK_ARG(m < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31), "size beyond int32 range");
   W8_CHECK_ARG(b_layout == W8_B_KN || b_layout == W8_B_NK, "b_layout must be W8_B_KN or W8_B_NK");
+  W8_CHECK_ARG(workspace_bytes >= 0, "negative workspace size");
   if (m == 0 || n == 0) return W8_OK;
   W8_CHECK_ARG(out != nullptr, "null output pointer");
   W8_CHECK_ARG(ldo >= n, "output row pitch %lld < n %lld", (long long)ldo, (long long)n);
   W8_CHECK_ALIGN(aligned(out, out_elem), "output must be aligned to its element size");
   if (epi == w8::kEpiBf16) W8_CHECK_ARG(sx != nullptr && sw != nullptr, "null scale pointer");
+  W8_CHECK_ALIGN(workspace == nullptr || aligned(workspace, 4), "workspace must be 4-byte aligned");
   int device = 0;
   int st = require_sm100(&device);
   if (st != W8_OK) return st;
@@ -478,13 +866,14 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   else
     W8_CHECK_ARG(ldb >= k, "ldb %lld < k %lld for an [N,K] B", (long long)ldb, (long long)k);
 
-  constexpr int BN = 256;
-  constexpr int STAGES = 4;
+  const bool pair = m > w8::kBM;            // 256-row tiles on CTA pairs
+  const int rows_per_tile = pair ? 2 * w8::kBM : w8::kBM;
+  const uint32_t b_box_n = pair ? 128 : w8::kBN;  // B columns one CTA stages per K-block
   CUtensorMap ta, tb, tc;
   st = encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, m, lda, w8::kBK, w8::kBM);
   if (st != W8_OK) return st;
   if (b_layout == W8_B_NK)
-    st = encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, k, n, ldb, w8::kBK, BN);
+    st = encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, k, n, ldb, w8::kBK, b_box_n);
   else
     st = encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, n, k, ldb, 128, w8::kBK);
   if (st != W8_OK) return st;
@@ -493,8 +882,8 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   args.m = static_cast<int>(m);
   args.n = static_cast<int>(n);
   args.k = static_cast<int>(k);
-  args.m_tiles = static_cast<int>((m + w8::kBM - 1) / w8::kBM);
-  args.n_tiles = static_cast<int>((n + BN - 1) / BN);
+  args.m_tiles = static_cast<int>((m + rows_per_tile - 1) / rows_per_tile);
+  args.n_tiles = static_cast<int>((n + w8::kBN - 1) / w8::kBN);
   args.k_blocks = static_cast<int>((k + w8::kBK - 1) / w8::kBK);
   args.out = out;
   args.ldo = ldo;
@@ -502,6 +891,9 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   args.sw = sw;
   args.vec_out = aligned(out, 16) && (ldo * out_elem) % 16 == 0;
   args.vec_sw = sw != nullptr && aligned(sw, 16);
+  args.stream_k = 0;
+  args.flags = static_cast<uint32_t*>(workspace);
+  const int64_t flag_words = workspace_bytes / 4;
   // Output through TMA when the tensor map can address it (16-byte base and pitch);
   // one box is 32 rows x 128 bytes.  Otherwise the epilogue stores directly.
   memset(&tc, 0, sizeof(tc));
@@ -515,11 +907,19 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   }
 
   const bool mn = b_layout == W8_B_KN;
-  if (epi == w8::kEpiI32)
-    return mn ? launch_gemm<BN, STAGES, true, w8::kEpiI32>(device, ta, tb, tc, args, stream)
-              : launch_gemm<BN, STAGES, false, w8::kEpiI32>(device, ta, tb, tc, args, stream);
-  return mn ? launch_gemm<BN, STAGES, true, w8::kEpiBf16>(device, ta, tb, tc, args, stream)
-            : launch_gemm<BN, STAGES, false, w8::kEpiBf16>(device, ta, tb, tc, args, stream);
+  const bool i32 = epi == w8::kEpiI32;
+  if (pair) {
+    if (i32)
+      return mn ? launch_pair<true, w8::kEpiI32>(device, ta, tb, tc, args, flag_words, stream)
+                : launch_pair<false, w8::kEpiI32>(device, ta, tb, tc, args, flag_words, stream);
+    return mn ? launch_pair<true, w8::kEpiBf16>(device, ta, tb, tc, args, flag_words, stream)
+              : launch_pair<false, w8::kEpiBf16>(device, ta, tb, tc, args, flag_words, stream);
+  }
+  if (i32)
+    return mn ? launch_single<true, w8::kEpiI32>(device, ta, tb, tc, args, flag_words, stream)
+              : launch_single<false, w8::kEpiI32>(device, ta, tb, tc, args, flag_words, stream);
+  return mn ? launch_single<true, w8::kEpiBf16>(device, ta, tb, tc, args, flag_words, stream)
+            : launch_single<false, w8::kEpiBf16>(device, ta, tb, tc, args, flag_words, stream);
 }
 
 // Read (and optionally clear) the GEMM kernels' sticky device status.
@@ -537,17 +937,31 @@ int gemm_device_status(int clear, int* out) {
 
 }  // namespace w8host
 
+extern "C" int64_t w8_mm_i8_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  (void)k;
+  if (m <= 0 || n <= 0) return 0;
+  // One 32-bit counter per output tile of the smaller (128 x 256) tiling.
+  return 4 * ((m + w8::kBM - 1) / w8::kBM) * ((n + w8::kBN - 1) / w8::kBN);
+}
+
 extern "C" int w8_mm_i8(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
                         int32_t* c, int64_t ldc, int64_t m, int64_t n, int64_t k,
                         w8_stream_t stream) {
-  return w8host::gemm_common(a, lda, b, ldb, b_layout, c, ldc, 4, nullptr, nullptr, m, n, k,
-                             reinterpret_cast<cudaStream_t>(stream), w8::kEpiI32);
+  return w8host::gemm_common(a, lda, b, ldb, b_layout, c, ldc, 4, nullptr, nullptr, m, n, k, nullptr,
+                             0, reinterpret_cast<cudaStream_t>(stream), w8::kEpiI32);
+}
+
+extern "C" int w8_mm_i8_ws(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
+                           int32_t* c, int64_t ldc, int64_t m, int64_t n, int64_t k, void* workspace,
+                           int64_t workspace_bytes, w8_stream_t stream) {
+  return w8host::gemm_common(a, lda, b, ldb, b_layout, c, ldc, 4, nullptr, nullptr, m, n, k, workspace,
+                             workspace_bytes, reinterpret_cast<cudaStream_t>(stream), w8::kEpiI32);
 }
 
 extern "C" int w8_gemm_dequant_bf16(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb,
                                     int b_layout, const float* sx, const float* sw, uint16_t* y,
                                     int64_t ldy, int64_t m, int64_t n, int64_t k,
                                     w8_stream_t stream) {
-  return w8host::gemm_common(a, lda, b, ldb, b_layout, y, ldy, 2, sx, sw, m, n, k,
+  return w8host::gemm_common(a, lda, b, ldb, b_layout, y, ldy, 2, sx, sw, m, n, k, nullptr, 0,
                              reinterpret_cast<cudaStream_t>(stream), w8::kEpiBf16);
 }

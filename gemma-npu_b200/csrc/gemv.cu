@@ -70,6 +70,26 @@ __global__ void __launch_bounds__(kGemvThreads)
   const int lane = threadIdx.x & 31;
   const int team = warp / S;
   const int sl = warp % S;
+  pdl_launch_dependents();
+
+  const int stride = gridDim.x * kTeams * R;
+  const int first = (blockIdx.x * kTeams + team) * R;
+  uint4 wv[R][J];
+  auto load_w = [&](int n0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int c = 0; c < J; ++c) {
+        const int k0 = ((sl * J + c) * 32 + lane) * 16;
+        const int row = n0 + r;
+        wv[r][c] = (row < n && k0 < k) ? ldg_stream(w + static_cast<int64_t>(row) * ldw + k0)
+                                       : make_uint4(0u, 0u, 0u, 0u);
+      }
+  };
+  // The weights do not depend on the previous kernel: start streaming them before
+  // waiting for it (only the activation row does).
+  load_w(first);
+  pdl_wait();
 
   for (int t = 0; t < t_count; ++t) {
     // This lane's slice of the activation row, in fp32.
@@ -92,18 +112,8 @@ __global__ void __launch_bounds__(kGemvThreads)
       }
     }
 
-    const int stride = gridDim.x * kTeams * R;
-    for (int n0 = (blockIdx.x * kTeams + team) * R; n0 < n; n0 += stride) {
-      uint4 wv[R][J];
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int c = 0; c < J; ++c) {
-          const int k0 = ((sl * J + c) * 32 + lane) * 16;
-          const int row = n0 + r;
-          wv[r][c] = (row < n && k0 < k) ? ldg_stream(w + static_cast<int64_t>(row) * ldw + k0)
-                                         : make_uint4(0u, 0u, 0u, 0u);
-        }
+    for (int n0 = first; n0 < n; n0 += stride) {
+      if (t > 0 || n0 != first) load_w(n0);
       float acc[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
@@ -173,8 +183,19 @@ static int launch_gemv(const __nv_bfloat16* x, int64_t ldx, const int8_t* w, int
   const int64_t need = (static_cast<int64_t>(n) + rows_per_cta - 1) / rows_per_cta;
   const int64_t cap_blocks = static_cast<int64_t>(sms) * per_sm;
   const int grid = static_cast<int>(need < cap_blocks ? need : cap_blocks);
-  kern<<<grid, w8::kGemvThreads, 0, stream>>>(x, ldx, w, ldw, s, y, ldy, t, n, k, cap);
-  return cuda_status(cudaGetLastError());
+  // Programmatic stream serialization: the kernel may start streaming its weights while
+  // the previous kernel on the stream drains (it waits before reading x).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(w8::kGemvThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, x, ldx, w, ldw, s, y, ldy, t, n, k, cap));
 }
 
 template <bool LOGITS>

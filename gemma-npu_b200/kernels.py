@@ -64,6 +64,30 @@ def _ld(t):
     return t.stride(0) if t.shape[0] > 1 else max(t.shape[1], t.stride(0))
 
 
+# Stream-K counters for the GEMMs, one zero-filled buffer per (device, stream): the
+# kernel leaves it zero after every call, and calls on one stream never overlap.
+_WORKSPACES = {}
+_MIN_WORKSPACE_WORDS = 1 << 16
+
+
+def _workspace(device, stream, nbytes):
+    key = (device.index, stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() * 4 < nbytes:
+        words = max(_MIN_WORKSPACE_WORDS, -(-nbytes // 4))
+        ws = torch.zeros(words, dtype=torch.int32, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def _mm(a, b, layout, c, M, N, K):
+    stream = _stream(a)
+    nbytes = _lib.lib().w8_mm_i8_workspace_bytes(M, N, K)
+    ws = _workspace(a.device, stream, nbytes)
+    _lib.call("w8_mm_i8_ws", a.data_ptr(), _ld(a), b.data_ptr(), _ld(b), layout, c.data_ptr(), _ld(c),
+              M, N, K, ws.data_ptr(), ws.numel() * 4, stream)
+
+
 def _check_vector(t, name, dtype, n):
     _need(isinstance(t, torch.Tensor) and t.is_cuda, f"{name} must be a CUDA tensor")
     _need(t.dtype == dtype, f"{name} must be {dtype} (got {t.dtype})")
@@ -86,8 +110,7 @@ def mm_i8(a, b, c):
     N = b.shape[1]
     _need(tuple(c.shape) == (M, N), f"c must be ({M}, {N}) (got {tuple(c.shape)})")
     _need(a.device == b.device == c.device, "a, b, c must be on one device")
-    _lib.call("w8_mm_i8", a.data_ptr(), _ld(a), b.data_ptr(), _ld(b), W8_B_KN, c.data_ptr(), _ld(c),
-              M, N, K, _stream(a))
+    _mm(a, b, W8_B_KN, c, M, N, K)
     return c
 
 
@@ -101,8 +124,7 @@ def mm_i8_nk(a, w, c):
     _need(w.shape[1] == K, f"inner sizes differ: a {tuple(a.shape)}, w {tuple(w.shape)}")
     _need(tuple(c.shape) == (M, N), f"c must be ({M}, {N}) (got {tuple(c.shape)})")
     _need(a.device == w.device == c.device, "a, w, c must be on one device")
-    _lib.call("w8_mm_i8", a.data_ptr(), _ld(a), w.data_ptr(), _ld(w), W8_B_NK, c.data_ptr(), _ld(c),
-              M, N, K, _stream(a))
+    _mm(a, w, W8_B_NK, c, M, N, K)
     return c
 
 

@@ -66,6 +66,19 @@ int w8_abi_version(void);
 int w8_mm_i8(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
              int32_t* c, int64_t ldc, int64_t m, int64_t n, int64_t k, w8_stream_t stream);
 
+/* w8_mm_i8 with a caller-provided workspace, which lets the kernel balance a ragged
+ * last wave of tiles (stream-K: tiles split across SMs are summed exactly in int32).
+ * Same result bits as w8_mm_i8.  The workspace holds one 32-bit counter per tile:
+ * it must be zero-filled before its first use, it is zero again when each call
+ * completes, and it must not be shared by calls that may run at the same time.
+ * A workspace smaller than w8_mm_i8_workspace_bytes() (or NULL) just disables
+ * stream-K.  Replaces the same reference call as w8_mm_i8 (npu_kernels.py:59-64). */
+int w8_mm_i8_ws(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
+                int32_t* c, int64_t ldc, int64_t m, int64_t n, int64_t k, void* workspace,
+                int64_t workspace_bytes, w8_stream_t stream);
+/* Bytes of workspace w8_mm_i8_ws can use for an M x N x K product (4 per tile). */
+int64_t w8_mm_i8_workspace_bytes(int64_t m, int64_t n, int64_t k);
+
 /* Y[M,N] (bf16) = bf16((float(A@B) * sx[m]) * sw[n]) with the dequant fused
  * into the GEMM epilogue.  Bit-identical to mm_i8 followed by _deq.
  * Replaces NPUGemm.matmul's launches + _dequant (gemma_npu.py:127-150).
