@@ -937,6 +937,58 @@ int gemm_device_status(int clear, int* out) {
 
 }  // namespace w8host
 
+// ---------------------------------------------------------------- allocation-free entry point
+// Scratch of w8_mm_i8_noalloc: the stream-K tile counters live in this library-owned
+// array instead of a caller workspace.  Every GPU that loads the library holds it
+// (64 KiB) until the process exits.  In host code the name is only a stand-in for the
+// device object: its device address comes from cudaGetSymbolAddress.
+namespace w8 {
+constexpr int64_t kNoAllocMaxTiles = 16384;
+static __device__ __align__(256) uint32_t g_noalloc_counters[kNoAllocMaxTiles];
+}  // namespace w8
+
+namespace w8host {
+// Device address of g_noalloc_counters, looked up once per device with that device current.
+static int noalloc_counters(int device, uint32_t** out) {
+  static std::mutex mu;
+  static uint32_t* ptr[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptr[device] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, w8::g_noalloc_counters);
+    if (e != cudaSuccess) return cuda_status(e);
+    ptr[device] = static_cast<uint32_t*>(p);
+  }
+  *out = ptr[device];
+  return W8_OK;
+}
+}  // namespace w8host
+
+extern "C" int w8_mm_i8_noalloc(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb,
+                                int b_layout, int32_t* c, int64_t ldc, int64_t m, int64_t n, int64_t k,
+                                w8_stream_t stream) {
+  W8_CHECK_ARG(m >= 0 && n >= 0 && k >= 0, "negative size (m=%lld n=%lld k=%lld)", (long long)m,
+               (long long)n, (long long)k);
+  if (m == 0 || n == 0) return W8_OK;
+  const int64_t tiles = ((m + w8::kBM - 1) / w8::kBM) * ((n + w8::kBN - 1) / w8::kBN);
+  W8_CHECK_ARG(tiles <= w8::kNoAllocMaxTiles,
+               "w8_mm_i8_noalloc: %lld x %lld needs %lld tile counters; its static scratch holds %lld "
+               "(M/128 * N/256 rounded up must be <= %lld); use w8_mm_i8_ws with a workspace",
+               (long long)m, (long long)n, (long long)tiles, (long long)w8::kNoAllocMaxTiles,
+               (long long)w8::kNoAllocMaxTiles);
+  int device = 0;
+  int st = w8host::require_sm100(&device);
+  if (st != W8_OK) return st;
+  uint32_t* counters = nullptr;
+  st = w8host::noalloc_counters(device, &counters);
+  if (st != W8_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // The array keeps whatever the last call left: start this call's counters at zero.
+  W8_CUDA_TRY(cudaMemsetAsync(counters, 0, static_cast<size_t>(tiles) * 4, s));
+  return w8host::gemm_common(a, lda, b, ldb, b_layout, c, ldc, 4, nullptr, nullptr, m, n, k, counters,
+                             tiles * 4, s, w8::kEpiI32);
+}
+
 extern "C" int64_t w8_mm_i8_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   (void)k;
   if (m <= 0 || n <= 0) return 0;

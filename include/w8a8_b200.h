@@ -79,6 +79,24 @@ int w8_mm_i8_ws(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int 
 /* Bytes of workspace w8_mm_i8_ws can use for an M x N x K product (4 per tile). */
 int64_t w8_mm_i8_workspace_bytes(int64_t m, int64_t n, int64_t k);
 
+/* w8_mm_i8_ws for callers that cannot allocate device memory.  It has no counterpart
+ * in the reference.  Some callers may not call cudaMalloc at all on their path: a
+ * plugin or operator run inside another framework's execute callback that owns the
+ * whole device-memory budget, a serving loop that must not synchronise the device
+ * (cudaMalloc and cudaFree can), or code with a fixed memory plan.  They pass only
+ * inputs and outputs; the stream-K tile counters live in a 64 KiB static device array
+ * inside this library, held by every GPU that loads it until the process exits.
+ * Limit: at most 16384 tile counters, i.e. ceil(M/128) * ceil(N/256) <= 16384
+ * (for example M = 4096 and N = 131072); larger products are rejected with
+ * W8_ERR_INVALID_ARG.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current), so make that first call before any
+ * stream capture.  Each call clears the counters it uses (an asynchronous memset on
+ * `stream`) and allocates nothing.  All calls share the one array: calls that can
+ * overlap on the GPU (other streams, other threads) race and must be serialised by the
+ * caller.  Same constraints and result bits as w8_mm_i8. */
+int w8_mm_i8_noalloc(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
+                     int32_t* c, int64_t ldc, int64_t m, int64_t n, int64_t k, w8_stream_t stream);
+
 /* Y[M,N] (bf16) = bf16((float(A@B) * sx[m]) * sw[n]) with the dequant fused
  * into the GEMM epilogue.  Bit-identical to mm_i8 followed by _deq.
  * Replaces NPUGemm.matmul's launches + _dequant (gemma_npu.py:127-150).
