@@ -40,9 +40,10 @@
 // B may be K-major ([N,K], the resident layout shared with the decode GEMV) or
 // MN-major ([K,N], the reference's mm_i8 layout); the instruction descriptor's B-major
 // bit and the shared-memory descriptor strides absorb the difference.  Tails in M, N
-// and K are handled by TMA zero fill (loads) and TMA clipping (stores).  No load uses
-// cluster multicast: every CTA issues its own TMA loads.  Every wait is bounded (see
-// common.cuh); all workers are co-resident, so a stream-K wait always ends.
+// and K are handled by TMA zero fill (loads) and TMA clipping (stores).  Every CTA
+// issues its own TMA loads into its own shared memory; no load is shared across the
+// cluster.  Every wait is bounded (see common.cuh); all workers are co-resident, so a
+// stream-K wait always ends.
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>

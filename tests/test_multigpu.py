@@ -1,8 +1,7 @@
 """The column-sharded LM head over NCCL on 2 GPUs equals the single-GPU head.
 
-One process per GPU; skipped with fewer than 2 sm_100 devices.  NVLS is off so the
-test uses plain NCCL rings (a rank that dies while bound to a multicast object is
-not a risk this test needs).
+One process per GPU; skipped with fewer than 2 sm_100 devices.  NCCL's in-switch
+reduction (NVLS) is off, so the test uses plain NCCL rings.
 """
 import os
 import socket
