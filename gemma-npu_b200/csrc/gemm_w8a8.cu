@@ -78,6 +78,7 @@ struct GemmArgs {
   int tma_out;       // the output tensor map is valid: epilogue stores go through TMA
   int stream_k;      // 1: stream-K schedule (int32 + TMA output + flags only)
   uint32_t* flags;   // stream-K: one zero-initialised counter per tile
+  int bn;            // output columns per tile: 256, or 192 on CTA pairs when it balances waves
 };
 
 constexpr int kEpiBufBytes = 32 * 128;  // one 32-row x 128-byte store box
@@ -217,7 +218,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmArgs& args, const CUtens
                                               uint32_t taddr, int row0, int col_base, float sxr,
                                               uint32_t stage_base, uint32_t& sbuf, int lane,
                                               bool reduce, Release release) {
-  const int n_cols = min(kBN, args.n - col_base);  // columns of this tile inside N
+  const int n_cols = min(args.bn, args.n - col_base);  // columns of this tile inside N
   const int row = row0 + lane;
   if (args.tma_out) {
     // One store box = 32 rows x 128 bytes: 32 int32 or 64 bf16 columns.
@@ -309,12 +310,14 @@ __device__ __forceinline__ void epilogue_segment(const GemmArgs& args, const CUt
 }
 
 // =====================================================================================
-// 256 x 256 tiles on a CTA pair (tcgen05 cta_group::2)
+// 256 x BN tiles on a CTA pair (tcgen05 cta_group::2); BN = 256 or 192 (args.bn == BN).
+// BN is a template parameter so the MMA instruction descriptor is a compile-time constant.
 // =====================================================================================
-template <bool B_MN, int EPI>
+template <bool B_MN, int EPI, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                      const __grid_constant__ CUtensorMap tm_c, const GemmArgs args) {
+  static_assert(BN % 64 == 0 && BN <= kBN, "tile width must be a multiple of 64 up to 256");
   using L = PairSmem;
   constexpr int STAGES = kPairStages;
   extern __shared__ uint8_t smem_raw[];
@@ -368,6 +371,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer (both CTAs): this CTA's A rows and B columns
+      // Bytes both CTAs land on the leader's full barrier per stage: A halves + B halves.
+      constexpr uint32_t stage_tx = 2u * (L::kA + (BN / 2) * kBK);
       Schedule sched(args, worker, workers);
       Segment sg;
       int stage = 0;
@@ -377,7 +382,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int mb = sg.tile % args.m_tiles;
         const int nb = sg.tile / args.m_tiles;
         const int a_row = mb * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int b_col = nb * kBN + static_cast<int>(rank) * 128;
+        const int b_col = nb * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, &g_gemm_status)) {
             ok = false;
@@ -386,7 +391,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t sa = base + stage * L::kStage;
           const uint32_t sb = sa + L::kA;
           const uint32_t fb = mapa_shared(full_bar(stage), 0);  // the leader's full barrier
-          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * L::kStage);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), stage_tx);
           tma_load_2d_pair(sa, &tm_a, fb, kb * kBK, a_row);
           if constexpr (B_MN)
             tma_load_2d_pair(sb, &tm_b, fb, b_col, kb * kBK);
@@ -405,7 +410,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (rank == 0 && lane == 0) {
       // ---------------- MMA issuer (leader CTA only)
-      constexpr uint32_t idesc = idesc_i8(2 * kBM, kBN, B_MN);
+      constexpr uint32_t idesc = idesc_i8(2 * kBM, BN, B_MN);
       const uint32_t empty_peer0 = mapa_shared(empty_bar(0), peer);
       const uint32_t tfull_peer0 = mapa_shared(tfull_bar(0), peer);
       Schedule sched(args, worker, workers);
@@ -478,7 +483,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       float sxr = 0.f;
       if constexpr (EPI == kEpiBf16) sxr = row0 + lane < args.m ? __ldg(args.sx + row0 + lane) : 0.f;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
-      epilogue_segment<EPI>(args, &tm_c, sg, taddr, row0, nb * kBN, sxr, stage_base, sbuf, lane,
+      epilogue_segment<EPI>(args, &tm_c, sg, taddr, row0, nb * args.bn, sxr, stage_base, sbuf, lane,
                             2 * kEpiWarps, [&] { mbar_arrive_cluster(tempty_leader0 + 8u * acc); });
     }
     if (lane == 0) bulk_wait_group<0>();  // every store of this warp has landed
@@ -736,9 +741,9 @@ static int set_smem_once(int device, Kernel kern, int bytes, bool* done) {
 
 // Co-resident CTA pairs of the pair kernel on this device (a GPC with an odd number of
 // SMs leaves one idle), cached per device.
-template <bool B_MN, int EPI>
+template <bool B_MN, int EPI, int BN>
 static int pair_capacity(int device, int* out) {
-  auto kern = w8::gemm_pair_kernel<B_MN, EPI>;
+  auto kern = w8::gemm_pair_kernel<B_MN, EPI, BN>;
   static bool done[64] = {};
   static int cap[64] = {};
   int st = set_smem_once(device, kern, w8::PairSmem::kAlloc, done);
@@ -793,12 +798,12 @@ static bool want_stream_k(int64_t tiles, int workers, int k_blocks) {
   return tiles * 100 < waves * workers * 90;  // whole-tile efficiency below 90 %
 }
 
-template <bool B_MN, int EPI>
+template <bool B_MN, int EPI, int BN>
 static int launch_pair(int device, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                        w8::GemmArgs args, int64_t flag_words, cudaStream_t stream) {
-  auto kern = w8::gemm_pair_kernel<B_MN, EPI>;
+  auto kern = w8::gemm_pair_kernel<B_MN, EPI, BN>;
   int cap = 0;
-  int st = pair_capacity<B_MN, EPI>(device, &cap);
+  int st = pair_capacity<B_MN, EPI, BN>(device, &cap);
   if (st != W8_OK) return st;
   const int64_t tiles = static_cast<int64_t>(args.m_tiles) * args.n_tiles;
   int workers = static_cast<int>(tiles < cap ? tiles : cap);
@@ -869,7 +874,21 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
 
   const bool pair = m > w8::kBM;            // 256-row tiles on CTA pairs
   const int rows_per_tile = pair ? 2 * w8::kBM : w8::kBM;
-  const uint32_t b_box_n = pair ? 128 : w8::kBN;  // B columns one CTA stages per K-block
+  // Tile width: on CTA pairs over a K-major B, 192 columns when that fills the last wave
+  // enough to pay for narrower tiles (measured: a 192-wide tile costs ~1.28x per column
+  // of a 256-wide one), e.g. N = 2560 (qkv) and N = 1536 (o) at M = 3658.  Shapes that
+  // stream-K will balance keep 256.
+  int bn = w8::kBN;
+  const int64_t k_blocks = (k + w8::kBK - 1) / w8::kBK;
+  if (pair && b_layout == W8_B_NK && !(epi == w8::kEpiI32 && workspace != nullptr && k_blocks >= 24)) {
+    int cap = 0;
+    st = pair_capacity<false, w8::kEpiI32, w8::kBN>(device, &cap);
+    if (st != W8_OK) return st;
+    const int64_t m_tiles = (m + rows_per_tile - 1) / rows_per_tile;
+    auto waves = [&](int64_t w) { return (m_tiles * ((n + w - 1) / w) + cap - 1) / cap; };
+    if (waves(192) * 192 * 128 < waves(256) * 256 * 100) bn = 192;
+  }
+  const uint32_t b_box_n = pair ? bn / 2 : w8::kBN;  // B columns one CTA stages per K-block
   CUtensorMap ta, tb, tc;
   st = encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, m, lda, w8::kBK, w8::kBM);
   if (st != W8_OK) return st;
@@ -884,7 +903,8 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   args.n = static_cast<int>(n);
   args.k = static_cast<int>(k);
   args.m_tiles = static_cast<int>((m + rows_per_tile - 1) / rows_per_tile);
-  args.n_tiles = static_cast<int>((n + w8::kBN - 1) / w8::kBN);
+  args.n_tiles = static_cast<int>((n + bn - 1) / bn);
+  args.bn = bn;
   args.k_blocks = static_cast<int>((k + w8::kBK - 1) / w8::kBK);
   args.out = out;
   args.ldo = ldo;
@@ -911,10 +931,12 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   const bool i32 = epi == w8::kEpiI32;
   if (pair) {
     if (i32)
-      return mn ? launch_pair<true, w8::kEpiI32>(device, ta, tb, tc, args, flag_words, stream)
-                : launch_pair<false, w8::kEpiI32>(device, ta, tb, tc, args, flag_words, stream);
-    return mn ? launch_pair<true, w8::kEpiBf16>(device, ta, tb, tc, args, flag_words, stream)
-              : launch_pair<false, w8::kEpiBf16>(device, ta, tb, tc, args, flag_words, stream);
+      return mn ? launch_pair<true, w8::kEpiI32, 256>(device, ta, tb, tc, args, flag_words, stream)
+                : bn == 192 ? launch_pair<false, w8::kEpiI32, 192>(device, ta, tb, tc, args, flag_words, stream)
+                            : launch_pair<false, w8::kEpiI32, 256>(device, ta, tb, tc, args, flag_words, stream);
+    return mn ? launch_pair<true, w8::kEpiBf16, 256>(device, ta, tb, tc, args, flag_words, stream)
+              : bn == 192 ? launch_pair<false, w8::kEpiBf16, 192>(device, ta, tb, tc, args, flag_words, stream)
+                          : launch_pair<false, w8::kEpiBf16, 256>(device, ta, tb, tc, args, flag_words, stream);
   }
   if (i32)
     return mn ? launch_single<true, w8::kEpiI32>(device, ta, tb, tc, args, flag_words, stream)
@@ -993,8 +1015,10 @@ extern "C" int w8_mm_i8_noalloc(const int8_t* a, int64_t lda, const int8_t* b, i
 extern "C" int64_t w8_mm_i8_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   (void)k;
   if (m <= 0 || n <= 0) return 0;
-  // One 32-bit counter per output tile of the smaller (128 x 256) tiling.
-  return 4 * ((m + w8::kBM - 1) / w8::kBM) * ((n + w8::kBN - 1) / w8::kBN);
+  // One 32-bit counter per output tile of whichever tiling the launch picks.
+  const int64_t single = ((m + w8::kBM - 1) / w8::kBM) * ((n + w8::kBN - 1) / w8::kBN);
+  const int64_t pair192 = ((m + 2 * w8::kBM - 1) / (2 * w8::kBM)) * ((n + 191) / 192);
+  return 4 * (single > pair192 ? single : pair192);
 }
 
 extern "C" int w8_mm_i8(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
