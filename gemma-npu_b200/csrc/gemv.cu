@@ -10,9 +10,14 @@
 // loads, coalesced across the warp.  The activation row is converted to fp32 once per
 // thread and kept in registers: lane l of the warp owning K-slice `sl` multiplies the
 // 16 consecutive k of chunk c, k = ((sl*J + c)*32 + l)*16 .. +15, of every weight row it
-// visits.  S warps ("a team") split K; the team's partial sums meet in shared memory.
+// visits.  S warps ("a team") split K; the team's partial sums meet in shared memory,
+// and lane r of the team's first warp finishes row r (scale, bf16, softcap, store).
 // int8 -> fp32 uses the exponent trick: byte b (offset to b+128) is placed in the
-// mantissa of 2^23 with one PRMT and the bias removed with one FADD, exactly.
+// mantissa of 2^23 with one PRMT and the bias removed exactly; the bias subtraction and
+// the multiply-add use sm_100's packed f32x2 instructions (two bytes per instruction),
+// which keeps the kernel off the issue limit at full HBM rate.
+// Weight loads of the first row batch are issued before waiting for the previous kernel
+// of the stream (programmatic dependent launch): only the activation row depends on it.
 #include "common.cuh"
 
 namespace w8 {
@@ -28,19 +33,37 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   return v;
 }
 
-// acc += sum over the 4 signed bytes of `word` times x[0..3].
-__device__ __forceinline__ float dot4_i8(uint32_t word, const float* x, float acc) {
-  const uint32_t u = word ^ 0x80808080u;  // b + 128 in each byte
-  constexpr float kBias = 8388736.0f;     // 2^23 + 128
-  const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - kBias;
-  const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - kBias;
-  const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - kBias;
-  const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - kBias;
-  acc = fmaf(f0, x[0], acc);
-  acc = fmaf(f1, x[1], acc);
-  acc = fmaf(f2, x[2], acc);
-  acc = fmaf(f3, x[3], acc);
-  return acc;
+// Two fp32 values in one 64-bit register pair, for sm_100's packed f32x2 instructions.
+__device__ __forceinline__ uint64_t pack_f32x2(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ float sum_f32x2(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
+}
+
+// (acc0, acc1) += the 16 signed bytes of `w` times x (8 packed pairs of fp32).
+// Byte b, offset to u = b + 128, is placed in the mantissa of 2^23 with one PRMT
+// (2^23 + u, exact); one packed add of -(2^23 + 128) per two bytes leaves b exactly,
+// and one packed FMA per two bytes accumulates: 9 instructions per 4 bytes.
+__device__ __forceinline__ void dot16_i8(const uint4& w, const uint64_t (&xp)[8], uint64_t& acc0,
+                                         uint64_t& acc1) {
+  const uint64_t neg_bias = pack_f32x2(0xCB000080u, 0xCB000080u);  // -(2^23 + 128) twice
+  const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t u = words[j] ^ 0x80808080u;
+    const uint64_t f01 = pack_f32x2(__byte_perm(u, 0x4B000000u, 0x7540), __byte_perm(u, 0x4B000000u, 0x7541));
+    const uint64_t f23 = pack_f32x2(__byte_perm(u, 0x4B000000u, 0x7542), __byte_perm(u, 0x4B000000u, 0x7543));
+    uint64_t d01, d23;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d01) : "l"(f01), "l"(neg_bias));
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d23) : "l"(f23), "l"(neg_bias));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc0) : "l"(d01), "l"(xp[2 * j]));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc1) : "l"(d23), "l"(xp[2 * j + 1]));
+  }
 }
 
 // Output of one row: bf16 of the scaled sum, optionally softcapped to fp32.
@@ -92,8 +115,8 @@ __global__ void __launch_bounds__(kGemvThreads)
   pdl_wait();
 
   for (int t = 0; t < t_count; ++t) {
-    // This lane's slice of the activation row, in fp32.
-    float xr[J][16];
+    // This lane's slice of the activation row, in fp32 pairs (bf16 -> fp32 is exact).
+    uint64_t xp[J][8];
 #pragma unroll
     for (int c = 0; c < J; ++c) {
       const int k0 = ((sl * J + c) * 32 + lane) * 16;
@@ -102,13 +125,10 @@ __global__ void __launch_bounds__(kGemvThreads)
         const uint4 a = __ldg(p), b = __ldg(p + 1);
         const uint32_t words[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          xr[c][2 * i] = __uint_as_float(words[i] << 16);
-          xr[c][2 * i + 1] = __uint_as_float(words[i] & 0xFFFF0000u);
-        }
+        for (int i = 0; i < 8; ++i) xp[c][i] = pack_f32x2(words[i] << 16, words[i] & 0xFFFF0000u);
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) xr[c][i] = 0.f;
+        for (int i = 0; i < 8; ++i) xp[c][i] = 0ull;
       }
     }
 
@@ -117,28 +137,23 @@ __global__ void __launch_bounds__(kGemvThreads)
       float acc[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        float a0 = 0.f, a1 = 0.f;
+        uint64_t a0 = 0ull, a1 = 0ull;
 #pragma unroll
-        for (int c = 0; c < J; ++c) {
-          a0 = dot4_i8(wv[r][c].x, &xr[c][0], a0);
-          a1 = dot4_i8(wv[r][c].y, &xr[c][4], a1);
-          a0 = dot4_i8(wv[r][c].z, &xr[c][8], a0);
-          a1 = dot4_i8(wv[r][c].w, &xr[c][12], a1);
-        }
-        acc[r] = a0 + a1;
+        for (int c = 0; c < J; ++c) dot16_i8(wv[r][c], xp[c], a0, a1);
+        acc[r] = sum_f32x2(a0) + sum_f32x2(a1);
       }
 #pragma unroll
       for (int r = 0; r < R; ++r)
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
 
+      // Lane r finishes row n0 + r (scale, bf16 rounding, softcap, store), in parallel.
       if constexpr (S == 1) {
-        if (lane == 0) {
+        float v = acc[0];
 #pragma unroll
-          for (int r = 0; r < R; ++r)
-            if (n0 + r < n)
-              write_out<LOGITS>(y, static_cast<int64_t>(t) * ldy + n0 + r, acc[r], s[n0 + r], cap);
-        }
+        for (int r = 1; r < R; ++r) v = lane == r ? acc[r] : v;  // every lane holds every sum
+        if (lane < R && n0 + lane < n)
+          write_out<LOGITS>(y, static_cast<int64_t>(t) * ldy + n0 + lane, v, s[n0 + lane], cap);
       } else {
         if (lane == 0) {
 #pragma unroll
@@ -146,15 +161,11 @@ __global__ void __launch_bounds__(kGemvThreads)
         }
         // Team barrier: the S warps of this team only.
         asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");
-        if (sl == 0 && lane == 0) {
+        if (sl == 0 && lane < R && n0 + lane < n) {
+          float v = red[team][0][lane];
 #pragma unroll
-          for (int r = 0; r < R; ++r) {
-            float v = red[team][0][r];
-#pragma unroll
-            for (int q = 1; q < S; ++q) v += red[team][q][r];
-            if (n0 + r < n)
-              write_out<LOGITS>(y, static_cast<int64_t>(t) * ldy + n0 + r, v, s[n0 + r], cap);
-          }
+          for (int q = 1; q < S; ++q) v += red[team][q][lane];
+          write_out<LOGITS>(y, static_cast<int64_t>(t) * ldy + n0 + lane, v, s[n0 + lane], cap);
         }
         asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");
       }
@@ -221,17 +232,27 @@ static int gemv_dispatch(const uint16_t* xh, int64_t ldx, const int8_t* w, int64
   const auto* x = reinterpret_cast<const __nv_bfloat16*>(xh);
   const auto* s = reinterpret_cast<const __nv_bfloat16*>(sh);
   const int ti = static_cast<int>(t), ni = static_cast<int>(n), ki = static_cast<int>(k);
+  int sms = 0;
+  const int st2 = num_sms(&sms);
+  if (st2 != W8_OK) return st2;
   // Smallest (S, J) whose slice covers K: x stays within 64 fp32 registers per lane.
-  if (k <= 512) return launch_gemv<1, 1, 4, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
-  if (k <= 1024) return launch_gemv<2, 1, 4, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
-  if (k <= 1536) return launch_gemv<3, 1, 4, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
-  if (k <= 2048) return launch_gemv<4, 1, 2, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
-  if (k <= 3072) return launch_gemv<3, 2, 4, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
-  if (k <= 4096) return launch_gemv<4, 2, 2, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
-  if (k <= 6144) return launch_gemv<3, 4, 4, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
-  if (k <= 8192) return launch_gemv<4, 4, 2, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
-  if (k <= 12288) return launch_gemv<3, 8, 4, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
-  return launch_gemv<4, 8, 2, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream);
+  // R rows per team per step: the large R keeps more weight bytes in flight per warp;
+  // a matrix too short to give two CTAs per SM at that R takes one row per team.
+#define W8_GEMV(J, S, R)                                                                      \
+  return n < 2 * sms * (w8::kGemvWarps / (S)) * (R)                                            \
+             ? launch_gemv<J, S, 1, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream) \
+             : launch_gemv<J, S, R, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream)
+  if (k <= 512) W8_GEMV(1, 1, 4);
+  if (k <= 1024) W8_GEMV(2, 1, 4);
+  if (k <= 1536) W8_GEMV(3, 1, 4);
+  if (k <= 2048) W8_GEMV(4, 1, 2);
+  if (k <= 3072) W8_GEMV(3, 2, 4);
+  if (k <= 4096) W8_GEMV(4, 2, 2);
+  if (k <= 6144) W8_GEMV(3, 4, 4);
+  if (k <= 8192) W8_GEMV(4, 4, 2);
+  if (k <= 12288) W8_GEMV(3, 8, 4);
+  W8_GEMV(4, 8, 2);
+#undef W8_GEMV
 }
 
 }  // namespace w8host
