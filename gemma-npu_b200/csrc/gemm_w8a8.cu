@@ -97,9 +97,15 @@ struct Smem {
   static_assert(kStage % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(kAlloc <= 232448, "shared memory budget of one CTA exceeded");
 };
-constexpr int kPairStages = 6;
+// CTA pairs stage 256 K bytes at a time (two swizzle chunks per copy): the TMA engine of
+// an SM moves large boxes far faster than small ones (measured on B200 with one CTA per
+// SM streaming from L2: 28 B/clk with 16 KB boxes, 56 B/clk with 32 KB boxes), and the
+// MMAs of a 128-row CTA consume about 50 B/clk at full rate.
+constexpr int kPairBK = 256;
+constexpr int kPairChunks = kPairBK / kBK;
+constexpr int kPairStages = 3;
 constexpr int kSingleStages = 4;
-using PairSmem = Smem<kPairStages, kBM * kBK, 128 * kBK>;     // A half + B half per CTA
+using PairSmem = Smem<kPairStages, kBM * kPairBK, 128 * kPairBK>;  // A half + B half per CTA
 using SingleSmem = Smem<kSingleStages, kBM * kBK, kBN * kBK>;  // A + whole B tile
 
 // ---------------------------------------------------------------- schedule
@@ -372,7 +378,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---------------- TMA producer (both CTAs): this CTA's A rows and B columns
       // Bytes both CTAs land on the leader's full barrier per stage: A halves + B halves.
-      constexpr uint32_t stage_tx = 2u * (L::kA + (BN / 2) * kBK);
+      constexpr uint32_t stage_tx = 2u * (L::kA + (BN / 2) * kPairBK);
       Schedule sched(args, worker, workers);
       Segment sg;
       int stage = 0;
@@ -392,11 +398,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t sb = sa + L::kA;
           const uint32_t fb = mapa_shared(full_bar(stage), 0);  // the leader's full barrier
           if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), stage_tx);
-          tma_load_2d_pair(sa, &tm_a, fb, kb * kBK, a_row);
+          tma_load_3d_pair(sa, &tm_a, fb, 0, a_row, kb * kPairChunks);
           if constexpr (B_MN)
-            tma_load_2d_pair(sb, &tm_b, fb, b_col, kb * kBK);
+            tma_load_2d_pair(sb, &tm_b, fb, b_col, kb * kPairBK);
           else
-            tma_load_2d_pair(sb, &tm_b, fb, kb * kBK, b_col);
+            tma_load_3d_pair(sb, &tm_b, fb, 0, b_col, kb * kPairChunks);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -411,6 +417,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (rank == 0 && lane == 0) {
       // ---------------- MMA issuer (leader CTA only)
       constexpr uint32_t idesc = idesc_i8(2 * kBM, BN, B_MN);
+      const int k_chunks = args.k / kBK;  // K is a multiple of 128 on CTA pairs
       const uint32_t empty_peer0 = mapa_shared(empty_bar(0), peer);
       const uint32_t tfull_peer0 = mapa_shared(tfull_bar(0), peer);
       Schedule sched(args, worker, workers);
@@ -436,11 +443,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t sa = base + stage * L::kStage;
           const uint32_t sb = sa + L::kA;
+          // The second chunk of the last stage may lie beyond K (odd K / 128): skip it.
+          const int chunks = min(kPairChunks, k_chunks - kb * kPairChunks);
 #pragma unroll
-          for (int k = 0; k < kBK / kUmmaK; ++k) {
-            const uint64_t ad = smem_desc_sw128(sa + k * kUmmaK, 16, 1024);
-            const uint64_t bd = B_MN ? smem_desc_sw128(sb + k * kUmmaK * 128, 128 * kBK, 1024)
-                                     : smem_desc_sw128(sb + k * kUmmaK, 16, 1024);
+          for (int k = 0; k < kPairBK / kUmmaK; ++k) {
+            constexpr int kPerChunk = kBK / kUmmaK;
+            const int c = k / kPerChunk, j = k % kPerChunk;
+            if (c >= chunks) break;
+            const uint64_t ad = smem_desc_sw128(sa + c * (kBM * kBK) + j * kUmmaK, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(sb + k * kUmmaK * 128, 128 * kPairBK, 1024)
+                                     : smem_desc_sw128(sb + c * ((BN / 2) * kBK) + j * kUmmaK, 16, 1024);
             mma_i8_pair(d, ad, bd, idesc, (kb > sg.kb0 || k > 0) ? 1u : 0u);
           }
           issued = true;
@@ -727,6 +739,33 @@ static int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* pt
   return W8_OK;
 }
 
+// A K-major int8 operand [rows, K] (K % 128 == 0) viewed in 3-D as (128-byte chunk,
+// row, chunk index): a box of {128, box_rows, kPairChunks} lands in shared memory as
+// kPairChunks consecutive swizzle-128 blocks of box_rows rows each.
+static int encode_kchunks(CUtensorMap* map, const void* ptr, int64_t k, int64_t rows, int64_t pitch,
+                          uint32_t box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return W8_ERR_CUDA;
+  }
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(w8::kBK), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(k / w8::kBK)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(pitch), static_cast<cuuint64_t>(w8::kBK)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(w8::kBK), box_rows, static_cast<cuuint32_t>(w8::kPairChunks)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (3-D) failed with CUresult %d (k %lld, rows %lld, pitch %lld)",
+              static_cast<int>(r), static_cast<long long>(k), static_cast<long long>(rows),
+              static_cast<long long>(pitch));
+    return W8_ERR_CUDA;
+  }
+  return W8_OK;
+}
+
 int require_sm100(int* device);
 
 template <typename Kernel>
@@ -792,8 +831,8 @@ static int launch_pdl(Kernel kern, int grid, int smem, cudaStream_t stream, cons
 
 // Stream-K pays off when whole tiles would leave the last wave of workers mostly idle
 // and each tile is long enough (K) that splitting it costs little next to its MMAs.
-static bool want_stream_k(int64_t tiles, int workers, int k_blocks) {
-  if (k_blocks < 24) return false;
+static bool want_stream_k(int64_t tiles, int workers, int k) {
+  if (k < 24 * w8::kBK) return false;
   const int64_t waves = (tiles + workers - 1) / workers;
   return tiles * 100 < waves * workers * 90;  // whole-tile efficiency below 90 %
 }
@@ -809,7 +848,7 @@ static int launch_pair(int device, const CUtensorMap& ta, const CUtensorMap& tb,
   int workers = static_cast<int>(tiles < cap ? tiles : cap);
   args.stream_k = 0;
   if (EPI == w8::kEpiI32 && args.tma_out && args.flags != nullptr && flag_words >= tiles &&
-      want_stream_k(tiles, cap, args.k_blocks)) {
+      want_stream_k(tiles, cap, args.k)) {
     const int64_t units = tiles * args.k_blocks;
     workers = static_cast<int>(units < cap ? units : cap);
     args.stream_k = 1;
@@ -831,7 +870,7 @@ static int launch_single(int device, const CUtensorMap& ta, const CUtensorMap& t
   int workers = static_cast<int>(tiles < sms ? tiles : sms);
   args.stream_k = 0;
   if (EPI == w8::kEpiI32 && args.tma_out && args.flags != nullptr && flag_words >= tiles &&
-      want_stream_k(tiles, sms, args.k_blocks)) {
+      want_stream_k(tiles, sms, args.k)) {
     const int64_t units = tiles * args.k_blocks;
     workers = static_cast<int>(units < sms ? units : sms);
     args.stream_k = 1;
@@ -872,15 +911,16 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   else
     W8_CHECK_ARG(ldb >= k, "ldb %lld < k %lld for an [N,K] B", (long long)ldb, (long long)k);
 
-  const bool pair = m > w8::kBM;            // 256-row tiles on CTA pairs
+  // 256-row tiles on CTA pairs; their operand copies cover two 128-byte K chunks, which
+  // needs K to be a multiple of 128.  Otherwise one CTA per 128 x 256 tile.
+  const bool pair = m > w8::kBM && k % w8::kBK == 0;
   const int rows_per_tile = pair ? 2 * w8::kBM : w8::kBM;
   // Tile width: on CTA pairs over a K-major B, 192 columns when that fills the last wave
   // enough to pay for narrower tiles (measured: a 192-wide tile costs ~1.28x per column
   // of a 256-wide one), e.g. N = 2560 (qkv) and N = 1536 (o) at M = 3658.  Shapes that
   // stream-K will balance keep 256.
   int bn = w8::kBN;
-  const int64_t k_blocks = (k + w8::kBK - 1) / w8::kBK;
-  if (pair && b_layout == W8_B_NK && !(epi == w8::kEpiI32 && workspace != nullptr && k_blocks >= 24)) {
+  if (pair && b_layout == W8_B_NK && !(epi == w8::kEpiI32 && workspace != nullptr && k >= 24 * w8::kBK)) {
     int cap = 0;
     st = pair_capacity<false, w8::kEpiI32, w8::kBN>(device, &cap);
     if (st != W8_OK) return st;
@@ -890,12 +930,18 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   }
   const uint32_t b_box_n = pair ? bn / 2 : w8::kBN;  // B columns one CTA stages per K-block
   CUtensorMap ta, tb, tc;
-  st = encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, m, lda, w8::kBK, w8::kBM);
+  const int stage_k = pair ? w8::kPairBK : w8::kBK;  // K bytes per pipeline stage
+  if (pair)
+    st = encode_kchunks(&ta, a, k, m, lda, w8::kBM);
+  else
+    st = encode_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, m, lda, w8::kBK, w8::kBM);
   if (st != W8_OK) return st;
-  if (b_layout == W8_B_NK)
+  if (b_layout == W8_B_NK && pair)
+    st = encode_kchunks(&tb, b, k, n, ldb, b_box_n);
+  else if (b_layout == W8_B_NK)
     st = encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, k, n, ldb, w8::kBK, b_box_n);
   else
-    st = encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, n, k, ldb, 128, w8::kBK);
+    st = encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, n, k, ldb, 128, stage_k);
   if (st != W8_OK) return st;
 
   w8::GemmArgs args;
@@ -905,7 +951,7 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   args.m_tiles = static_cast<int>((m + rows_per_tile - 1) / rows_per_tile);
   args.n_tiles = static_cast<int>((n + bn - 1) / bn);
   args.bn = bn;
-  args.k_blocks = static_cast<int>((k + w8::kBK - 1) / w8::kBK);
+  args.k_blocks = static_cast<int>((k + stage_k - 1) / stage_k);
   args.out = out;
   args.ldo = ldo;
   args.sx = sx;
