@@ -270,6 +270,85 @@ def build_decode(w8, work, dev):
     return step, nbytes, len(chain) + 1, head
 
 
+def prompt_lengths(count=8, seed=0, lo=200, hi=3700):
+    """Config 4: prompt lengths uniform in [lo, hi], seeded."""
+    g = torch.Generator().manual_seed(seed)
+    return [int(v) for v in torch.randint(lo, hi + 1, (count,), generator=g)]
+
+
+def prompts_dp(w8, dev, stream, world, rank, steps, warmup):
+    """Config 4: 8 independent prompts, prompt i on rank i % world, each running the 35-layer
+    prefill linear set at its own length; aggregate TOPS over the max-over-ranks time."""
+    lengths = prompt_lengths()
+    mine = [m for i, m in enumerate(lengths) if i % world == rank]
+    work = build_prefill(w8, dev, max(lengths), seed=100 + rank)
+    graphs, ops_all = [], sum(2 * m * macs_per_token() for m in lengths)
+    for m in mine:
+        calls = [(xq[:m], wq, c[:m]) for xq, wq, c, _ in work["calls"]]
+
+        def step(calls=calls):
+            for xq, wq, c in calls:
+                w8.mm_i8_nk(xq, wq, c)
+
+        graphs.append(capture(step, stream))
+
+    def replay():
+        for gr in graphs:
+            gr.replay()
+
+    ms = timed(replay, steps, warmup, stream, world) / steps
+    del graphs
+    return {"workload": "config 4: 8 prompts, lengths uniform in [200, 3700] (seed 0), prompt i on rank i % N, "
+                        "35-layer prefill linear set each", "lengths": lengths,
+            "value": ops_all / (ms * 1e-3) / 1e12, "unit": "TOPS", "ms_per_pass": ms, "steps": steps}
+
+
+def sharded_head(w8, dev, stream, world, steps, warmup, pk):
+    """Config 4: the 262144-wide LM head column-sharded over the N ranks (local int8 GEMV
+    with the softcap + NCCL all-gather of the fp32 logits), time per token, max over ranks."""
+    g = torch.Generator(device=dev).manual_seed(77)
+    weight = torch.randn((VOCAB, HIDDEN), device=dev, generator=g, dtype=torch.bfloat16) * 0.02
+    head = w8.ShardedInt8Head(weight, device=dev, cap=SOFTCAP)
+    del weight
+    h = torch.randn((HIDDEN,), device=dev, generator=g).to(torch.bfloat16)
+    ms = timed(lambda: head(h), steps, warmup, stream, world) / steps
+    shard_bytes = (head.r1 - head.r0) * (HIDDEN + 2)
+    return {"workload": f"config 4: LM head {VOCAB}x{HIDDEN} int8 split by rows over {world} GPU(s), "
+                        "fused softcap, NCCL all-gather of fp32 logits" + (" (no collective at N=1)" if world == 1 else ""),
+            "us_per_token": ms * 1e3, "shard_rows": head.r1 - head.r0,
+            "local_gemv_gbs": shard_bytes / (ms * 1e-3) / 1e9, "allgather_bytes": 4 * world * head.per,
+            "steps": steps}
+
+
+def sweep(w8, dev, stream, steps, warmup):
+    """Config 3: each projection shape over 35 layers at M in {207, 858, 1878, 3658}, with
+    and without the reference's 512-row padding (TOPS on the unpadded rows)."""
+    out = {}
+    for m in (207, 858, 1878, 3658):
+        mp = -(-m // 512) * 512
+        work = build_prefill(w8, dev, mp)
+        row = {}
+        for name, n, k in LAYER_SHAPES + [PLE_SHAPE]:
+            calls = [(xq, wq, c) for xq, wq, c, nm in work["calls"] if nm == name]
+            res = {}
+            for label, rows in (("unpadded", m), ("padded", mp)):
+                cs = [(xq[:rows], wq, c[:rows]) for xq, wq, c in calls]
+
+                def step(cs=cs):
+                    for xq, wq, c in cs:
+                        w8.mm_i8_nk(xq, wq, c)
+
+                gr = capture(step, stream)
+                ms = timed(lambda: gr.replay(), steps, warmup, stream, 1) / steps
+                del gr
+                res[label] = {"us_per_gemm": ms * 1e3 / len(cs),
+                              "tops": 2 * m * n * k * len(cs) / (ms * 1e-3) / 1e12}
+            row[name] = res
+        out[str(m)] = row
+        del work
+    return out
+
+
 # ----------------------------------------------------------------------------- CPU reference
 def cpu_reference_step(m, layers, seed=0):
     """The reference's cpu-int8 prefill GEMMs (torch._int_mm) over `layers` layers; returns ops."""
@@ -367,6 +446,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-step-s", type=float, default=4.0, help="CPU seconds per reference-arm step")
+    ap.add_argument("--sweep", action="store_true", help="config 3: per-shape M sweep, padded vs unpadded (own JSON line)")
+    ap.add_argument("--no-config4", action="store_true", help="skip the config-4 prompts / sharded LM head objects")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -388,8 +469,15 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     try:
         pk = peaks()
-        work = build_prefill(w8, dev, args.m, only=args.only, seed=rank, layers=args.layers)
         stream = torch.cuda.Stream(device=dev)
+        if args.sweep:
+            table = sweep(w8, dev, stream, args.steps, args.warmup)
+            if rank == 0:
+                print(json.dumps({"metric": "W8A8 GEMM TOPS sweep (config 3)", "unit": "TOPS", "n_gpus": 1,
+                                  "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                                  "dtype": "int8", "data": "synthetic", "sweep": table}), flush=True)
+            return
+        work = build_prefill(w8, dev, args.m, only=args.only, seed=rank, layers=args.layers)
 
         def prefill_step():
             for xq, wq, c, _ in work["calls"]:
@@ -438,19 +526,32 @@ def main():
                            "steps": args.e2e_steps,
                            "path": "gemma_npu_b200.mm_i8_nk per GEMM: pinned int8 activations H2D, int32 results D2H"}
         if not args.no_decode and args.only is None:
-            step, nbytes, launches, _ = build_decode(w8, work, dev)
+            step, nbytes, launches, head = build_decode(w8, work, dev)
             dgraph = capture(step, stream)
             dms = timed(lambda: dgraph.replay(), args.decode_steps, args.warmup, stream, world)
             per = dms / args.decode_steps
             gbs = nbytes / (per * 1e-3) / 1e9
+            del dgraph
+            hx, hq, hsc, hlog = head
+            hgraph = capture(lambda: w8.lm_head_logits(hx, hq, hsc, SOFTCAP, out=hlog), stream)
+            hms = timed(lambda: hgraph.replay(), args.decode_steps, args.warmup, stream, world) / args.decode_steps
+            del hgraph
+            head_bytes = VOCAB * HIDDEN + 2 * VOCAB + 2 * HIDDEN + 4 * VOCAB
+            head_gbs = head_bytes / (hms * 1e-3) / 1e9
             line["decode_gemv"] = {
                 "metric": "int8 GEMV GB/s, decode chain (config 2: 140 layer GEMVs + LM head 262144x1536, softcap)",
                 "value": world * gbs, "unit": "GB/s", "ms_per_token": per, "bytes_per_token": nbytes,
                 "launches_per_token": launches,
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                              "frac": gbs / pk["hbm_gbs"], "traffic": None,
-                             "peak_note": f"{pk['source']} HBM copy bandwidth"}}
-            del dgraph
+                             "peak_note": f"{pk['source']} HBM copy bandwidth"},
+                "lm_head": {"us": hms * 1e3, "bytes": head_bytes, "gbs": head_gbs,
+                            "frac": head_gbs / pk["hbm_gbs"],
+                            "note": "the 262144x1536 head GEMV alone (402.7 MB int8): the chain's per-layer "
+                                    "GEMVs (3.1-18.9 MB) are bound by launch and DRAM latency, not bandwidth"}}
+        if not args.no_config4 and args.only is None:
+            line["config4"] = {"prompts_dp": prompts_dp(w8, dev, stream, world, rank, 3, 3),
+                               "lm_head_sharded": sharded_head(w8, dev, stream, world, 50, 5, pk)}
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference_rate(args.m)
         if rank == 0:

@@ -54,8 +54,11 @@ def test_golden_int_mm(cuda, golden):
         np.testing.assert_array_equal(c.cpu().numpy(), full["c"])
 
 
+# CTA-pair tiles (M > 128, K % 128 == 0) stage 256 K bytes at a time; K / 128 odd leaves
+# half of the last stage beyond K: (300, 384, 384), (257, 200, 128), (513, 264, 640).
 SMALL = [(1, 16, 16), (7, 40, 32), (128, 256, 128), (129, 257, 144), (300, 384, 1536),
-         (64, 256, 1536), (64, 1536, 256), (5, 1000, 48), (255, 520, 272)]
+         (64, 256, 1536), (64, 1536, 256), (5, 1000, 48), (255, 520, 272),
+         (300, 384, 384), (257, 200, 128), (513, 264, 640)]
 
 
 @pytest.mark.parametrize("layout", ["kn", "nk"])

@@ -18,7 +18,8 @@ pytestmark = pytest.mark.gpu
 # prompts) and single-kernel shapes with only a few tiles (M <= 128).
 SHAPES = [(3658, 1536, 2048), (3658, 1536, 6144), (3658, 2560, 1536), (207, 1536, 6144),
           (858, 2560, 1536), (300, 512, 4096), (64, 1536, 256), (64, 256, 1536), (100, 1536, 6144),
-          (16, 2560, 1536), (1, 2560, 1536), (129, 384, 2048)]
+          (16, 2560, 1536), (1, 2560, 1536), (129, 384, 2048),
+          (600, 1536, 3200)]  # K / 128 = 25: the last 256-byte K stage of a CTA pair is half empty
 
 
 def plain(a, w):
