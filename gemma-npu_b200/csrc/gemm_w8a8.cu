@@ -64,7 +64,11 @@ constexpr int kEpiWarps = 4;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint32_t kTmemCols = 2 * kBN;  // two accumulators of 256 int32 columns
 
-enum EpiKind : int { kEpiI32 = 0, kEpiBf16 = 1 };
+// kEpiI32: int32 accumulators.  kEpiBf16: _deq to bf16.  kEpiGeluUp: the gate/up glue
+// k_gelu (pipeline.py:102-107) up to its quant: bf16(gelu_tanh(gate) * up) of the
+// dequantised halves of each 256-column tile (packed weights: tile t holds gate rows
+// 128t.. and up rows I + 128t..), 128 bf16 outputs per tile row, plus the row absmax.
+enum EpiKind : int { kEpiI32 = 0, kEpiBf16 = 1, kEpiGeluUp = 2 };
 
 struct GemmArgs {
   int m, n, k;
@@ -79,6 +83,7 @@ struct GemmArgs {
   int stream_k;      // 1: stream-K schedule (int32 + TMA output + flags only)
   uint32_t* flags;   // stream-K: one zero-initialised counter per tile
   int bn;            // output columns per tile: 256, or 192 on CTA pairs when it balances waves
+  float* row_absmax; // kEpiGeluUp: per-row max |output| (fp32 bits, atomicMax), zero on entry
 };
 
 constexpr int kEpiBufBytes = 32 * 128;  // one 32-row x 128-byte store box
@@ -214,6 +219,82 @@ __device__ __forceinline__ void dequant_pack(const GemmArgs& a, int col0, const 
   }
 }
 
+constexpr float kGeluBeta = 0.7978845608028654f;  // sqrt(2 / pi)
+constexpr float kGeluKappa = 0.044715f;
+
+__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// bf16 of F.gelu(g, approximate="tanh") for a bf16 value g: ATen's fp32 operation order
+// 0.5 * g * (1 + tanh(sqrt(2/pi) * (g + 0.044715 * g^3))), every step rounded (no FMA
+// contraction), rounded once to bf16 at the end.
+__device__ __forceinline__ float gelu_tanh_bf16(float g) {
+  const float g3 = __fmul_rn(__fmul_rn(g, g), g);
+  const float inner = __fmul_rn(kGeluBeta, __fadd_rn(g, __fmul_rn(kGeluKappa, g3)));
+  return round_bf16(__fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.f, tanhf(inner))));
+}
+
+// 32 gate accumulators (GEMM columns gcol0..) and the 32 up accumulators 128 columns to
+// their right -> 16 words of packed bf16 a = bf16(gelu(_deq(gate)) * _deq(up)); `amax`
+// accumulates max |a|.
+__device__ __forceinline__ void gelu_up_pack(const GemmArgs& a, int gcol0, const uint32_t (&rg)[32],
+                                             const uint32_t (&ru)[32], float sxr, uint32_t* out,
+                                             float& amax) {
+  float wg[32], wu[32];
+  if (a.vec_sw) {
+    const float4* g4 = reinterpret_cast<const float4*>(a.sw + gcol0);
+    const float4* u4 = reinterpret_cast<const float4*>(a.sw + gcol0 + 128);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 t = __ldg(g4 + j), v = __ldg(u4 + j);
+      wg[4 * j] = t.x, wg[4 * j + 1] = t.y, wg[4 * j + 2] = t.z, wg[4 * j + 3] = t.w;
+      wu[4 * j] = v.x, wu[4 * j + 1] = v.y, wu[4 * j + 2] = v.z, wu[4 * j + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      wg[j] = __ldg(a.sw + gcol0 + j);
+      wu[j] = __ldg(a.sw + gcol0 + 128 + j);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float av[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int c = 2 * j + e;
+      const float g = round_bf16(__fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(rg[c])), sxr), wg[c]));
+      const float u = round_bf16(__fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(ru[c])), sxr), wu[c]));
+      av[e] = round_bf16(__fmul_rn(gelu_tanh_bf16(g), u));
+      amax = fmaxf(amax, fabsf(av[e]));
+    }
+    __nv_bfloat162 p = __floats2bfloat162_rn(av[0], av[1]);
+    out[j] = *reinterpret_cast<uint32_t*>(&p);
+  }
+}
+
+// Stage one 32-row x 128-byte box in this warp's swizzled buffer and store it with TMA
+// (or add it, for a stream-K partial) at column x, row row0.
+__device__ __forceinline__ void put_box(const CUtensorMap* tm_c, const uint32_t (&v)[32], uint32_t stage_base,
+                                       uint32_t& sbuf, int lane, int x, int row0, bool reduce) {
+  const uint32_t buf = stage_base + (sbuf & 1u) * kEpiBufBytes;
+  ++sbuf;
+  if (lane == 0) bulk_wait_group_read<kEpiBufs - 1>();  // the box last stored from buf is read
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    st_shared_v4(buf + lane * 128 + ((j ^ (lane & 7)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                 v[4 * j + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (reduce)
+      tma_reduce_add_2d(tm_c, buf, x, row0);
+    else
+      tma_store_2d(tm_c, buf, x, row0);
+    bulk_commit_group();
+  }
+}
+
 // Drain one 32-row slice of a finished accumulator (called by one whole epilogue warp).
 // `taddr` addresses the warp's TMEM lanes at the accumulator's first column; rows
 // row0.. and columns col_base.. of the output.  `release` hands the accumulator back to
@@ -226,6 +307,32 @@ __device__ __forceinline__ void epilogue_rows(const GemmArgs& args, const CUtens
                                               bool reduce, Release release) {
   const int n_cols = min(args.bn, args.n - col_base);  // columns of this tile inside N
   const int row = row0 + lane;
+  if constexpr (EPI == kEpiGeluUp) {
+    // 256 accumulator columns = 128 gate + 128 up -> output columns col_base / 2 ..+128,
+    // two 64-column bf16 boxes (the output must be TMA-addressable).
+    float amax = 0.f;
+#pragma unroll 1
+    for (int b = 0; b < 2; ++b) {
+      uint32_t v[32];
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        const int c = b * 64 + h * 32;
+        uint32_t rg[32], ru[32];
+        tmem_ld_32x32b_x32(taddr + c, rg);
+        tmem_ld_32x32b_x32(taddr + 128 + c, ru);
+        tmem_wait_ld();
+        if (b == 1 && h == 1) {  // the accumulator is in registers: hand TMEM back
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) release();
+        }
+        gelu_up_pack(args, col_base + c, rg, ru, sxr, v + h * 16, amax);
+      }
+      put_box(tm_c, v, stage_base, sbuf, lane, col_base / 2 + b * 64, row0, false);
+    }
+    if (row < args.m) atomicMax(reinterpret_cast<int*>(args.row_absmax) + row, __float_as_int(amax));
+    return;
+  }
   if (args.tma_out) {
     // One store box = 32 rows x 128 bytes: 32 int32 or 64 bf16 columns.
     constexpr int kCols = EPI == kEpiI32 ? 32 : 64;
@@ -250,23 +357,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmArgs& args, const CUtens
         __syncwarp();
         if (lane == 0) release();
       }
-      const uint32_t buf = stage_base + (sbuf & 1u) * kEpiBufBytes;
-      ++sbuf;
-      if (lane == 0) bulk_wait_group_read<kEpiBufs - 1>();  // the box last stored from buf is read
-      __syncwarp();
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        st_shared_v4(buf + lane * 128 + ((j ^ (lane & 7)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
-                     v[4 * j + 3]);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        if (reduce)
-          tma_reduce_add_2d(tm_c, buf, col_base + c * kCols, row0);
-        else
-          tma_store_2d(tm_c, buf, col_base + c * kCols, row0);
-        bulk_commit_group();
-      }
+      put_box(tm_c, v, stage_base, sbuf, lane, col_base + c * kCols, row0, reduce);
     }
   } else {
     const int n_chunks = (n_cols + 31) / 32;
@@ -493,7 +584,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int nb = sg.tile / args.m_tiles;
       const int row0 = mb * 2 * kBM + static_cast<int>(rank) * kBM + quarter * 32;
       float sxr = 0.f;
-      if constexpr (EPI == kEpiBf16) sxr = row0 + lane < args.m ? __ldg(args.sx + row0 + lane) : 0.f;
+      if constexpr (EPI != kEpiI32) sxr = row0 + lane < args.m ? __ldg(args.sx + row0 + lane) : 0.f;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
       epilogue_segment<EPI>(args, &tm_c, sg, taddr, row0, nb * args.bn, sxr, stage_base, sbuf, lane,
                             2 * kEpiWarps, [&] { mbar_arrive_cluster(tempty_leader0 + 8u * acc); });
@@ -672,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nb = sg.tile / args.m_tiles;
       const int row0 = mb * kBM + quarter * 32;
       float sxr = 0.f;
-      if constexpr (EPI == kEpiBf16) sxr = row0 + lane < args.m ? __ldg(args.sx + row0 + lane) : 0.f;
+      if constexpr (EPI != kEpiI32) sxr = row0 + lane < args.m ? __ldg(args.sx + row0 + lane) : 0.f;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
       epilogue_segment<EPI>(args, &tm_c, sg, taddr, row0, nb * kBN, sxr, stage_base, sbuf, lane,
                             kEpiWarps, [&] { mbar_arrive(tempty_bar(acc)); });
@@ -881,7 +972,9 @@ static int launch_single(int device, const CUtensorMap& ta, const CUtensorMap& t
 static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
                        void* out, int64_t ldo, int out_elem, const float* sx, const float* sw,
                        int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
-                       cudaStream_t stream, int epi) {
+                       cudaStream_t stream, int epi, float* row_absmax = nullptr) {
+  // Output columns: the GEMM's N, or N / 2 for the gate/up glue (gelu(gate) * up).
+  const int64_t n_out = epi == w8::kEpiGeluUp ? n / 2 : n;
   W8_CHECK_ARG(m >= 0 && n >= 0 && k >= 0, "negative size (m=%lld n=%lld k=%lld)", (long long)m,
                (long long)n, (long long)k);
   W8_CHECK_ARG(m < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31), "size beyond int32 range");
@@ -889,16 +982,24 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   W8_CHECK_ARG(workspace_bytes >= 0, "negative workspace size");
   if (m == 0 || n == 0) return W8_OK;
   W8_CHECK_ARG(out != nullptr, "null output pointer");
-  W8_CHECK_ARG(ldo >= n, "output row pitch %lld < n %lld", (long long)ldo, (long long)n);
+  W8_CHECK_ARG(ldo >= n_out, "output row pitch %lld < %lld columns", (long long)ldo, (long long)n_out);
   W8_CHECK_ALIGN(aligned(out, out_elem), "output must be aligned to its element size");
-  if (epi == w8::kEpiBf16) W8_CHECK_ARG(sx != nullptr && sw != nullptr, "null scale pointer");
+  if (epi != w8::kEpiI32) W8_CHECK_ARG(sx != nullptr && sw != nullptr, "null scale pointer");
+  if (epi == w8::kEpiGeluUp) {
+    W8_CHECK_ARG(b_layout == W8_B_NK, "the gate/up glue takes packed [2I, K] weights (W8_B_NK)");
+    W8_CHECK_ARG(n % 256 == 0, "2 * inter = %lld must be a multiple of 256", (long long)n);
+    W8_CHECK_ARG(row_absmax != nullptr, "null row absmax scratch");
+    W8_CHECK_ALIGN(aligned(row_absmax, 4), "row absmax scratch must be 4-byte aligned");
+    W8_CHECK_ALIGN(aligned(out, 16) && (ldo * out_elem) % 16 == 0,
+                   "the gate/up glue output must be 16-byte aligned with a 16-byte row pitch");
+  }
   W8_CHECK_ALIGN(workspace == nullptr || aligned(workspace, 4), "workspace must be 4-byte aligned");
   int device = 0;
   int st = require_sm100(&device);
   if (st != W8_OK) return st;
   if (k == 0) {
     // An empty contraction: the product is all zeros (and so is its dequant).
-    W8_CUDA_TRY(cudaMemset2DAsync(out, ldo * out_elem, 0, n * out_elem, m, stream));
+    W8_CUDA_TRY(cudaMemset2DAsync(out, ldo * out_elem, 0, n_out * out_elem, m, stream));
     return W8_OK;
   }
   W8_CHECK_ARG(a != nullptr && b != nullptr, "null operand pointer");
@@ -920,7 +1021,8 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   // of a 256-wide one), e.g. N = 2560 (qkv) and N = 1536 (o) at M = 3658.  Shapes that
   // stream-K will balance keep 256.
   int bn = w8::kBN;
-  if (pair && b_layout == W8_B_NK && !(epi == w8::kEpiI32 && workspace != nullptr && k >= 24 * w8::kBK)) {
+  if (pair && b_layout == W8_B_NK && epi != w8::kEpiGeluUp &&
+      !(epi == w8::kEpiI32 && workspace != nullptr && k >= 24 * w8::kBK)) {
     int cap = 0;
     st = pair_capacity<false, w8::kEpiI32, w8::kBN>(device, &cap);
     if (st != W8_OK) return st;
@@ -960,6 +1062,7 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   args.vec_sw = sw != nullptr && aligned(sw, 16);
   args.stream_k = 0;
   args.flags = static_cast<uint32_t*>(workspace);
+  args.row_absmax = row_absmax;
   const int64_t flag_words = workspace_bytes / 4;
   // Output through TMA when the tensor map can address it (16-byte base and pitch);
   // one box is 32 rows x 128 bytes.  Otherwise the epilogue stores directly.
@@ -967,7 +1070,7 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   args.tma_out = 0;
   if (args.vec_out) {
     const bool i32 = epi == w8::kEpiI32;
-    st = encode_2d(&tc, i32 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, n, m,
+    st = encode_2d(&tc, i32 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, n_out, m,
                    ldo * out_elem, i32 ? 32 : 64, 32);
     if (st != W8_OK) return st;
     args.tma_out = 1;
@@ -975,6 +1078,9 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
 
   const bool mn = b_layout == W8_B_KN;
   const bool i32 = epi == w8::kEpiI32;
+  if (epi == w8::kEpiGeluUp)
+    return pair ? launch_pair<false, w8::kEpiGeluUp, 256>(device, ta, tb, tc, args, flag_words, stream)
+                : launch_single<false, w8::kEpiGeluUp>(device, ta, tb, tc, args, flag_words, stream);
   if (pair) {
     if (i32)
       return mn ? launch_pair<true, w8::kEpiI32, 256>(device, ta, tb, tc, args, flag_words, stream)
@@ -1079,6 +1185,24 @@ extern "C" int w8_mm_i8_ws(const int8_t* a, int64_t lda, const int8_t* b, int64_
                            int64_t workspace_bytes, w8_stream_t stream) {
   return w8host::gemm_common(a, lda, b, ldb, b_layout, c, ldc, 4, nullptr, nullptr, m, n, k, workspace,
                              workspace_bytes, reinterpret_cast<cudaStream_t>(stream), w8::kEpiI32);
+}
+
+namespace w8host {
+int quant_rows_absmax_bf16(const uint16_t* y, int64_t ldy, float* absmax, int8_t* q, int64_t ldq, float* s,
+                           int64_t m, int64_t k, cudaStream_t stream);
+}  // namespace w8host
+
+extern "C" int w8_gemm_gelu_up_quant(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw,
+                                     const float* sx, const float* sw, int64_t m, int64_t inter, int64_t k,
+                                     uint16_t* y, int64_t ldy, float* row_absmax, int8_t* q, int64_t ldq,
+                                     float* s, w8_stream_t stream) {
+  W8_CHECK_ARG(inter >= 0 && inter % 128 == 0, "inter = %lld must be a multiple of 128", (long long)inter);
+  if (m == 0 || inter == 0) return W8_OK;
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int r = w8host::gemm_common(a, lda, w, ldw, W8_B_NK, y, ldy, 2, sx, sw, m, 2 * inter, k, nullptr, 0,
+                                    st, w8::kEpiGeluUp, row_absmax);
+  if (r != W8_OK) return r;
+  return w8host::quant_rows_absmax_bf16(y, ldy, row_absmax, q, ldq, s, m, inter, st);
 }
 
 extern "C" int w8_gemm_dequant_bf16(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb,

@@ -164,9 +164,49 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The quant half of the gate/up glue (pipeline.py:107, _quant of k_gelu's bf16 output)
+// when the row absmax is already known: the fused GEMM epilogue folded it into
+// absmax[row] (fp32 bits, atomicMax).  s = max(absmax, 1e-8) / 127 and q exactly as in
+// quant_rows_kernel; absmax[row] is reset to zero for the next call.  One CTA per row,
+// 8 bf16 per thread step (16-byte loads, 8-byte stores).
+__global__ void __launch_bounds__(kQuantThreads)
+    quant_absmax_kernel(const __nv_bfloat16* __restrict__ y, int64_t ldy, float* __restrict__ absmax,
+                        int8_t* __restrict__ q, int64_t ldq, float* __restrict__ s, int k) {
+  const int row = blockIdx.x;
+  const float sc = __fdiv_rn(fmaxf(absmax[row], 1e-8f), 127.f);
+  __syncthreads();  // every thread has read absmax[row]
+  if (threadIdx.x == 0) {
+    s[row] = sc;
+    absmax[row] = 0.f;
+  }
+  const __nv_bfloat16* yr = y + static_cast<int64_t>(row) * ldy;
+  int8_t* qr = q + static_cast<int64_t>(row) * ldq;
+  for (int vi = threadIdx.x; vi < k / 8; vi += kQuantThreads) {
+    const Vec<__nv_bfloat16, 8> v = load_vec<__nv_bfloat16, 8>(yr + vi * 8);
+    int8_t out[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) out[e] = quant_one(__bfloat162float(v.v[e]), sc);
+    store_q<8>(qr + vi * 8, out);
+  }
+}
+
 }  // namespace w8
 
 namespace w8host {
+
+int quant_rows_absmax_bf16(const uint16_t* y, int64_t ldy, float* absmax, int8_t* q, int64_t ldq, float* s,
+                           int64_t m, int64_t k, cudaStream_t stream) {
+  W8_CHECK_ARG(m >= 0 && k >= 0 && m < (1ll << 31) && k < (1ll << 31), "bad size");
+  if (m == 0) return W8_OK;
+  W8_CHECK_ARG(y != nullptr && absmax != nullptr && q != nullptr && s != nullptr, "null pointer");
+  W8_CHECK_ARG(ldy >= k && ldq >= k, "row pitch smaller than k");
+  W8_CHECK_ARG(k % 8 == 0, "k = %lld must be a multiple of 8", (long long)k);
+  W8_CHECK_ALIGN(aligned(y, 16) && (ldy * 2) % 16 == 0, "y must be 16-byte aligned with a 16-byte row pitch");
+  W8_CHECK_ALIGN(aligned(q, 8) && ldq % 8 == 0, "q must be 8-byte aligned with ldq %% 8 == 0");
+  w8::quant_absmax_kernel<<<static_cast<unsigned>(m), w8::kQuantThreads, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(y), ldy, absmax, q, ldq, s, static_cast<int>(k));
+  return cuda_status(cudaGetLastError());
+}
 
 int require_sm100(int* device);
 

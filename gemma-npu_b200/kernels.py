@@ -8,6 +8,7 @@ quant/dequant glue of `pipeline.py` / `gemma_npu.py`:
     quant_rows(x) -> (q, s)      pipeline.py:49-52, gemma_npu.py:37-42
     dequant(acc, sx, sw)         pipeline.py:55-57, gemma_npu.py:45-47
     int8_linear(x, wq, sw)       gemma_npu.py:155-156   (torch._weight_int8pack_mm)
+    gelu_up_quant(x, sx, w, sw)  pipeline.py:102-107   (k_gelu fused onto the gate/up GEMM)
 
 Every function validates dtype/shape/layout on the host, passes raw device
 pointers and torch's current CUDA stream to the C ABI, and raises a W8Error
@@ -148,6 +149,68 @@ def gemm_dequant(a, w, sx, sw, out=None):
     _lib.call("w8_gemm_dequant_bf16", a.data_ptr(), _ld(a), w.data_ptr(), _ld(w), W8_B_NK,
               sx.data_ptr(), sw.data_ptr(), out.data_ptr(), _ld(out), M, N, K, _stream(a))
     return out
+
+
+def pack_gelu_up(w, sw):
+    """Reorder a gate/up weight [2I, K] (gate rows, then up rows) and its scales [2I] for
+    gelu_up_quant: packed row 256t + j = gate row 128t + j, packed row 256t + 128 + j =
+    up row I + 128t + j (j < 128), so each 256-column GEMM tile holds matching gate and
+    up columns.  Done once, when the resident weight is built.  I % 128 == 0."""
+    two_i = w.shape[0]
+    _need(two_i % 256 == 0, f"2 * I = {two_i} must be a multiple of 256")
+    _need(sw.shape == (two_i,), f"sw must have shape ({two_i},)")
+    inter = two_i // 2
+    blk = torch.arange(inter // 128, device=w.device)[:, None] * 128 + torch.arange(128, device=w.device)
+    idx = torch.stack([blk, blk + inter], dim=1).reshape(-1)
+    return w.index_select(0, idx).contiguous(), sw.index_select(0, idx).contiguous()
+
+
+# Row-absmax scratch of the gate/up glue, zero between calls, one per (device, stream).
+_ABSMAX = {}
+
+
+def _absmax_scratch(device, stream, rows):
+    key = (device.index, stream)
+    buf = _ABSMAX.get(key)
+    if buf is None or buf.numel() < rows:
+        buf = torch.zeros(max(rows, 4096), dtype=torch.float32, device=device)
+        _ABSMAX[key] = buf
+    return buf
+
+
+def gelu_up_quant(x, sx, w_packed, sw_packed, q=None, s=None, y=None):
+    """k_gelu (pipeline.py:102-107) fused onto the gate/up GEMM.
+
+    x int8 [T, K] with per-row scales sx fp32 [T]; w_packed int8 [2I, K] and sw_packed
+    fp32 [2I] from pack_gelu_up.  Returns (q int8 [T, I], s fp32 [T]) =
+    _quant(bf16(gelu_tanh(_deq(gate)) * _deq(up))).  `y` (bf16 [T, I]) receives the
+    pre-quant activation; it is allocated when not given.
+    """
+    _check_matrix(x, "x", torch.int8)
+    _check_matrix(w_packed, "w_packed", torch.int8)
+    T, K = x.shape
+    two_i = w_packed.shape[0]
+    _need(w_packed.shape[1] == K, f"inner sizes differ: x {tuple(x.shape)}, w {tuple(w_packed.shape)}")
+    _need(two_i % 256 == 0, f"2 * I = {two_i} must be a multiple of 256")
+    inter = two_i // 2
+    _check_vector(sx, "sx", torch.float32, T)
+    _check_vector(sw_packed, "sw_packed", torch.float32, two_i)
+    if q is None:
+        q = torch.empty((T, inter), dtype=torch.int8, device=x.device)
+    if s is None:
+        s = torch.empty((T,), dtype=torch.float32, device=x.device)
+    if y is None:
+        y = torch.empty((T, inter), dtype=torch.bfloat16, device=x.device)
+    _check_matrix(q, "q", torch.int8)
+    _check_matrix(y, "y", torch.bfloat16)
+    _need(tuple(q.shape) == (T, inter) and tuple(y.shape) == (T, inter), f"q and y must be ({T}, {inter})")
+    _check_vector(s, "s", torch.float32, T)
+    stream = _stream(x)
+    absmax = _absmax_scratch(x.device, stream, T)
+    _lib.call("w8_gemm_gelu_up_quant", x.data_ptr(), _ld(x), w_packed.data_ptr(), _ld(w_packed),
+              sx.data_ptr(), sw_packed.data_ptr(), T, inter, K, y.data_ptr(), _ld(y), absmax.data_ptr(),
+              q.data_ptr(), _ld(q), s.data_ptr(), stream)
+    return q, s
 
 
 def quant_rows(x, q=None, s=None):

@@ -19,6 +19,8 @@
  *   w8_dequant_bf16         pipeline.py:55-57 (_deq), gemma_npu.py:45-47 (_dequant)
  *   w8_int8_linear_bf16     gemma_npu.py:155-156 (cpu_int8_linear = torch._weight_int8pack_mm)
  *   w8_lm_head_f32          gemma_npu.py:170-172 (Int8Head.forward) + pipeline.py:335-338 (softcap)
+ *   w8_gemm_gelu_up_quant   pipeline.py:102-107 (k_gelu) fused onto the gate/up GEMM of
+ *                           pipeline.py:233-242 (Prefill.gemm)
  */
 #ifndef W8A8_B200_H
 #define W8A8_B200_H
@@ -105,6 +107,24 @@ int w8_mm_i8_noalloc(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb,
 int w8_gemm_dequant_bf16(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
                          const float* sx, const float* sw, uint16_t* y, int64_t ldy,
                          int64_t m, int64_t n, int64_t k, w8_stream_t stream);
+
+/* The gate/up GEMM with the glue that follows it fused (k_gelu, pipeline.py:102-107):
+ *   y   = _deq(A @ W^T, sx, sw)                      [M, 2I], never written
+ *   a   = bf16(gelu_tanh(y[:, :I]) * y[:, I:])       [M, I] bf16, written to `y_out`
+ *   q,s = _quant(a)                                  int8 [M, I] + fp32 [M]
+ * W and sw are the gate/up weight and scales PACKED by 128-row blocks: packed row
+ * 256t + j (j < 128) is gate row 128t + j and packed row 256t + 128 + j is up row
+ * I + 128t + j, so each 256-column GEMM tile holds matching gate and up columns.
+ * inter = I must be a multiple of 128; K % 16 == 0 (K % 128 == 0 for M > 128 to use
+ * CTA pairs).  y_out: 16-byte aligned, ldy*2 % 16 == 0.  q: 8-byte aligned, ldq % 8 == 0.
+ * row_absmax: M floats that must be zero on entry; they are zero again on return.
+ * Two launches on `stream`: the GEMM (epilogue writes a and folds max|a| per row into
+ * row_absmax) and the row quant.  No counterpart in the reference beyond the glue it
+ * fuses: the reference runs k_gelu on the CPU over the int32 GEMM output. */
+int w8_gemm_gelu_up_quant(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw,
+                          const float* sx, const float* sw, int64_t m, int64_t inter, int64_t k,
+                          uint16_t* y_out, int64_t ldy, float* row_absmax, int8_t* q, int64_t ldq,
+                          float* s, w8_stream_t stream);
 
 /* ---- quantisation ------------------------------------------------------ */
 

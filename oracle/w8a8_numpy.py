@@ -78,3 +78,31 @@ def softcap(logits, cap):
     """cap * tanh(logits / cap) (pipeline.py:336-338); identity when cap is falsy."""
     logits = np.asarray(logits, dtype=np.float64)
     return np.tanh(logits / cap) * cap if cap else logits
+
+
+GELU_BETA = np.float32(np.sqrt(2.0) * (2.0 / np.sqrt(np.pi)) * 0.5)  # sqrt(2 / pi)
+GELU_KAPPA = np.float32(0.044715)
+
+
+def gelu_tanh_bf16(g):
+    """F.gelu(g, approximate="tanh") of bf16 values g (float32 in, bf16-rounded float32 out).
+
+    0.5 * g * (1 + tanh(sqrt(2/pi) * (g + 0.044715 * g^3))) in fp32, rounded once to bf16,
+    the operation order of ATen's CPU kernel for reduced-precision inputs.
+    """
+    g = np.asarray(g, dtype=np.float32)
+    inner = GELU_BETA * (g + GELU_KAPPA * (g * g * g))
+    out = np.float32(0.5) * g * (np.float32(1) + np.tanh(inner).astype(np.float32))
+    return bf16_bits_to_f32(f32_to_bf16_bits(out.astype(np.float32)))
+
+
+def gelu_up_quant(acc, sx, sw, inter):
+    """The gate/up epilogue glue k_gelu (pipeline.py:102-107).
+
+    y = _deq(acc, sx, sw) (bf16 [T, 2I]); a = bf16(gelu_tanh(y[:, :I]) * y[:, I:]);
+    returns _quant(a): int8 [T, I] and fp32 scales [T].
+    """
+    y = bf16_bits_to_f32(dequant(acc, sx, sw))
+    g, u = y[:, :inter], y[:, inter:]
+    a = bf16_bits_to_f32(f32_to_bf16_bits((gelu_tanh_bf16(g) * u).astype(np.float32)))
+    return quant_rows(a)

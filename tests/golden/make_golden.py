@@ -12,6 +12,7 @@ repository) and records, on seeded inputs:
   deq       pipeline._deq (pipeline.py:55-57) and gemma_npu._dequant (gemma_npu.py:45-47)
   gemv      gemma_npu.cpu_int8_linear (gemma_npu.py:155-156), T = 1 and T = 3
   head      gemma_npu.Int8Head.forward + the softcap of pipeline.py:335-338
+  gelu_up   pipeline.k_gelu (pipeline.py:102-107): dequant, gelu_tanh(gate) * up, int8 quant
 
 The weight of the GEMM, GEMV and head cases is the one stored in wquant.npz
 (q [N,K] int8, s bf16 [N]); the GEMM's B operand is its transpose.  The outputs
@@ -100,6 +101,21 @@ def main(ref_dir):
     cap = 30.0
     logits = torch.tanh(logits / cap) * cap
     out["head"] = dict(h=bf16_bits(h.reshape(-1)), cap=np.float32(cap), logits=logits.numpy())
+
+    # ---- gate/up epilogue glue (pipeline.py:102-107, k_gelu): dequant -> gelu_tanh(gate) * up
+    # -> per-row int8 quant of the down projection's input.  k_gelu is torch.compile'd; its
+    # eager function (the same Python body) is what runs here.
+    k_gelu = getattr(pipeline.k_gelu, "_torchdynamo_orig_callable", pipeline.k_gelu)
+    gi, gk, gt = 512, 256, 24
+    gx, gsx = pipeline._quant(torch.randn(gt, gk).to(torch.bfloat16))
+    gw = (torch.randn(2 * gi, gk) * 0.02).float()
+    gsw = gw.abs().amax(dim=1).clamp(min=1e-8) / 127
+    gwq = torch.round(gw / gsw[:, None]).clamp(-127, 127).to(torch.int8)
+    gx[0] = 0                                             # zero row: the 1e-8 scale floor
+    gacc = torch._int_mm(gx, gwq.t().contiguous())
+    gq, gs = k_gelu(gacc, gsx, gsw, gi)
+    out["gelu_up"] = dict(x=gx.numpy(), w=gwq.numpy(), acc=gacc.numpy(), sx=gsx.numpy(), sw=gsw.numpy(),
+                          inter=np.int32(gi), q=gq.numpy(), s=gs.numpy())
 
     for name, arrays in out.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)

@@ -58,6 +58,12 @@ def test_host_side_argument_checks_need_no_gpu():
     assert lib.w8_quant_rows_bf16(None, 16, None, 16, None, 4, 16, None) == _lib.W8_ERR_INVALID_ARG
     assert lib.w8_dequant_bf16(None, 16, None, None, None, 16, 4, 16, None) == _lib.W8_ERR_INVALID_ARG
     assert lib.w8_lm_head_f32(None, None, None, 30.0, None, 8, 16, None) == _lib.W8_ERR_INVALID_ARG
+    # gate/up glue: I must be a multiple of 128; the absmax scratch is required
+    assert lib.w8_gemm_gelu_up_quant(None, 16, None, 16, None, None, 4, 100, 16, None, 128, None, None, 128,
+                                     None, None) == _lib.W8_ERR_INVALID_ARG
+    assert b"inter" in lib.w8_last_error()
+    assert lib.w8_gemm_gelu_up_quant(None, 16, None, 16, None, None, 0, 128, 16, None, 128, None, None, 128,
+                                     None, None) == _lib.W8_OK
 
 
 def test_status_maps_to_exceptions():

@@ -82,3 +82,19 @@ def test_kernels_reject_host_tensors():
         w8.quant_rows(torch.zeros(4, 16))
     with pytest.raises(ValueError, match="CUDA"):
         w8.int8_linear(torch.zeros(1, 16), torch.zeros(4, 16, dtype=torch.int8), torch.zeros(4))
+
+
+def test_pack_gelu_up_layout():
+    """Packed row 256t + j = gate row 128t + j; packed row 256t + 128 + j = up row I + 128t + j."""
+    import torch
+
+    inter, k = 384, 16
+    w = torch.arange(2 * inter, dtype=torch.int32)[:, None].expand(2 * inter, k).to(torch.int8).contiguous()
+    rows = torch.arange(2 * inter, dtype=torch.float32)
+    wp, sp = w8.pack_gelu_up(torch.arange(2 * inter)[:, None].expand(2 * inter, k).contiguous(), rows)
+    for t in range(inter // 128):
+        for j in (0, 5, 127):
+            assert sp[256 * t + j].item() == 128 * t + j
+            assert sp[256 * t + 128 + j].item() == inter + 128 * t + j
+            assert wp[256 * t + 128 + j, 3].item() == inter + 128 * t + j
+    assert w.shape == wp.shape

@@ -100,3 +100,12 @@ def test_bf16_round_trip():
     x = np.array([1.0, -2.5, 3.14159, 1e-30, 65504.0, np.float32(1.00390625)], dtype=np.float32)
     t = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     np.testing.assert_array_equal(ref.f32_to_bf16_bits(x), t)
+
+
+def test_gelu_up_quant_bit_exact(golden):
+    """k_gelu (pipeline.py:102-107): dequant, gelu_tanh(gate) * up, int8 quant."""
+    g = golden("gelu_up")
+    np.testing.assert_array_equal(ref.int_mm(g["x"], g["w"].T), g["acc"])
+    q, s = ref.gelu_up_quant(g["acc"], g["sx"], g["sw"], int(g["inter"]))
+    np.testing.assert_array_equal(q, g["q"])
+    np.testing.assert_array_equal(s, g["s"])
