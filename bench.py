@@ -320,6 +320,51 @@ def sharded_head(w8, dev, stream, world, steps, warmup, pk):
             "steps": steps}
 
 
+def fused_gelu_up(w8, work, dev, stream, steps, warmup, world):
+    """SURVEY next row 1: the gate/up GEMM with the k_gelu glue (pipeline.py:102-107)
+    fused into its epilogue, against the same work unfused on the GPU (int32 GEMM, then
+    dequant, gelu(gate) * up and quant as separate kernels), 35 layers each."""
+    name, n, k = LAYER_SHAPES[2]
+    inter = n // 2
+    g = torch.Generator(device=dev).manual_seed(31)
+    xs = [xq for xq, _, _, nm in work["calls"] if nm == name]
+    m = xs[0].shape[0]
+    layers = []
+    for per, xq in zip(work["weights"], xs):
+        sx = torch.rand((m,), device=dev, generator=g) * 0.03 + 0.01
+        sw = torch.rand((n,), device=dev, generator=g) * 1e-3 + 1e-4
+        wp, swp = w8.pack_gelu_up(per[name], sw)
+        layers.append((xq, sx, per[name], sw, wp, swp))
+    q = torch.empty((m, inter), dtype=torch.int8, device=dev)
+    s = torch.empty((m,), dtype=torch.float32, device=dev)
+    y = torch.empty((m, inter), dtype=torch.bfloat16, device=dev)
+    acc = torch.empty((m, n), dtype=torch.int32, device=dev)
+
+    def fused():
+        for xq, sx, _, _, wp, swp in layers:
+            w8.gelu_up_quant(xq, sx, wp, swp, q=q, s=s, y=y)
+
+    def unfused():
+        for xq, sx, wq, sw, _, _ in layers:
+            w8.mm_i8_nk(xq, wq, acc)
+            d = w8.dequant(acc, sx, sw)
+            a = (torch.nn.functional.gelu(d[:, :inter], approximate="tanh") * d[:, inter:]).to(torch.bfloat16)
+            w8.quant_rows(a, q=q, s=s)
+
+    res = {}
+    for label, fn in (("fused", fused), ("unfused", unfused)):
+        gr = capture(fn, stream)
+        res[label] = timed(lambda: gr.replay(), steps, warmup, stream, world) / steps / len(layers)
+        del gr
+    ops = 2 * m * n * k
+    return {"workload": f"config-1 gate/up (M={m}, 2I={n}, K={k}) x {len(layers)} layers, k_gelu glue "
+                        "(dequant, gelu_tanh(gate) * up, int8 quant) fused into the GEMM epilogue",
+            "us_per_layer_fused": res["fused"] * 1e3, "us_per_layer_unfused": res["unfused"] * 1e3,
+            "tops_fused": ops / (res["fused"] * 1e-3) / 1e12, "speedup": res["unfused"] / res["fused"],
+            "unfused": "int32 GEMM + dequant kernel + torch gelu/mul + quant kernel on the same GPU",
+            "hbm_bytes_avoided_per_layer": 4 * m * n * 2 + 2 * m * n * 2}
+
+
 def sweep(w8, dev, stream, steps, warmup):
     """Config 3: each projection shape over 35 layers at M in {207, 858, 1878, 3658}, with
     and without the reference's 512-row padding (TOPS on the unpadded rows)."""
@@ -448,6 +493,7 @@ def main():
     ap.add_argument("--ref-step-s", type=float, default=4.0, help="CPU seconds per reference-arm step")
     ap.add_argument("--sweep", action="store_true", help="config 3: per-shape M sweep, padded vs unpadded (own JSON line)")
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 prompts / sharded LM head objects")
+    ap.add_argument("--no-fused", action="store_true", help="skip the fused gate/up glue object")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -549,6 +595,8 @@ def main():
                             "frac": head_gbs / pk["hbm_gbs"],
                             "note": "the 262144x1536 head GEMV alone (402.7 MB int8): the chain's per-layer "
                                     "GEMVs (3.1-18.9 MB) are bound by launch and DRAM latency, not bandwidth"}}
+        if not args.no_fused and args.only is None:
+            line["fused_gelu_up"] = fused_gelu_up(w8, work, dev, stream, 10, 3, world)
         if not args.no_config4 and args.only is None:
             line["config4"] = {"prompts_dp": prompts_dp(w8, dev, stream, world, rank, 3, 3),
                                "lm_head_sharded": sharded_head(w8, dev, stream, world, 50, 5, pk)}
