@@ -61,7 +61,6 @@ constexpr int kBN = 256;      // columns per tile = accumulator columns
 constexpr int kBK = 128;      // K elements (= bytes) per stage: one 128-byte swizzle row
 constexpr int kUmmaK = 32;    // K of one tcgen05.mma kind::i8
 constexpr int kEpiWarps = 4;
-constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint32_t kTmemCols = 2 * kBN;  // two accumulators of 256 int32 columns
 
 // kEpiI32: int32 accumulators.  kEpiBf16: _deq to bf16.  kEpiGeluUp: the gate/up glue
@@ -88,6 +87,18 @@ struct GemmArgs {
 
 constexpr int kEpiBufBytes = 32 * 128;  // one 32-row x 128-byte store box
 constexpr int kEpiBufs = 2;             // per epilogue warp: fill one while TMA drains the other
+
+// Epilogue warps of a CTA: one per TMEM lane quarter, each with two staging boxes.  The
+// gate/up glue, whose per-element math outweighs its stores, takes two warps per quarter
+// (each finishes one of the tile's two output boxes) with one staging box each: the
+// same shared memory, twice the issue slots.
+template <int EPI>
+constexpr int epi_warps() { return EPI == kEpiGeluUp ? 2 * kEpiWarps : kEpiWarps; }
+template <int EPI>
+constexpr int epi_bufs() { return EPI == kEpiGeluUp ? kEpiBufs / 2 : kEpiBufs; }
+template <int EPI>
+constexpr int threads_for() { return 64 + 32 * epi_warps<EPI>(); }
+static_assert(2 * kEpiWarps * (kEpiBufs / 2) == kEpiWarps * kEpiBufs, "staging layout differs");
 
 // Shared-memory plan of one CTA: the operand ring, the epilogue staging boxes, barriers.
 template <int STAGES, int A_BYTES, int B_BYTES>
@@ -224,13 +235,25 @@ constexpr float kGeluKappa = 0.044715f;
 
 __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// 1 + tanh(z) = 2 / (1 + e^(-2z)), from one ex2.approx and one rcp.approx (relative error
+// a few 2^-23).  Like 1 + tanhf(z) in fp32 it is exactly 2 for large z and exactly 0 for
+// very negative z (e^(-2z) overflows to +inf, whose reciprocal is 0).
+__device__ __forceinline__ float one_plus_tanh(float z) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(__fmul_rn(z, -2.8853900817779268f)));  // -2 log2(e)
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fadd_rn(1.f, e)));
+  return 2.f * r;
+}
+
 // bf16 of F.gelu(g, approximate="tanh") for a bf16 value g: ATen's fp32 operation order
-// 0.5 * g * (1 + tanh(sqrt(2/pi) * (g + 0.044715 * g^3))), every step rounded (no FMA
-// contraction), rounded once to bf16 at the end.
+// 0.5 * g * (1 + tanh(sqrt(2/pi) * (g + 0.044715 * g^3))) with every product and sum
+// rounded (no FMA contraction), rounded once to bf16 at the end.  Only 1 + tanh comes
+// from the approximation above, so the result is the reference's except for a bf16
+// rounding flip about once in 10^4 values.
 __device__ __forceinline__ float gelu_tanh_bf16(float g) {
   const float g3 = __fmul_rn(__fmul_rn(g, g), g);
   const float inner = __fmul_rn(kGeluBeta, __fadd_rn(g, __fmul_rn(kGeluKappa, g3)));
-  return round_bf16(__fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.f, tanhf(inner))));
+  return round_bf16(__fmul_rn(__fmul_rn(0.5f, g), one_plus_tanh(inner)));
 }
 
 // 32 gate accumulators (GEMM columns gcol0..) and the 32 up accumulators 128 columns to
@@ -274,11 +297,12 @@ __device__ __forceinline__ void gelu_up_pack(const GemmArgs& a, int gcol0, const
 
 // Stage one 32-row x 128-byte box in this warp's swizzled buffer and store it with TMA
 // (or add it, for a stream-K partial) at column x, row row0.
+template <int BUFS>
 __device__ __forceinline__ void put_box(const CUtensorMap* tm_c, const uint32_t (&v)[32], uint32_t stage_base,
                                        uint32_t& sbuf, int lane, int x, int row0, bool reduce) {
-  const uint32_t buf = stage_base + (sbuf & 1u) * kEpiBufBytes;
+  const uint32_t buf = stage_base + (sbuf & (BUFS - 1u)) * kEpiBufBytes;
   ++sbuf;
-  if (lane == 0) bulk_wait_group_read<kEpiBufs - 1>();  // the box last stored from buf is read
+  if (lane == 0) bulk_wait_group_read<BUFS - 1>();  // the box last stored from buf is read
   __syncwarp();
 #pragma unroll
   for (int j = 0; j < 8; ++j)
@@ -304,31 +328,32 @@ template <int EPI, typename Release>
 __device__ __forceinline__ void epilogue_rows(const GemmArgs& args, const CUtensorMap* tm_c,
                                               uint32_t taddr, int row0, int col_base, float sxr,
                                               uint32_t stage_base, uint32_t& sbuf, int lane,
-                                              bool reduce, Release release) {
+                                              bool reduce, int part, Release release) {
   const int n_cols = min(args.bn, args.n - col_base);  // columns of this tile inside N
   const int row = row0 + lane;
   if constexpr (EPI == kEpiGeluUp) {
     // 256 accumulator columns = 128 gate + 128 up -> output columns col_base / 2 ..+128,
-    // two 64-column bf16 boxes (the output must be TMA-addressable).
+    // two 64-column bf16 boxes (the output must be TMA-addressable); this warp finishes
+    // box `part`, the warp of the same lane quarter in the other half the other box.
     float amax = 0.f;
-#pragma unroll 1
-    for (int b = 0; b < 2; ++b) {
+    {
+      const int b = part;
       uint32_t v[32];
-#pragma unroll 1
+#pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int c = b * 64 + h * 32;
         uint32_t rg[32], ru[32];
         tmem_ld_32x32b_x32(taddr + c, rg);
         tmem_ld_32x32b_x32(taddr + 128 + c, ru);
         tmem_wait_ld();
-        if (b == 1 && h == 1) {  // the accumulator is in registers: hand TMEM back
+        if (h == 1) {  // this warp's columns are in registers: hand TMEM back
           tc_fence_before();
           __syncwarp();
           if (lane == 0) release();
         }
         gelu_up_pack(args, col_base + c, rg, ru, sxr, v + h * 16, amax);
       }
-      put_box(tm_c, v, stage_base, sbuf, lane, col_base / 2 + b * 64, row0, false);
+      put_box<epi_bufs<EPI>()>(tm_c, v, stage_base, sbuf, lane, col_base / 2 + b * 64, row0, false);
     }
     if (row < args.m) atomicMax(reinterpret_cast<int*>(args.row_absmax) + row, __float_as_int(amax));
     return;
@@ -357,7 +382,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmArgs& args, const CUtens
         __syncwarp();
         if (lane == 0) release();
       }
-      put_box(tm_c, v, stage_base, sbuf, lane, col_base + c * kCols, row0, reduce);
+      put_box<epi_bufs<EPI>()>(tm_c, v, stage_base, sbuf, lane, col_base + c * kCols, row0, reduce);
     }
   } else {
     const int n_chunks = (n_cols + 31) / 32;
@@ -382,7 +407,7 @@ __device__ __forceinline__ void epilogue_segment(const GemmArgs& args, const CUt
                                                  const Segment& s, uint32_t taddr, int row0,
                                                  int col_base, float sxr, uint32_t stage_base,
                                                  uint32_t& sbuf, int lane, int warps_per_contrib,
-                                                 Release release) {
+                                                 int part, Release release) {
   const bool split = s.contributors > 1;
   const bool tail = s.kb1 == args.k_blocks;  // owns the tile's last K-block: stores first
   uint32_t* flag = split ? args.flags + s.tile : nullptr;
@@ -396,7 +421,7 @@ __device__ __forceinline__ void epilogue_segment(const GemmArgs& args, const CUt
     (void)ok;  // on a timeout the sum is wrong and the status says so; the launch still ends
   }
   epilogue_rows<EPI>(args, tm_c, taddr, row0, col_base, sxr, stage_base, sbuf, lane, split && !tail,
-                     release);
+                     part, release);
   if (split && lane == 0) {
     bulk_wait_group<0>();  // this warp's boxes have landed in C
     __threadfence();
@@ -411,7 +436,7 @@ __device__ __forceinline__ void epilogue_segment(const GemmArgs& args, const CUt
 // BN is a template parameter so the MMA instruction descriptor is a compile-time constant.
 // =====================================================================================
 template <bool B_MN, int EPI, int BN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                      const __grid_constant__ CUtensorMap tm_c, const GemmArgs args) {
   static_assert(BN % 64 == 0 && BN <= kBN, "tile width must be a multiple of 64 up to 256");
@@ -444,7 +469,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);               // both: one MMA commit
-      mbar_init(tempty_bar(a), 2 * kEpiWarps);  // leader: the epilogue warps of both CTAs
+      mbar_init(tempty_bar(a), 2 * epi_warps<EPI>());  // leader: the epilogue warps of both CTAs
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -566,8 +591,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue (both CTAs): this CTA's 128 rows of every 256 x 256 tile
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const uint32_t stage_base = base + L::kEpiOff + (warp - 2) * kEpiBufs * kEpiBufBytes;
+    const int quarter = warp & 3;     // TMEM lane quarter this warp may access
+    const int part = (warp - 2) / 4;  // which share of the tile's columns (gate/up glue)
+    const uint32_t stage_base = base + L::kEpiOff + (warp - 2) * epi_bufs<EPI>() * kEpiBufBytes;
     const uint32_t tempty_leader0 = mapa_shared(tempty_bar(0), 0);
     Schedule sched(args, worker, workers);
     Segment sg;
@@ -587,7 +613,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if constexpr (EPI != kEpiI32) sxr = row0 + lane < args.m ? __ldg(args.sx + row0 + lane) : 0.f;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
       epilogue_segment<EPI>(args, &tm_c, sg, taddr, row0, nb * args.bn, sxr, stage_base, sbuf, lane,
-                            2 * kEpiWarps, [&] { mbar_arrive_cluster(tempty_leader0 + 8u * acc); });
+                            2 * epi_warps<EPI>(), part, [&] { mbar_arrive_cluster(tempty_leader0 + 8u * acc); });
     }
     if (lane == 0) bulk_wait_group<0>();  // every store of this warp has landed
   }
@@ -606,7 +632,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // 128 x 256 tiles on one CTA (tcgen05 cta_group::1), for M <= 128
 // =====================================================================================
 template <bool B_MN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for<EPI>(), 1)
     gemm_single_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                        const __grid_constant__ CUtensorMap tm_c, const GemmArgs args) {
   using L = SingleSmem;
@@ -636,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), kEpiWarps);
+      mbar_init(tempty_bar(a), epi_warps<EPI>());
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -747,7 +773,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue
     const int quarter = warp & 3;
-    const uint32_t stage_base = base + L::kEpiOff + (warp - 2) * kEpiBufs * kEpiBufBytes;
+    const int part = (warp - 2) / 4;
+    const uint32_t stage_base = base + L::kEpiOff + (warp - 2) * epi_bufs<EPI>() * kEpiBufBytes;
     Schedule sched(args, blockIdx.x, gridDim.x);
     Segment sg;
     uint32_t sbuf = 0;
@@ -766,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (EPI != kEpiI32) sxr = row0 + lane < args.m ? __ldg(args.sx + row0 + lane) : 0.f;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
       epilogue_segment<EPI>(args, &tm_c, sg, taddr, row0, nb * kBN, sxr, stage_base, sbuf, lane,
-                            kEpiWarps, [&] { mbar_arrive(tempty_bar(acc)); });
+                            epi_warps<EPI>(), part, [&] { mbar_arrive(tempty_bar(acc)); });
     }
     if (lane == 0) bulk_wait_group<0>();
   }
@@ -884,7 +911,7 @@ static int pair_capacity(int device, int* out) {
     if (st != W8_OK) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sms & ~1, 1, 1);
-    cfg.blockDim = dim3(w8::kThreads, 1, 1);
+    cfg.blockDim = dim3(w8::threads_for<EPI>(), 1, 1);
     cfg.dynamicSmemBytes = w8::PairSmem::kAlloc;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
@@ -905,11 +932,11 @@ static int pair_capacity(int device, int* out) {
 // previous kernel on the stream drains; it waits (griddepcontrol.wait) before touching
 // global memory, so only its launch and prologue overlap.
 template <typename Kernel>
-static int launch_pdl(Kernel kern, int grid, int smem, cudaStream_t stream, const CUtensorMap& ta,
+static int launch_pdl(Kernel kern, int grid, int threads, int smem, cudaStream_t stream, const CUtensorMap& ta,
                       const CUtensorMap& tb, const CUtensorMap& tc, const w8::GemmArgs& args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(w8::kThreads, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr;
@@ -944,7 +971,7 @@ static int launch_pair(int device, const CUtensorMap& ta, const CUtensorMap& tb,
     workers = static_cast<int>(units < cap ? units : cap);
     args.stream_k = 1;
   }
-  return launch_pdl(kern, 2 * workers, w8::PairSmem::kAlloc, stream, ta, tb, tc, args);
+  return launch_pdl(kern, 2 * workers, w8::threads_for<EPI>(), w8::PairSmem::kAlloc, stream, ta, tb, tc, args);
 }
 
 template <bool B_MN, int EPI>
@@ -966,7 +993,7 @@ static int launch_single(int device, const CUtensorMap& ta, const CUtensorMap& t
     workers = static_cast<int>(units < sms ? units : sms);
     args.stream_k = 1;
   }
-  return launch_pdl(kern, workers, w8::SingleSmem::kAlloc, stream, ta, tb, tc, args);
+  return launch_pdl(kern, workers, w8::threads_for<EPI>(), w8::SingleSmem::kAlloc, stream, ta, tb, tc, args);
 }
 
 static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,

@@ -6,11 +6,13 @@ everything before the quant into the GEMM epilogue and finishes with a row quant
 oracle restatement (oracle/w8a8_numpy.gelu_up_quant) is pinned bit-exactly to the
 reference's own function by tests/golden/gelu_up.npz.
 
-Tolerance: gelu's tanh is CUDA's tanhf against numpy's, so an element of the bf16
-activation may differ by one bf16 step, which can move its int8 code by one.  So:
-|q - q_ref| <= 1 everywhere with at most 0.5 % of codes different, the bf16 activation
-within one bf16 step (relative 2^-7), and the row scales within max-rel 1e-2 (the
-north-star bound for dequantised outputs).
+Tolerance: the kernel forms 1 + tanh(z) from hardware exp2 / reciprocal approximations
+(relative error a few 2^-23) where the oracle calls numpy's tanh, so an element of the
+bf16 activation may differ by one bf16 step, which can move its int8 code by one.  So:
+|q - q_ref| <= 1 everywhere with at most 0.5 % of codes different; the bf16 activation
+within one bf16 step (relative 2^-7) plus an absolute 1e-6 of its row's absmax (the
+deep negative tail of gelu, where both sides are within 1e-6 of zero); and the row
+scales within max-rel 1e-2 (the north-star bound for dequantised outputs).
 """
 import numpy as np
 import pytest
@@ -36,7 +38,8 @@ def _check(q, s, y, rows, a_ref, q_ref, s_ref):
     assert qd.max() <= 1
     assert (qd != 0).mean() <= 5e-3
     yv = y[rows].float().cpu().numpy()
-    assert np.all(np.abs(yv - a_ref) <= np.abs(a_ref) * 2.0 ** -7 + 1e-30)
+    floor = 1e-6 * np.abs(a_ref).max(axis=1, keepdims=True)  # far below one int8 step of the row
+    assert np.all(np.abs(yv - a_ref) <= np.abs(a_ref) * 2.0 ** -7 + floor)
     sv = s[rows].cpu().numpy()
     assert float(np.abs(sv - s_ref).max() / max(np.abs(s_ref).max(), 1e-30)) <= 1e-2
 
