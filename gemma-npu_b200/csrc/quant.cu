@@ -32,8 +32,18 @@ __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
   return __bfloat162float(v);
 }
 
-__device__ __forceinline__ int8_t quant_one(float v, float s) {
-  float q = rintf(__fdiv_rn(v, s));
+// x / s correctly rounded, from r = RN(1/s) (one IEEE reciprocal per row): the product
+// t = RN(x * r) is within one ulp of x / s, the residual x - s * t is exact in one FMA,
+// and one more FMA t + r * residual rounds to RN(x / s) (P. Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1),
+// 1990; no over- or underflow here: s >= 1e-8 / 127 and |x / s| <= 127).
+__device__ __forceinline__ float div_rn_by(float x, float s, float r) {
+  const float t = __fmul_rn(x, r);
+  return __fmaf_rn(__fmaf_rn(-s, t, x), r, t);
+}
+
+__device__ __forceinline__ int8_t quant_one(float v, float s, float r) {
+  float q = rintf(div_rn_by(v, s, r));
   q = fminf(fmaxf(q, -127.f), 127.f);
   return static_cast<int8_t>(static_cast<int>(q));
 }
@@ -111,6 +121,7 @@ __global__ void __launch_bounds__(kQuantThreads)
 #pragma unroll
   for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, red[w]);
   const float sc = __fdiv_rn(fmaxf(amax, 1e-8f), 127.f);
+  const float rc = __frcp_rn(sc);
   if (threadIdx.x == 0) s[row] = sc;
 
 #pragma unroll
@@ -119,7 +130,7 @@ __global__ void __launch_bounds__(kQuantThreads)
     if (vi < nvec) {
       int8_t out[VEC];
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) out[e] = quant_one(to_f32(held[i].v[e]), sc);
+      for (int e = 0; e < VEC; ++e) out[e] = quant_one(to_f32(held[i].v[e]), sc, rc);
       store_q<VEC>(qr + static_cast<int64_t>(vi) * VEC, out);
     }
   }
@@ -127,7 +138,7 @@ __global__ void __launch_bounds__(kQuantThreads)
     const Vec<T, VEC> v = load_vec<T, VEC>(xr + static_cast<int64_t>(vi) * VEC);
     int8_t out[VEC];
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) out[e] = quant_one(to_f32(v.v[e]), sc);
+    for (int e = 0; e < VEC; ++e) out[e] = quant_one(to_f32(v.v[e]), sc, rc);
     store_q<VEC>(qr + static_cast<int64_t>(vi) * VEC, out);
   }
 }
@@ -168,24 +179,44 @@ __global__ void __launch_bounds__(256)
 // when the row absmax is already known: the fused GEMM epilogue folded it into
 // absmax[row] (fp32 bits, atomicMax).  s = max(absmax, 1e-8) / 127 and q exactly as in
 // quant_rows_kernel; absmax[row] is reset to zero for the next call.  One CTA per row,
-// 8 bf16 per thread step (16-byte loads, 8-byte stores).
+// 8 bf16 per thread step (16-byte loads, 8-byte stores); the row's loads are issued
+// before the absmax word is read, so the two latencies overlap.
 __global__ void __launch_bounds__(kQuantThreads)
     quant_absmax_kernel(const __nv_bfloat16* __restrict__ y, int64_t ldy, float* __restrict__ absmax,
                         int8_t* __restrict__ q, int64_t ldq, float* __restrict__ s, int k) {
   const int row = blockIdx.x;
+  const __nv_bfloat16* yr = y + static_cast<int64_t>(row) * ldy;
+  int8_t* qr = q + static_cast<int64_t>(row) * ldq;
+  const int nvec = k / 8;
+  Vec<__nv_bfloat16, 8> held[kQuantMaxVecs];
+#pragma unroll
+  for (int i = 0; i < kQuantMaxVecs; ++i) {
+    const int vi = threadIdx.x + i * kQuantThreads;
+    if (vi < nvec) held[i] = load_vec<__nv_bfloat16, 8>(yr + vi * 8);
+  }
   const float sc = __fdiv_rn(fmaxf(absmax[row], 1e-8f), 127.f);
+  const float rc = __frcp_rn(sc);
   __syncthreads();  // every thread has read absmax[row]
   if (threadIdx.x == 0) {
     s[row] = sc;
     absmax[row] = 0.f;
   }
-  const __nv_bfloat16* yr = y + static_cast<int64_t>(row) * ldy;
-  int8_t* qr = q + static_cast<int64_t>(row) * ldq;
-  for (int vi = threadIdx.x; vi < k / 8; vi += kQuantThreads) {
+#pragma unroll
+  for (int i = 0; i < kQuantMaxVecs; ++i) {
+    const int vi = threadIdx.x + i * kQuantThreads;
+    if (vi < nvec) {
+      int8_t out[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) out[e] = quant_one(__bfloat162float(held[i].v[e]), sc, rc);
+      store_q<8>(qr + vi * 8, out);
+    }
+  }
+  // Rows longer than the register window: the rest streams through.
+  for (int vi = threadIdx.x + kQuantMaxVecs * kQuantThreads; vi < nvec; vi += kQuantThreads) {
     const Vec<__nv_bfloat16, 8> v = load_vec<__nv_bfloat16, 8>(yr + vi * 8);
     int8_t out[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) out[e] = quant_one(__bfloat162float(v.v[e]), sc);
+    for (int e = 0; e < 8; ++e) out[e] = quant_one(__bfloat162float(v.v[e]), sc, rc);
     store_q<8>(qr + vi * 8, out);
   }
 }

@@ -94,3 +94,35 @@ def test_fused_dequant_equals_mm_then_dequant(cuda, m, n, k):
     want = ref.dequant(ref.int_mm(xq[rows].cpu().numpy(), wq.t().cpu().numpy()), sx[rows].cpu().numpy(),
                        sw.cpu().numpy())
     np.testing.assert_array_equal(bits(y[rows]), want)
+
+
+def _near_ties(rows, k, seed):
+    """fp32 rows whose quotients x / s sit on and next to the half-integers k + 0.5, where a
+    division one ulp off would change round-half-even: row r has absmax 127 * s0 (so its
+    scale s is s0 up to rounding) and its other entries are (j + 0.5) * s0 nudged by
+    -2..2 ulps, over scales s0 spread across 40 binades."""
+    rng = np.random.default_rng(seed)
+    s0 = (2.0 ** rng.uniform(-30, 10, size=(rows, 1))).astype(np.float32)
+    j = rng.integers(-127, 127, size=(rows, k)).astype(np.float32)
+    x = ((j + np.float32(0.5)) * s0).astype(np.float32)
+    nudge = rng.integers(-2, 3, size=(rows, k)).astype(np.int32)
+    x = (x.view(np.int32) + nudge).view(np.float32)
+    x[:, 0] = np.float32(127) * s0[:, 0]
+    x[:, 1] = -np.float32(127) * s0[:, 0]
+    return x
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_quant_division_is_correctly_rounded(cuda, seed):
+    """The kernels divide with a reciprocal and one correction step; the int8 codes must
+    equal those of an IEEE division (numpy) bit for bit, on near-tie quotients and on
+    random rows, for fp32 and bf16 input."""
+    x = _near_ties(1024, 2048, seed)
+    rng = np.random.default_rng(seed + 10)
+    x = np.concatenate([x, (rng.standard_normal((1024, 2048)) * 2.0 ** rng.uniform(-20, 20, (1024, 1)))
+                        .astype(np.float32)])
+    for t in (torch.from_numpy(x).to(cuda), torch.from_numpy(x).to(cuda).to(torch.bfloat16)):
+        q, s = w8.quant_rows(t)
+        qr, sr = ref.quant_rows(t.float().cpu().numpy())
+        np.testing.assert_array_equal(s.cpu().numpy().view(np.uint32), sr.view(np.uint32))
+        np.testing.assert_array_equal(q.cpu().numpy(), qr)
