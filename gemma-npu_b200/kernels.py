@@ -9,6 +9,9 @@ quant/dequant glue of `pipeline.py` / `gemma_npu.py`:
     dequant(acc, sx, sw)         pipeline.py:55-57, gemma_npu.py:45-47
     int8_linear(x, wq, sw)       gemma_npu.py:155-156   (torch._weight_int8pack_mm)
     gelu_up_quant(x, sx, w, sw)  pipeline.py:102-107   (k_gelu fused onto the gate/up GEMM)
+    rms_quant(h, w, eps)         pipeline.py:66-69     (k_in)
+    post_norm_quant(y, res, ..)  pipeline.py:95-99, 110-114 (k_post_attn / k_post_ff)
+    attn_out_quant(o)            pipeline.py:88-92     (k_attn_out)
 
 Every function validates dtype/shape/layout on the host, passes raw device
 pointers and torch's current CUDA stream to the C ABI, and raises a W8Error
@@ -210,6 +213,71 @@ def gelu_up_quant(x, sx, w_packed, sw_packed, q=None, s=None, y=None):
     _lib.call("w8_gemm_gelu_up_quant", x.data_ptr(), _ld(x), w_packed.data_ptr(), _ld(w_packed),
               sx.data_ptr(), sw_packed.data_ptr(), T, inter, K, y.data_ptr(), _ld(y), absmax.data_ptr(),
               q.data_ptr(), _ld(q), s.data_ptr(), stream)
+    return q, s
+
+
+def _bf16_rows(t, name, n=None):
+    _check_matrix(t, name, torch.bfloat16)
+    if n is not None:
+        _need(t.shape[1] == n, f"{name} must have {n} columns (got {t.shape[1]})")
+
+
+def _bf16_vec(t, name, n):
+    _check_vector(t, name, torch.bfloat16, n)
+
+
+def rms_quant(h, w, eps, q=None, s=None):
+    """k_in (pipeline.py:66-69): (q int8 [T, N], s fp32 [T]) = _quant(bf16(_rms(h, w, eps))).
+
+    h bf16 [T, N] (N <= 2048, N % 8 == 0), w bf16 [N] (the input_layernorm weight)."""
+    _bf16_rows(h, "h")
+    T, N = h.shape
+    _bf16_vec(w, "w", N)
+    q = torch.empty((T, N), dtype=torch.int8, device=h.device) if q is None else q
+    s = torch.empty((T,), dtype=torch.float32, device=h.device) if s is None else s
+    _check_matrix(q, "q", torch.int8)
+    _check_vector(s, "s", torch.float32, T)
+    _lib.call("w8_rms_quant_bf16", h.data_ptr(), _ld(h), w.data_ptr(), float(eps), q.data_ptr(), _ld(q),
+              s.data_ptr(), T, N, _stream(h))
+    return q, s
+
+
+def post_norm_quant(y, res, w1, w2, eps, h=None, q=None, s=None):
+    """The glue after the o / down GEMMs, on y = the GEMM's dequantised bf16 output:
+    h = bf16(res + bf16(_rms(y, w1))); with w2 (k_post_attn, pipeline.py:95-99)
+    q, s = _quant(bf16(_rms(h, w2))), without (k_post_ff, pipeline.py:110-114) q, s = _quant(h).
+    Returns (h, q, s); `h` may be `res` itself (in-place residual update)."""
+    _bf16_rows(y, "y")
+    T, N = y.shape
+    _bf16_rows(res, "res", N)
+    _need(res.shape[0] == T, "res must have the rows of y")
+    _bf16_vec(w1, "w1", N)
+    if w2 is not None:
+        _bf16_vec(w2, "w2", N)
+    h = torch.empty((T, N), dtype=torch.bfloat16, device=y.device) if h is None else h
+    q = torch.empty((T, N), dtype=torch.int8, device=y.device) if q is None else q
+    s = torch.empty((T,), dtype=torch.float32, device=y.device) if s is None else s
+    _bf16_rows(h, "h", N)
+    _check_matrix(q, "q", torch.int8)
+    _check_vector(s, "s", torch.float32, T)
+    _lib.call("w8_post_norm_quant_bf16", y.data_ptr(), _ld(y), res.data_ptr(), _ld(res), w1.data_ptr(),
+              None if w2 is None else w2.data_ptr(), float(eps), h.data_ptr(), _ld(h), q.data_ptr(), _ld(q),
+              s.data_ptr(), T, N, _stream(y))
+    return h, q, s
+
+
+def attn_out_quant(o, q=None, s=None):
+    """k_attn_out (pipeline.py:88-92): o bf16 [H, T, D] -> _quant of its [T, H*D] rows."""
+    _need(isinstance(o, torch.Tensor) and o.is_cuda and o.dtype == torch.bfloat16 and o.dim() == 3,
+          "o must be a bf16 CUDA tensor [H, T, D]")
+    _need(o.stride(2) == 1, "o must have unit stride along D")
+    H, T, D = o.shape
+    q = torch.empty((T, H * D), dtype=torch.int8, device=o.device) if q is None else q
+    s = torch.empty((T,), dtype=torch.float32, device=o.device) if s is None else s
+    _check_matrix(q, "q", torch.int8)
+    _check_vector(s, "s", torch.float32, T)
+    _lib.call("w8_attn_out_quant_bf16", o.data_ptr(), o.stride(0), o.stride(1), q.data_ptr(), _ld(q), s.data_ptr(),
+              T, H, D, _stream(o))
     return q, s
 
 

@@ -21,6 +21,9 @@
  *   w8_lm_head_f32          gemma_npu.py:170-172 (Int8Head.forward) + pipeline.py:335-338 (softcap)
  *   w8_gemm_gelu_up_quant   pipeline.py:102-107 (k_gelu) fused onto the gate/up GEMM of
  *                           pipeline.py:233-242 (Prefill.gemm)
+ *   w8_rms_quant_bf16       pipeline.py:66-69 (k_in)
+ *   w8_post_norm_quant_bf16 pipeline.py:95-99 (k_post_attn), :110-114 (k_post_ff)
+ *   w8_attn_out_quant_bf16  pipeline.py:88-92 (k_attn_out)
  */
 #ifndef W8A8_B200_H
 #define W8A8_B200_H
@@ -125,6 +128,34 @@ int w8_gemm_gelu_up_quant(const int8_t* a, int64_t lda, const int8_t* w, int64_t
                           const float* sx, const float* sw, int64_t m, int64_t inter, int64_t k,
                           uint16_t* y_out, int64_t ldy, float* row_absmax, int8_t* q, int64_t ldq,
                           float* s, w8_stream_t stream);
+
+/* ---- the RMSNorm / residual glue around the GEMMs (bf16 rows) ------------
+ * One warp per row, the row held in registers: row length n <= 2048, n % 8 == 0, rows
+ * and norm weights 16-byte aligned, pitches in elements % 8 == 0, q 8-byte aligned.
+ * _rms (pipeline.py:43-46) is fp32 x * pow(mean(x^2) + eps, -0.5) * w with the mean
+ * summed in a different order than ATen's, so a bf16 output may differ from the
+ * reference by one bf16 step and an int8 code by one. */
+
+/* k_in (pipeline.py:66-69): q, s = _quant(bf16(_rms(h, w))). */
+int w8_rms_quant_bf16(const uint16_t* h, int64_t ldh, const uint16_t* w, float eps, int8_t* q,
+                      int64_t ldq, float* s, int64_t t, int64_t n, w8_stream_t stream);
+
+/* After the o or down GEMM with the dequant fused (y = w8_gemm_dequant_bf16 output):
+ *   h = bf16(res + bf16(_rms(y, w1)))                          written to h
+ *   w2 != NULL: q, s = _quant(bf16(_rms(h, w2)))   (k_post_attn, pipeline.py:95-99)
+ *   w2 == NULL: q, s = _quant(h)                   (k_post_ff, pipeline.py:110-114)
+ * h may alias res (in-place residual update); it must not alias y. */
+int w8_post_norm_quant_bf16(const uint16_t* y, int64_t ldy, const uint16_t* res, int64_t ldr,
+                            const uint16_t* w1, const uint16_t* w2, float eps, uint16_t* h,
+                            int64_t ldh, int8_t* q, int64_t ldq, float* s, int64_t t, int64_t n,
+                            w8_stream_t stream);
+
+/* k_attn_out (pipeline.py:88-92): the attention output o [H, T, D] (bf16; element
+ * (h, t, d) at o[h * ld_head + t * ld_tok + d]) quantised per token over its H * D
+ * values: q [T, H * D] int8, s [T] fp32.  Bit-exact (no reduction but the absmax). */
+int w8_attn_out_quant_bf16(const uint16_t* o, int64_t ld_head, int64_t ld_tok, int8_t* q,
+                           int64_t ldq, float* s, int64_t t, int64_t heads, int64_t head_dim,
+                           w8_stream_t stream);
 
 /* ---- quantisation ------------------------------------------------------ */
 

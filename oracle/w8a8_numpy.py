@@ -106,3 +106,66 @@ def gelu_up_quant(acc, sx, sw, inter):
     g, u = y[:, :inter], y[:, inter:]
     a = bf16_bits_to_f32(f32_to_bf16_bits((gelu_tanh_bf16(g) * u).astype(np.float32)))
     return quant_rows(a)
+
+
+def bf16_round(x):
+    """float32 values rounded to bf16 (RNE) and returned as float32."""
+    return bf16_bits_to_f32(f32_to_bf16_bits(np.asarray(x, dtype=np.float32)))
+
+
+def rms(x, w, eps):
+    """_rms (pipeline.py:43-46): x * (mean(x^2) + eps)^-0.5 [* w], fp32 out, unrounded to bf16.
+
+    The mean is accumulated in float64 and rounded to fp32 (ATen's fp32 sum order is not
+    reproduced: the last bit of the mean may differ), then pow(., -0.5) = rsqrt in fp32.
+    """
+    x = np.asarray(x, dtype=np.float32)
+    ms = (x.astype(np.float64) ** 2).mean(axis=-1, keepdims=True).astype(np.float32)
+    r = (1.0 / np.sqrt((ms + np.float32(eps)).astype(np.float64))).astype(np.float32)
+    y = (x * r).astype(np.float32)
+    return (y * np.asarray(w, dtype=np.float32)).astype(np.float32) if w is not None else y
+
+
+def rope(x, cos, sin):
+    """_rope (pipeline.py:60-63) on bf16 values: x * cos + rotate_half(x) * sin, each bf16 op
+    rounded to bf16 as eager torch does."""
+    half = x.shape[-1] // 2
+    rot = np.concatenate([-x[..., half:], x[..., :half]], axis=-1)
+    return bf16_round(bf16_round(x * cos) + bf16_round(rot * sin))
+
+
+def k_in(h, w, eps):
+    """k_in (pipeline.py:66-69): _quant(bf16(_rms(h, w)))."""
+    return quant_rows(bf16_round(rms(h, w, eps)))
+
+
+def k_post(y, res, w1, w2, eps):
+    """k_post_attn (pipeline.py:95-99; w2 given) and k_post_ff (pipeline.py:110-114; w2 None)
+    after the dequant: h = bf16(res + bf16(_rms(y, w1))); q, s = _quant(bf16(_rms(h, w2)) or h)."""
+    h = bf16_round(np.asarray(res, np.float32) + bf16_round(rms(y, w1, eps)))
+    t = bf16_round(rms(h, w2, eps)) if w2 is not None else h
+    q, s = quant_rows(t)
+    return h, q, s
+
+
+def k_attn_out(o):
+    """k_attn_out (pipeline.py:88-92): o [H, T, D] -> _quant of the [T, H*D] rows."""
+    o = np.asarray(o, np.float32)
+    nh, t, d = o.shape
+    return quant_rows(o.transpose(1, 0, 2).reshape(t, nh * d))
+
+
+def k_qkv(acc, sx, sw, cos, sin, qw, kw, eps, nh, kv, d, shared):
+    """k_qkv (pipeline.py:72-86): dequant, per-head _rms with q_norm / k_norm (v: no
+    weight), RoPE on q and k; returns q [H, T, D], k, v [KV, T, D] as bf16 values."""
+    y = bf16_bits_to_f32(dequant(acc, sx, sw))
+    t = y.shape[0]
+    cos, sin = np.asarray(cos, np.float32)[:, None], np.asarray(sin, np.float32)[:, None]
+    q = rope(bf16_round(rms(y[:, : nh * d].reshape(t, nh, d), qw, eps)), cos, sin).transpose(1, 0, 2)
+    if shared:
+        return q, q, q
+    k = y[:, nh * d: (nh + kv) * d].reshape(t, kv, d)
+    v = y[:, (nh + kv) * d:].reshape(t, kv, d)
+    k = rope(bf16_round(rms(k, kw, eps)), cos, sin).transpose(1, 0, 2)
+    v = bf16_round(rms(v, None, eps)).transpose(1, 0, 2)
+    return q, k, v

@@ -13,6 +13,8 @@ repository) and records, on seeded inputs:
   gemv      gemma_npu.cpu_int8_linear (gemma_npu.py:155-156), T = 1 and T = 3
   head      gemma_npu.Int8Head.forward + the softcap of pipeline.py:335-338
   gelu_up   pipeline.k_gelu (pipeline.py:102-107): dequant, gelu_tanh(gate) * up, int8 quant
+  k_in, k_post_attn, k_post_ff, k_attn_out, k_qkv(_shared)
+            the RMSNorm / residual / RoPE glue of pipeline.py:66-99, 110-114 (eager bodies)
 
 The weight of the GEMM, GEMV and head cases is the one stored in wquant.npz
 (q [N,K] int8, s bf16 [N]); the GEMM's B operand is its transpose.  The outputs
@@ -116,6 +118,55 @@ def main(ref_dir):
     gq, gs = k_gelu(gacc, gsx, gsw, gi)
     out["gelu_up"] = dict(x=gx.numpy(), w=gwq.numpy(), acc=gacc.numpy(), sx=gsx.numpy(), sw=gsw.numpy(),
                           inter=np.int32(gi), q=gq.numpy(), s=gs.numpy())
+
+    # ---- the norm / RoPE glue around the other GEMMs (pipeline.py:66-99, 110-114), eager
+    def eager(f):
+        return getattr(f, "_torchdynamo_orig_callable", f)
+
+    eps = 1e-6
+    nt, nn = 16, 512
+
+    def norm_w(n):
+        return (1.0 + 0.1 * torch.randn(n)).to(torch.bfloat16)
+
+    def gemm_out(t, n, k=256):
+        xq, sx_ = pipeline._quant(torch.randn(t, k).to(torch.bfloat16))
+        wf = torch.randn(n, k) * 0.02
+        sw_ = wf.abs().amax(dim=1).clamp(min=1e-8) / 127
+        wq_ = torch.round(wf / sw_[:, None]).clamp(-127, 127).to(torch.int8)
+        return torch._int_mm(xq, wq_.t().contiguous()), sx_, sw_
+
+    hin = (torch.randn(nt, nn) * 2).to(torch.bfloat16)
+    w_in = norm_w(nn)
+    q_, s_ = eager(pipeline.k_in)(hin, w_in, eps)
+    out["k_in"] = dict(h=bf16_bits(hin), w=bf16_bits(w_in), eps=np.float32(eps), q=q_.numpy(), s=s_.numpy())
+
+    acc, sxa, swa = gemm_out(nt, nn)
+    res = torch.randn(nt, nn).to(torch.bfloat16)
+    w1, w2 = norm_w(nn), norm_w(nn)
+    h_, q_, s_ = eager(pipeline.k_post_attn)(acc, sxa, swa, res, w1, w2, eps)
+    out["k_post_attn"] = dict(acc=acc.numpy(), sx=sxa.numpy(), sw=swa.numpy(), res=bf16_bits(res), w1=bf16_bits(w1),
+                              w2=bf16_bits(w2), eps=np.float32(eps), h=bf16_bits(h_), q=q_.numpy(), s=s_.numpy())
+    h_, q_, s_ = eager(pipeline.k_post_ff)(acc, sxa, swa, res, w1, eps)
+    out["k_post_ff"] = dict(acc=acc.numpy(), sx=sxa.numpy(), sw=swa.numpy(), res=bf16_bits(res), w1=bf16_bits(w1),
+                            eps=np.float32(eps), h=bf16_bits(h_), q=q_.numpy(), s=s_.numpy())
+
+    o = torch.randn(4, nt, 64).to(torch.bfloat16)
+    q_, s_ = eager(pipeline.k_attn_out)(o)
+    out["k_attn_out"] = dict(o=bf16_bits(o), q=q_.numpy(), s=s_.numpy())
+
+    nh, kv, hd = 2, 1, 64
+    acc, sxa, swa = gemm_out(nt, (nh + 2 * kv) * hd)
+    ang = torch.arange(nt)[:, None].float() * (10000.0 ** (-torch.arange(0, hd, 2).float() / hd))[None]
+    ang = torch.cat([ang, ang], dim=-1)
+    cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    qw, kw = norm_w(hd), norm_w(hd)
+    for shared in (False, True):
+        qq, kk, vv = eager(pipeline.k_qkv)(acc, sxa, swa, cos, sin, qw, None if shared else kw, eps, nh, kv, hd, shared)
+        out[f"k_qkv{'_shared' if shared else ''}"] = dict(
+            acc=acc.numpy(), sx=sxa.numpy(), sw=swa.numpy(), cos=bf16_bits(cos), sin=bf16_bits(sin), qw=bf16_bits(qw),
+            kw=bf16_bits(kw), eps=np.float32(eps), dims=np.array([nh, kv, hd, int(shared)], np.int32),
+            q=bf16_bits(qq), k=bf16_bits(kk), v=bf16_bits(vv))
 
     for name, arrays in out.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)

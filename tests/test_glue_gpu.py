@@ -1,0 +1,120 @@
+"""The RMSNorm / residual / quant glue (k_in, k_post_attn, k_post_ff, k_attn_out of
+pipeline.py:66-99, 110-114) on the GPU against the oracle and the reference's own outputs.
+
+The oracle restatements (oracle/w8a8_numpy.k_in / k_post / k_attn_out) reproduce the
+reference's eager functions bit for bit on tests/golden/k_*.npz.  The kernels sum
+mean(x^2) in another order than ATen, so the last bit of a mean can differ: a bf16
+output may move by one bf16 step (relative 2^-7; for h = res + t one step of t) and an
+int8 code by one, on at most 1 % of the elements; scales within relative 2^-7.  k_attn_out has no reduction but the
+absmax and is bit-exact.
+"""
+import numpy as np
+import pytest
+import torch
+
+import gemma_npu_b200 as w8
+from oracle import w8a8_numpy as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def bf16(bits, dev):
+    return torch.from_numpy(bits.astype(np.uint16).view(np.int16)).view(torch.bfloat16).to(dev)
+
+
+def bits(t):
+    return t.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def close_bf16(a_bits, b_bits, frac=1e-2, res=None):
+    """Within one bf16 step.  For h = bf16(res + t) the step is t's: when res and t nearly
+    cancel, one step of t is large next to h, so the bound is 2^-7 (|h| + |res|)."""
+    a, b = ref.bf16_bits_to_f32(a_bits), ref.bf16_bits_to_f32(b_bits)
+    d = np.abs(a - b)
+    scale = np.abs(b) if res is None else np.abs(b) + np.abs(np.asarray(res, np.float32))
+    assert np.all(d <= scale * 2.0 ** -7 + 1e-30)
+    assert (d != 0).mean() <= frac
+
+
+def close_q(q, q_ref, frac=1e-2):
+    d = np.abs(q.astype(np.int32) - q_ref.astype(np.int32))
+    assert d.max() <= 1 and (d != 0).mean() <= frac
+
+
+def test_golden_k_in(cuda, golden):
+    g = golden("k_in")
+    q, s = w8.rms_quant(bf16(g["h"], cuda), bf16(g["w"], cuda), float(g["eps"]))
+    close_q(q.cpu().numpy(), g["q"])
+    np.testing.assert_allclose(s.cpu().numpy(), g["s"], rtol=2.0 ** -7)
+
+
+@pytest.mark.parametrize("name", ["k_post_attn", "k_post_ff"])
+def test_golden_k_post(cuda, golden, name):
+    g = golden(name)
+    acc = torch.from_numpy(g["acc"]).to(cuda)
+    y = w8.dequant(acc, torch.from_numpy(g["sx"]).to(cuda), torch.from_numpy(g["sw"]).to(cuda))
+    w2 = bf16(g["w2"], cuda) if "w2" in g else None
+    h, q, s = w8.post_norm_quant(y, bf16(g["res"], cuda), bf16(g["w1"], cuda), w2, float(g["eps"]))
+    close_bf16(bits(h), g["h"], res=ref.bf16_bits_to_f32(g["res"]))
+    close_q(q.cpu().numpy(), g["q"])
+    np.testing.assert_allclose(s.cpu().numpy(), g["s"], rtol=2.0 ** -7)
+
+
+def test_golden_k_attn_out_bit_exact(cuda, golden):
+    g = golden("k_attn_out")
+    q, s = w8.attn_out_quant(bf16(g["o"], cuda))
+    np.testing.assert_array_equal(q.cpu().numpy(), g["q"])
+    np.testing.assert_array_equal(s.cpu().numpy(), g["s"])
+
+
+def _rows(t, seed):
+    return sorted({0, t - 1} | set(torch.randint(0, t, (62,), generator=torch.Generator().manual_seed(seed)).tolist()))
+
+
+@pytest.mark.parametrize("t,n", [(3658, 1536), (207, 2048), (5, 8)])
+def test_k_in_matches_oracle(cuda, t, n):
+    gen = torch.Generator(device=cuda).manual_seed(t + n)
+    h = (torch.randn((t, n), device=cuda, generator=gen) * 3).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn((n,), device=cuda, generator=gen)).to(torch.bfloat16)
+    q, s = w8.rms_quant(h, w, 1e-6)
+    rows = _rows(t, n)
+    qr, sr = ref.k_in(h[rows].float().cpu().numpy(), w.float().cpu().numpy(), 1e-6)
+    close_q(q[rows].cpu().numpy(), qr)
+    np.testing.assert_allclose(s[rows].cpu().numpy(), sr, rtol=2.0 ** -7)
+
+
+@pytest.mark.parametrize("two", [True, False])
+@pytest.mark.parametrize("t,n", [(3658, 1536), (300, 512)])
+def test_gemm_then_post_norm_matches_oracle(cuda, t, n, two):
+    """o / down GEMM with the dequant fused, then k_post_attn (two) or k_post_ff glue."""
+    k = 2048
+    gen = torch.Generator(device=cuda).manual_seed(t + n + two)
+    x, sx = w8.quant_rows(torch.randn((t, k), device=cuda, generator=gen, dtype=torch.bfloat16))
+    wq, sw = w8.quant_rows(torch.randn((n, k), device=cuda, generator=gen, dtype=torch.bfloat16) * 0.02)
+    res = torch.randn((t, n), device=cuda, generator=gen).to(torch.bfloat16)
+    w1 = (1 + 0.1 * torch.randn((n,), device=cuda, generator=gen)).to(torch.bfloat16)
+    w2 = (1 + 0.1 * torch.randn((n,), device=cuda, generator=gen)).to(torch.bfloat16) if two else None
+    y = w8.gemm_dequant(x, wq, sx, sw)
+    res0 = res.clone()
+    h, q, s = w8.post_norm_quant(y, res, w1, w2, 1e-6, h=res)  # in place, as the residual stream
+    assert h.data_ptr() == res.data_ptr()
+    rows = _rows(t, n)
+    acc = ref.int_mm(x[rows].cpu().numpy(), wq.t().cpu().numpy())
+    yr = ref.bf16_bits_to_f32(ref.dequant(acc, sx[rows].cpu().numpy(), sw.cpu().numpy()))
+    hr, qr, sr = ref.k_post(yr, res0[rows].float().cpu().numpy(), w1.float().cpu().numpy(),
+                            None if w2 is None else w2.float().cpu().numpy(), 1e-6)
+    close_bf16(bits(h[rows]), ref.f32_to_bf16_bits(hr), res=res0[rows].float().cpu().numpy())
+    close_q(q[rows].cpu().numpy(), qr)
+    np.testing.assert_allclose(s[rows].cpu().numpy(), sr, rtol=2.0 ** -7)
+
+
+def test_attn_out_strided_bit_exact(cuda):
+    """o as attention produces it ([H, T, D], here a slice of a wider buffer)."""
+    H, T, D = 8, 1000, 256
+    gen = torch.Generator(device=cuda).manual_seed(3)
+    big = torch.randn((H, T + 24, D), device=cuda, generator=gen).to(torch.bfloat16)
+    o = big[:, 10:10 + T]
+    q, s = w8.attn_out_quant(o)
+    qr, sr = ref.k_attn_out(o.float().cpu().numpy())
+    np.testing.assert_array_equal(q.cpu().numpy(), qr)
+    np.testing.assert_array_equal(s.cpu().numpy(), sr)

@@ -109,3 +109,54 @@ def test_gelu_up_quant_bit_exact(golden):
     q, s = ref.gelu_up_quant(g["acc"], g["sx"], g["sw"], int(g["inter"]))
     np.testing.assert_array_equal(q, g["q"])
     np.testing.assert_array_equal(s, g["s"])
+
+
+# The norm glue reduces mean(x^2) in fp32 in ATen's order (and takes pow(., -0.5) as
+# ATen's rsqrt); the oracle rounds an fp64 mean.  The last bit of the mean may differ,
+# so a bf16 output may move by one bf16 step and an int8 code by one.
+def _close_bf16(a_bits, b_bits, frac=1e-2):
+    a, b = ref.bf16_bits_to_f32(a_bits), ref.bf16_bits_to_f32(b_bits)
+    d = np.abs(a - b)
+    assert np.all(d <= np.abs(b) * 2.0 ** -7 + 1e-30)
+    assert (d != 0).mean() <= frac
+
+
+def _close_q(q, q_ref, frac=1e-2):
+    d = np.abs(q.astype(np.int32) - q_ref.astype(np.int32))
+    assert d.max() <= 1 and (d != 0).mean() <= frac
+
+
+def test_k_in(golden):
+    g = golden("k_in")
+    q, s = ref.k_in(ref.bf16_bits_to_f32(g["h"]), ref.bf16_bits_to_f32(g["w"]), float(g["eps"]))
+    _close_q(q, g["q"])
+    np.testing.assert_allclose(s, g["s"], rtol=2.0 ** -7)
+
+
+def test_k_post_attn_and_ff(golden):
+    for name in ("k_post_attn", "k_post_ff"):
+        g = golden(name)
+        y = ref.bf16_bits_to_f32(ref.dequant(g["acc"], g["sx"], g["sw"]))
+        w2 = ref.bf16_bits_to_f32(g["w2"]) if "w2" in g else None
+        h, q, s = ref.k_post(y, ref.bf16_bits_to_f32(g["res"]), ref.bf16_bits_to_f32(g["w1"]), w2, float(g["eps"]))
+        _close_bf16(ref.f32_to_bf16_bits(h), g["h"])
+        _close_q(q, g["q"])
+        np.testing.assert_allclose(s, g["s"], rtol=2.0 ** -7)
+
+
+def test_k_attn_out_bit_exact(golden):
+    g = golden("k_attn_out")
+    q, s = ref.k_attn_out(ref.bf16_bits_to_f32(g["o"]))
+    np.testing.assert_array_equal(q, g["q"])
+    np.testing.assert_array_equal(s, g["s"])
+
+
+def test_k_qkv(golden):
+    for name in ("k_qkv", "k_qkv_shared"):
+        g = golden(name)
+        nh, kv, d, shared = (int(v) for v in g["dims"])
+        f = ref.bf16_bits_to_f32
+        q, k, v = ref.k_qkv(g["acc"], g["sx"], g["sw"], f(g["cos"]), f(g["sin"]), f(g["qw"]),
+                            None if shared else f(g["kw"]), float(g["eps"]), nh, kv, d, bool(shared))
+        for mine, theirs in ((q, g["q"]), (k, g["k"]), (v, g["v"])):
+            _close_bf16(ref.f32_to_bf16_bits(mine), theirs)
