@@ -365,6 +365,100 @@ def fused_gelu_up(w8, work, dev, stream, steps, warmup, world):
             "hbm_bytes_avoided_per_layer": 4 * m * n * 2 + 2 * m * n * 2}
 
 
+def _torch_rms(x, w, eps):
+    x = x.float()
+    y = x * torch.pow(x.pow(2).mean(-1, keepdim=True) + eps, -0.5)
+    return y * w.float() if w is not None else y
+
+
+def _torch_rope(x, cos, sin):
+    half = x.shape[-1] // 2
+    return x * cos + torch.cat((-x[..., half:], x[..., :half]), dim=-1) * sin
+
+
+def fused_layer(w8, dev, stream, m, steps, warmup, world, layers=35):
+    """SURVEY next row 1 across a whole decoder layer: the linear set with all of its glue
+    on the GPU (k_in, qkv + k_qkv, k_attn_out, o + k_post_attn, gate_up + k_gelu,
+    down + k_post_ff; pipeline.py:66-114), attention excluded (a synthetic o of the right
+    shape stands in).  Fused: dequant / gelu in the GEMM epilogues plus warp-per-row glue
+    kernels.  Unfused: int32 GEMMs, then the reference's glue expressions as torch ops on
+    the same GPU."""
+    eps, nh, kv, d, hid = 1e-6, 8, 1, 256, 1536
+    g = torch.Generator(device=dev).manual_seed(57)
+
+    def wq(n, k):
+        w, s_ = w8.quant_rows(torch.randn((n, k), device=dev, generator=g, dtype=torch.bfloat16) * 0.02)
+        return w, s_
+
+    def nw(n):
+        return (1 + 0.1 * torch.randn((n,), device=dev, generator=g)).to(torch.bfloat16)
+
+    L = []
+    for _ in range(layers):
+        qkv, o, gu, dn = wq((nh + 2 * kv) * d, hid), wq(hid, nh * d), wq(12288, hid), wq(hid, 6144)
+        gup = w8.pack_gelu_up(*gu)
+        L.append(dict(qkv=qkv, o=o, gu=gu, gup=gup, dn=dn, w_in=nw(hid), qn=nw(d), kn=nw(d), w_post=nw(hid),
+                      w_pre=nw(hid), w_pff=nw(hid)))
+    h0 = torch.randn((m, hid), device=dev, generator=g).to(torch.bfloat16)
+    ang = torch.arange(m, device=dev)[:, None].float() * (1e6 ** (-torch.arange(0, d, 2, device=dev).float() / d))[None]
+    ang = torch.cat([ang, ang], dim=-1)
+    cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    attn = torch.randn((nh, m, d), device=dev, generator=g).to(torch.bfloat16)  # stands in for attention
+    h = torch.empty_like(h0)
+    c_qkv = torch.empty((m, (nh + 2 * kv) * d), dtype=torch.int32, device=dev)
+    c_o = torch.empty((m, hid), dtype=torch.int32, device=dev)
+    c_gu = torch.empty((m, 12288), dtype=torch.int32, device=dev)
+    c_dn = torch.empty((m, hid), dtype=torch.int32, device=dev)
+
+    def fused():
+        h.copy_(h0)
+        for l in L:
+            xq, sx = w8.rms_quant(h, l["w_in"], eps)
+            y = w8.gemm_dequant(xq, l["qkv"][0], sx, l["qkv"][1])
+            w8.qkv_norm_rope(y, cos, sin, l["qn"], l["kn"], eps, nh, kv, d)
+            xq, sx = w8.attn_out_quant(attn)
+            y = w8.gemm_dequant(xq, l["o"][0], sx, l["o"][1])
+            _, xq, sx = w8.post_norm_quant(y, h, l["w_post"], l["w_pre"], eps, h=h)
+            xq, sx = w8.gelu_up_quant(xq, sx, *l["gup"])
+            y = w8.gemm_dequant(xq, l["dn"][0], sx, l["dn"][1])
+            w8.post_norm_quant(y, h, l["w_pff"], None, eps, h=h)
+
+    def unfused():
+        hh = h0
+        for l in L:
+            xq, sx = w8.quant_rows(_torch_rms(hh, l["w_in"], eps).to(torch.bfloat16))
+            w8.mm_i8_nk(xq, l["qkv"][0], c_qkv)
+            yq = w8.dequant(c_qkv, sx, l["qkv"][1])
+            q = yq[:, : nh * d].reshape(m, nh, d)
+            q = _torch_rope(_torch_rms(q, l["qn"], eps).to(torch.bfloat16), cos[:, None], sin[:, None]).transpose(0, 1)
+            k_ = yq[:, nh * d: (nh + kv) * d].reshape(m, kv, d)
+            k_ = _torch_rope(_torch_rms(k_, l["kn"], eps).to(torch.bfloat16), cos[:, None], sin[:, None]).transpose(0, 1)
+            v_ = _torch_rms(yq[:, (nh + kv) * d:].reshape(m, kv, d), None, eps).to(torch.bfloat16).transpose(0, 1)
+            xq, sx = w8.quant_rows(attn.transpose(0, 1).reshape(m, nh * d).contiguous())
+            w8.mm_i8_nk(xq, l["o"][0], c_o)
+            hh = hh + _torch_rms(w8.dequant(c_o, sx, l["o"][1]), l["w_post"], eps).to(torch.bfloat16)
+            xq, sx = w8.quant_rows(_torch_rms(hh, l["w_pre"], eps).to(torch.bfloat16))
+            w8.mm_i8_nk(xq, l["gu"][0], c_gu)
+            yg = w8.dequant(c_gu, sx, l["gu"][1])
+            a = (torch.nn.functional.gelu(yg[:, :6144], approximate="tanh") * yg[:, 6144:]).to(torch.bfloat16)
+            xq, sx = w8.quant_rows(a)
+            w8.mm_i8_nk(xq, l["dn"][0], c_dn)
+            hh = hh + _torch_rms(w8.dequant(c_dn, sx, l["dn"][1]), l["w_pff"], eps).to(torch.bfloat16)
+            del q, k_, v_
+
+    res = {}
+    for label, fn in (("fused", fused), ("unfused", unfused)):
+        gr = capture(fn, stream)
+        res[label] = timed(lambda: gr.replay(), steps, warmup, stream, world) / steps / layers
+        del gr
+    ops = 2 * m * sum(n * k for _, n, k in LAYER_SHAPES)
+    return {"workload": f"{layers} decoder layers at M={m}: k_in, qkv + k_qkv (H=8, KV=1, D=256, RoPE), "
+                        "k_attn_out, o + k_post_attn, gate_up + k_gelu, down + k_post_ff (attention excluded)",
+            "us_per_layer_fused": res["fused"] * 1e3, "us_per_layer_unfused": res["unfused"] * 1e3,
+            "tops_fused": ops / (res["fused"] * 1e-3) / 1e12, "speedup": res["unfused"] / res["fused"],
+            "unfused": "int32 GEMMs + dequant / quant kernels + the reference's glue as torch ops on the same GPU"}
+
+
 def sweep(w8, dev, stream, steps, warmup):
     """Config 3: each projection shape over 35 layers at M in {207, 858, 1878, 3658}, with
     and without the reference's 512-row padding (TOPS on the unpadded rows)."""
@@ -597,6 +691,7 @@ def main():
                                     "GEMVs (3.1-18.9 MB) are bound by launch and DRAM latency, not bandwidth"}}
         if not args.no_fused and args.only is None:
             line["fused_gelu_up"] = fused_gelu_up(w8, work, dev, stream, 10, 3, world)
+            line["fused_layer"] = fused_layer(w8, dev, stream, args.m, 5, 3, world)
         if not args.no_config4 and args.only is None:
             line["config4"] = {"prompts_dp": prompts_dp(w8, dev, stream, world, rank, 3, 3),
                                "lm_head_sharded": sharded_head(w8, dev, stream, world, 50, 5, pk)}

@@ -183,6 +183,107 @@ __global__ void __launch_bounds__(32 * kGlueWarps) glue_rows_kernel(const GlueAr
   }
 }
 
+// k_qkv (pipeline.py:72-86) after the qkv GEMM with the dequant fused (y = _deq(acc),
+// bf16 [T, (H + 2 KV) * D], or [T, H * D] for a KV-shared layer): one warp per
+// (token, head).  q and k heads: bf16(_rms(x, w)) then RoPE, each bf16 op rounded as
+// eager torch does: out = bf16(bf16(x * cos) + bf16(rotate_half(x) * sin)); v heads:
+// bf16(_rms(x, None)).  Output head-major: out[head * ld_head + t * ld_tok + d], the
+// layout of the reference's .transpose(0, 1) results.  D is 64, 128, 256 or 512, so a
+// lane's rotate_half partner is in its own registers (D = 512) or in lane ^ (D / 16).
+struct QkvArgs {
+  const __nv_bfloat16* y;
+  int64_t ldy;
+  const __nv_bfloat16* cos;
+  const __nv_bfloat16* sin;
+  int64_t ldcs;
+  const __nv_bfloat16* qw;
+  const __nv_bfloat16* kw;
+  float eps;
+  __nv_bfloat16* out;
+  int64_t ld_head, ld_tok;
+  int t, heads, kv_heads, d, shared;
+};
+
+__global__ void __launch_bounds__(32 * kGlueWarps) qkv_rows_kernel(const QkvArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per_tok = a.shared ? a.heads : a.heads + 2 * a.kv_heads;
+  const int64_t job = static_cast<int64_t>(blockIdx.x) * kGlueWarps + warp;
+  if (job >= static_cast<int64_t>(a.t) * per_tok) return;
+  const int tok = static_cast<int>(job / per_tok);
+  const int head = static_cast<int>(job - static_cast<int64_t>(tok) * per_tok);
+  const bool is_v = head >= a.heads + a.kv_heads;
+  const __nv_bfloat16* w = head < a.heads ? a.qw : (is_v ? nullptr : a.kw);
+  const int nv = a.d / 8;                 // vectors of the head
+  const int slots = nv > 32 ? 2 : 1;      // vectors per lane
+  const bool active = lane < nv;          // D = 64 / 128 use 8 / 16 lanes
+  const __nv_bfloat16* yr = a.y + static_cast<int64_t>(tok) * a.ldy + static_cast<int64_t>(head) * a.d;
+  uint4 v[2];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+    if (j < slots && active) {
+      v[j] = ld16(yr + (lane + 32 * j) * 8);
+      float f[8];
+      unpack8(v[j], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(f[e], f[e]));
+    }
+  const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(ss), static_cast<float>(a.d)), a.eps));
+  // bf16(_rms(x, w)) of this lane's vectors.
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+    if (j < slots && active) {
+      const int c = (lane + 32 * j) * 8;
+      float f[8], g[8];
+      unpack8(v[j], f);
+      if (w != nullptr) unpack8(ld16(w + c), g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float t = __fmul_rn(f[e], r);
+        f[e] = rbf16(w != nullptr ? __fmul_rn(t, g[e]) : t);
+      }
+      v[j] = pack8(f);
+    }
+  if (!is_v) {
+    // rotate_half partner of vector vi is vi + nv/2 (first half) or vi - nv/2.
+    uint4 p[2];
+    if (slots == 2) {
+      p[0] = v[1];
+      p[1] = v[0];
+    } else {
+      const int src = lane ^ (nv / 2);
+      p[0].x = __shfl_sync(0xffffffffu, v[0].x, src);
+      p[0].y = __shfl_sync(0xffffffffu, v[0].y, src);
+      p[0].z = __shfl_sync(0xffffffffu, v[0].z, src);
+      p[0].w = __shfl_sync(0xffffffffu, v[0].w, src);
+    }
+    const __nv_bfloat16* cr = a.cos + static_cast<int64_t>(tok) * a.ldcs;
+    const __nv_bfloat16* sr = a.sin + static_cast<int64_t>(tok) * a.ldcs;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      if (j < slots && active) {
+        const int vi = lane + 32 * j;
+        const int c = vi * 8;
+        const bool first = vi < nv / 2;
+        float x[8], px[8], cs[8], sn[8];
+        unpack8(v[j], x);
+        unpack8(p[j], px);
+        unpack8(ld16(cr + c), cs);
+        unpack8(ld16(sr + c), sn);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float rot = first ? -px[e] : px[e];
+          x[e] = rbf16(__fadd_rn(rbf16(__fmul_rn(x[e], cs[e])), rbf16(__fmul_rn(rot, sn[e]))));
+        }
+        v[j] = pack8(x);
+      }
+  }
+  __nv_bfloat16* orow = a.out + static_cast<int64_t>(head) * a.ld_head + static_cast<int64_t>(tok) * a.ld_tok;
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+    if (j < slots && active) *reinterpret_cast<uint4*>(orow + (lane + 32 * j) * 8) = v[j];
+}
+
 }  // namespace w8
 
 namespace w8host {
@@ -291,4 +392,48 @@ extern "C" int w8_attn_out_quant_bf16(const uint16_t* o, int64_t ld_head, int64_
   a.ldq = ldq;
   a.s = s;
   return w8host::glue_launch(w8::kGlueAttnOut, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int w8_qkv_norm_rope_bf16(const uint16_t* y, int64_t ldy, const uint16_t* cos, const uint16_t* sin,
+                                     int64_t ldcs, const uint16_t* qw, const uint16_t* kw, float eps,
+                                     uint16_t* out, int64_t ld_head, int64_t ld_tok, int64_t t, int64_t heads,
+                                     int64_t kv_heads, int64_t head_dim, int shared, w8_stream_t stream) {
+  using namespace w8host;
+  W8_CHECK_ARG(t >= 0 && heads >= 0 && kv_heads >= 0 && t < (1ll << 31), "bad size");
+  W8_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256 || head_dim == 512,
+               "head_dim = %lld must be 64, 128, 256 or 512", (long long)head_dim);
+  const int64_t per_tok = shared ? heads : heads + 2 * kv_heads;
+  if (t == 0 || per_tok == 0) return W8_OK;
+  W8_CHECK_ARG(y != nullptr && cos != nullptr && sin != nullptr && qw != nullptr && out != nullptr,
+               "null pointer");
+  W8_CHECK_ARG(shared || kv_heads == 0 || kw != nullptr, "null k_norm weight");
+  W8_CHECK_ARG(ldy >= per_tok * head_dim && ldcs >= head_dim && ld_tok >= head_dim, "pitch too small");
+  W8_CHECK_ALIGN(aligned(y, 16) && ldy % 8 == 0 && aligned(cos, 16) && aligned(sin, 16) && ldcs % 8 == 0 &&
+                     aligned(qw, 16) && (kw == nullptr || aligned(kw, 16)) && aligned(out, 16) &&
+                     ld_head % 8 == 0 && ld_tok % 8 == 0,
+                 "rows, weights and cos/sin must be 16-byte aligned with pitches %% 8 == 0");
+  int device = 0;
+  const int st = require_sm100(&device);
+  if (st != W8_OK) return st;
+  w8::QkvArgs a = {};
+  a.y = reinterpret_cast<const __nv_bfloat16*>(y);
+  a.ldy = ldy;
+  a.cos = reinterpret_cast<const __nv_bfloat16*>(cos);
+  a.sin = reinterpret_cast<const __nv_bfloat16*>(sin);
+  a.ldcs = ldcs;
+  a.qw = reinterpret_cast<const __nv_bfloat16*>(qw);
+  a.kw = reinterpret_cast<const __nv_bfloat16*>(kw);
+  a.eps = eps;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.ld_head = ld_head;
+  a.ld_tok = ld_tok;
+  a.t = static_cast<int>(t);
+  a.heads = static_cast<int>(heads);
+  a.kv_heads = static_cast<int>(kv_heads);
+  a.d = static_cast<int>(head_dim);
+  a.shared = shared != 0;
+  const int64_t jobs = t * per_tok;
+  const unsigned grid = static_cast<unsigned>((jobs + w8::kGlueWarps - 1) / w8::kGlueWarps);
+  w8::qkv_rows_kernel<<<grid, 32 * w8::kGlueWarps, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return cuda_status(cudaGetLastError());
 }

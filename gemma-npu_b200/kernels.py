@@ -12,6 +12,7 @@ quant/dequant glue of `pipeline.py` / `gemma_npu.py`:
     rms_quant(h, w, eps)         pipeline.py:66-69     (k_in)
     post_norm_quant(y, res, ..)  pipeline.py:95-99, 110-114 (k_post_attn / k_post_ff)
     attn_out_quant(o)            pipeline.py:88-92     (k_attn_out)
+    qkv_norm_rope(y, cos, sin,..)pipeline.py:72-86     (k_qkv)
 
 Every function validates dtype/shape/layout on the host, passes raw device
 pointers and torch's current CUDA stream to the C ABI, and raises a W8Error
@@ -264,6 +265,34 @@ def post_norm_quant(y, res, w1, w2, eps, h=None, q=None, s=None):
               None if w2 is None else w2.data_ptr(), float(eps), h.data_ptr(), _ld(h), q.data_ptr(), _ld(q),
               s.data_ptr(), T, N, _stream(y))
     return h, q, s
+
+
+def qkv_norm_rope(y, cos, sin, qw, kw, eps, heads, kv_heads, head_dim, shared=False, out=None):
+    """k_qkv (pipeline.py:72-86) on y = the qkv GEMM's dequantised bf16 output [T, (H+2KV)*D]
+    (or [T, H*D] when shared): returns (q [H, T, D], k [KV, T, D], v [KV, T, D]) bf16, slices of
+    one head-major buffer `out` [H + 2KV, T, D]; a KV-shared layer returns (q, q, q)."""
+    _bf16_rows(y, "y")
+    T = y.shape[0]
+    per_tok = heads if shared else heads + 2 * kv_heads
+    _need(y.shape[1] == per_tok * head_dim, f"y must have {per_tok * head_dim} columns")
+    _bf16_rows(cos, "cos", head_dim)
+    _bf16_rows(sin, "sin", head_dim)
+    _need(cos.shape[0] == T and sin.shape[0] == T and cos.stride(0) == sin.stride(0),
+          "cos and sin must be [T, D] with the same pitch")
+    _bf16_vec(qw, "qw", head_dim)
+    if not shared and kv_heads:
+        _bf16_vec(kw, "kw", head_dim)
+    if out is None:
+        out = torch.empty((per_tok, T, head_dim), dtype=torch.bfloat16, device=y.device)
+    _need(out.dtype == torch.bfloat16 and out.is_cuda and tuple(out.shape) == (per_tok, T, head_dim)
+          and out.stride(2) == 1, f"out must be bf16 ({per_tok}, {T}, {head_dim}) with unit stride along D")
+    _lib.call("w8_qkv_norm_rope_bf16", y.data_ptr(), _ld(y), cos.data_ptr(), sin.data_ptr(), cos.stride(0),
+              qw.data_ptr(), None if (shared or not kv_heads) else kw.data_ptr(), float(eps), out.data_ptr(),
+              out.stride(0), out.stride(1), T, heads, kv_heads, head_dim, int(bool(shared)), _stream(y))
+    q = out[:heads]
+    if shared:
+        return q, q, q
+    return q, out[heads: heads + kv_heads], out[heads + kv_heads:]
 
 
 def attn_out_quant(o, q=None, s=None):

@@ -24,6 +24,7 @@
  *   w8_rms_quant_bf16       pipeline.py:66-69 (k_in)
  *   w8_post_norm_quant_bf16 pipeline.py:95-99 (k_post_attn), :110-114 (k_post_ff)
  *   w8_attn_out_quant_bf16  pipeline.py:88-92 (k_attn_out)
+ *   w8_qkv_norm_rope_bf16   pipeline.py:72-86 (k_qkv)
  */
 #ifndef W8A8_B200_H
 #define W8A8_B200_H
@@ -156,6 +157,19 @@ int w8_post_norm_quant_bf16(const uint16_t* y, int64_t ldy, const uint16_t* res,
 int w8_attn_out_quant_bf16(const uint16_t* o, int64_t ld_head, int64_t ld_tok, int8_t* q,
                            int64_t ldq, float* s, int64_t t, int64_t heads, int64_t head_dim,
                            w8_stream_t stream);
+
+/* k_qkv (pipeline.py:72-86) after the qkv GEMM with the dequant fused: y = _deq(acc) bf16
+ * [T, (H + 2 KV) * D] (q heads, k heads, v heads), or [T, H * D] when shared != 0 (a
+ * KV-shared layer, whose k and v are the reference's q).  Per (token, head): q heads
+ * bf16(_rms(x, qw)) then RoPE with cos/sin bf16 [T, D] (pitch ldcs), k heads the same
+ * with kw, v heads bf16(_rms(x, None)).  out[head * ld_head + t * ld_tok + d], head in
+ * the order q, k, v: with ld_head = T * D and ld_tok = D, out is [H + 2 KV, T, D] and
+ * its q / k / v slices are the reference's transposed [heads, T, D] tensors.
+ * head_dim 64, 128, 256 or 512.  Same tolerance as the other norm glue. */
+int w8_qkv_norm_rope_bf16(const uint16_t* y, int64_t ldy, const uint16_t* cos, const uint16_t* sin,
+                          int64_t ldcs, const uint16_t* qw, const uint16_t* kw, float eps,
+                          uint16_t* out, int64_t ld_head, int64_t ld_tok, int64_t t, int64_t heads,
+                          int64_t kv_heads, int64_t head_dim, int shared, w8_stream_t stream);
 
 /* ---- quantisation ------------------------------------------------------ */
 

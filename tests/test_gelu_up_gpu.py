@@ -61,7 +61,8 @@ def test_golden_vectors(cuda, golden):
 
 # (M, I, K): config-1 gate/up (M = 3658, I = 6144, K = 1536); CTA pairs with K / 128 odd;
 # a single-CTA M; K % 128 != 0 (single-CTA tiles at any M); the smallest I.
-SHAPES = [(3658, 6144, 1536), (300, 256, 1664), (64, 6144, 1536), (200, 384, 208), (257, 128, 256)]
+SHAPES = [(3658, 6144, 1536), (300, 256, 1664), (64, 6144, 1536), (200, 384, 208), (257, 128, 256),
+          (3658, 12288, 1536)]  # the double-wide MLP of the real E2B mix
 
 
 @pytest.mark.parametrize("m,inter,k", SHAPES)

@@ -46,7 +46,9 @@ def test_golden_head_softcap(cuda, golden):
 
 # Every decode shape of BASELINE config 2 plus the K > 6144 team paths.
 SHAPES = [(2560, 1536), (1536, 2048), (12288, 1536), (1536, 6144), (256, 1536), (1536, 256),
-          (1024, 12288), (512, 16384), (1000, 48), (77, 4096), (333, 3072), (64, 8192)]
+          (1024, 12288), (512, 16384), (1000, 48), (77, 4096), (333, 3072), (64, 8192),
+          # the real E2B mix: double-wide MLP, head_dim-512 attention, q-only qkv
+          (24576, 1536), (1536, 12288), (5120, 1536), (1536, 4096), (2048, 1536)]
 
 
 @pytest.mark.parametrize("n,k", SHAPES)

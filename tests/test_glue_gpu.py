@@ -26,12 +26,16 @@ def bits(t):
     return t.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
 
 
-def close_bf16(a_bits, b_bits, frac=1e-2, res=None):
+def close_bf16(a_bits, b_bits, frac=1e-2, res=None, per_vector=False):
     """Within one bf16 step.  For h = bf16(res + t) the step is t's: when res and t nearly
-    cancel, one step of t is large next to h, so the bound is 2^-7 (|h| + |res|)."""
+    cancel, one step of t is large next to h, so the bound is 2^-7 (|h| + |res|).  RoPE's
+    x * cos + rotate_half(x) * sin can cancel the same way: per_vector bounds by one step
+    of the largest element of the (token, head) vector."""
     a, b = ref.bf16_bits_to_f32(a_bits), ref.bf16_bits_to_f32(b_bits)
     d = np.abs(a - b)
     scale = np.abs(b) if res is None else np.abs(b) + np.abs(np.asarray(res, np.float32))
+    if per_vector:
+        scale = scale + np.abs(b).max(axis=-1, keepdims=True)
     assert np.all(d <= scale * 2.0 ** -7 + 1e-30)
     assert (d != 0).mean() <= frac
 
@@ -118,3 +122,47 @@ def test_attn_out_strided_bit_exact(cuda):
     qr, sr = ref.k_attn_out(o.float().cpu().numpy())
     np.testing.assert_array_equal(q.cpu().numpy(), qr)
     np.testing.assert_array_equal(s.cpu().numpy(), sr)
+
+
+@pytest.mark.parametrize("name", ["k_qkv", "k_qkv_shared"])
+def test_golden_k_qkv(cuda, golden, name):
+    g = golden(name)
+    nh, kv, d, shared = (int(v) for v in g["dims"])
+    y = w8.dequant(torch.from_numpy(g["acc"]).to(cuda), torch.from_numpy(g["sx"]).to(cuda),
+                   torch.from_numpy(g["sw"]).to(cuda))
+    if shared:
+        y = y[:, : nh * d].contiguous()
+    q, k, v = w8.qkv_norm_rope(y, bf16(g["cos"], cuda), bf16(g["sin"], cuda), bf16(g["qw"], cuda),
+                               None if shared else bf16(g["kw"], cuda), float(g["eps"]), nh, kv, d, bool(shared))
+    for mine, theirs in ((q, g["q"]), (k, g["k"]), (v, g["v"])):
+        close_bf16(bits(mine), theirs, per_vector=True)
+
+
+def _rope_tables(t, d, dev):
+    ang = torch.arange(t, device=dev)[:, None].float() * (1e6 ** (-torch.arange(0, d, 2, device=dev).float() / d))[None]
+    ang = torch.cat([ang, ang], dim=-1)
+    return ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("t,nh,kv,d,shared", [(3658, 8, 1, 256, False), (3658, 8, 1, 256, True),
+                                              (300, 4, 2, 512, False), (129, 16, 4, 128, False),
+                                              (64, 8, 2, 64, False)])
+def test_qkv_gemm_then_norm_rope_matches_oracle(cuda, t, nh, kv, d, shared):
+    """qkv GEMM with the dequant fused, then the k_qkv glue, against the oracle on sampled tokens."""
+    k = 1536
+    n = (nh if shared else nh + 2 * kv) * d
+    gen = torch.Generator(device=cuda).manual_seed(t + d)
+    x, sx = w8.quant_rows(torch.randn((t, k), device=cuda, generator=gen, dtype=torch.bfloat16))
+    wq, sw = w8.quant_rows(torch.randn((n, k), device=cuda, generator=gen, dtype=torch.bfloat16) * 0.02)
+    cos, sin = _rope_tables(t, d, cuda)
+    qw = (1 + 0.1 * torch.randn((d,), device=cuda, generator=gen)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn((d,), device=cuda, generator=gen)).to(torch.bfloat16)
+    y = w8.gemm_dequant(x, wq, sx, sw)
+    q, kk, v = w8.qkv_norm_rope(y, cos, sin, qw, kw, 1e-6, nh, kv, d, shared)
+    rows = _rows(t, d)
+    acc = ref.int_mm(x[rows].cpu().numpy(), wq.t().cpu().numpy())
+    f = lambda z: z.float().cpu().numpy()
+    qr, kr, vr = ref.k_qkv(acc, f(sx[rows]), f(sw), f(cos[rows]), f(sin[rows]), f(qw), None if shared else f(kw),
+                           1e-6, nh, kv, d, shared)
+    for mine, theirs in ((q, qr), (kk, kr), (v, vr)):
+        close_bf16(bits(mine[:, rows]), ref.f32_to_bf16_bits(theirs), per_vector=True)
