@@ -93,12 +93,10 @@ __device__ __forceinline__ float rms_factor(const uint4 (&v)[kGlueMaxVecs], int 
 
 __device__ __forceinline__ float rbf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// One row of the glue (the warp's registers hold the row between the steps).
 template <int MODE>
-__global__ void __launch_bounds__(32 * kGlueWarps) glue_rows_kernel(const GlueArgs a) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kGlueWarps + warp;
-  if (row >= a.t) return;
-  const int nv = a.n / 8;
+__device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, int nv, const uint4* w1s,
+                                         const uint4* w2s) {
   uint4 v[kGlueMaxVecs];
 #pragma unroll
   for (int i = 0; i < kGlueMaxVecs; ++i) {
@@ -126,7 +124,7 @@ __global__ void __launch_bounds__(32 * kGlueWarps) glue_rows_kernel(const GlueAr
       if (vi < nv) {
         float x[8], w[8];
         unpack8(v[i], x);
-        unpack8(ld16(a.w1 + vi * 8), w);
+        unpack8(w1s[vi], w);
         float rr[8];
         if constexpr (MODE != kGlueIn) unpack8(res[i], rr);
 #pragma unroll
@@ -147,7 +145,7 @@ __global__ void __launch_bounds__(32 * kGlueWarps) glue_rows_kernel(const GlueAr
         if (vi < nv) {
           float x[8], w[8];
           unpack8(v[i], x);
-          unpack8(ld16(a.w2 + vi * 8), w);
+          unpack8(w2s[vi], w);
 #pragma unroll
           for (int e = 0; e < 8; ++e) x[e] = rbf16(__fmul_rn(__fmul_rn(x[e], r2), w[e]));
           v[i] = pack8(x);
@@ -181,6 +179,24 @@ __global__ void __launch_bounds__(32 * kGlueWarps) glue_rows_kernel(const GlueAr
       store_q<8>(a.q + static_cast<int64_t>(row) * a.ldq + vi * 8, out);
     }
   }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(32 * kGlueWarps, 3) glue_rows_kernel(const GlueArgs a) {
+  // The norm weights are the same for every row: staged once per CTA in shared memory.
+  __shared__ uint4 w1s[MODE == kGlueAttnOut ? 1 : 32 * kGlueMaxVecs];
+  __shared__ uint4 w2s[MODE == kGluePost2 ? 32 * kGlueMaxVecs : 1];
+  const int nv = a.n / 8;
+  if constexpr (MODE != kGlueAttnOut) {
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+      w1s[i] = ld16(a.w1 + i * 8);
+      if constexpr (MODE == kGluePost2) w2s[i] = ld16(a.w2 + i * 8);
+    }
+    __syncthreads();
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * kGlueWarps + warp; row < a.t; row += gridDim.x * kGlueWarps)
+    glue_row<MODE>(a, row, lane, nv, w1s, w2s);
 }
 
 // k_qkv (pipeline.py:72-86) after the qkv GEMM with the dequant fused (y = _deq(acc),
@@ -290,6 +306,21 @@ namespace w8host {
 
 int require_sm100(int* device);
 
+// One warp per row, at most as many CTAs as fit on the GPU at once (each warp then loops
+// over rows a grid's worth of warps apart).
+template <typename Kernel>
+static int glue_go(Kernel kern, const w8::GlueArgs& a, cudaStream_t stream) {
+  int sms = 0, per_sm = 0;
+  int st = num_sms(&sms);
+  if (st != W8_OK) return st;
+  W8_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * w8::kGlueWarps, 0));
+  const int64_t need = (static_cast<int64_t>(a.t) + w8::kGlueWarps - 1) / w8::kGlueWarps;
+  const int64_t cap = static_cast<int64_t>(sms) * (per_sm > 0 ? per_sm : 1);
+  const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
+  kern<<<grid, 32 * w8::kGlueWarps, 0, stream>>>(a);
+  return cuda_status(cudaGetLastError());
+}
+
 static int glue_launch(int mode, const w8::GlueArgs& a, cudaStream_t stream) {
   W8_CHECK_ARG(a.t >= 0 && a.n >= 0, "negative size");
   if (a.t == 0) return W8_OK;
@@ -322,15 +353,12 @@ static int glue_launch(int mode, const w8::GlueArgs& a, cudaStream_t stream) {
   int device = 0;
   const int st = require_sm100(&device);
   if (st != W8_OK) return st;
-  const unsigned grid = static_cast<unsigned>((a.t + w8::kGlueWarps - 1) / w8::kGlueWarps);
-  const unsigned threads = 32 * w8::kGlueWarps;
   switch (mode) {
-    case w8::kGlueIn: w8::glue_rows_kernel<w8::kGlueIn><<<grid, threads, 0, stream>>>(a); break;
-    case w8::kGluePost1: w8::glue_rows_kernel<w8::kGluePost1><<<grid, threads, 0, stream>>>(a); break;
-    case w8::kGluePost2: w8::glue_rows_kernel<w8::kGluePost2><<<grid, threads, 0, stream>>>(a); break;
-    default: w8::glue_rows_kernel<w8::kGlueAttnOut><<<grid, threads, 0, stream>>>(a); break;
+    case w8::kGlueIn: return glue_go(w8::glue_rows_kernel<w8::kGlueIn>, a, stream);
+    case w8::kGluePost1: return glue_go(w8::glue_rows_kernel<w8::kGluePost1>, a, stream);
+    case w8::kGluePost2: return glue_go(w8::glue_rows_kernel<w8::kGluePost2>, a, stream);
+    default: return glue_go(w8::glue_rows_kernel<w8::kGlueAttnOut>, a, stream);
   }
-  return cuda_status(cudaGetLastError());
 }
 
 static w8::GlueArgs glue_args(int64_t t, int64_t n) {
