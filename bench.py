@@ -265,7 +265,7 @@ def build_decode(w8, work, dev):
         for x, wq, s, y in chain:
             w8.int8_linear(x, wq, s, out=y)
         h, hq, hsc, logits = head
-        w8.lm_head_logits(h, hq, hsc, SOFTCAP, out=logits)
+        w8.lm_head_logits(h, hq, hsc, SOFTCAP, out=logits, argmax=True)  # + the greedy token
 
     return step, nbytes, len(chain) + 1, head
 
@@ -312,10 +312,11 @@ def sharded_head(w8, dev, stream, world, steps, warmup, pk):
     del weight
     h = torch.randn((HIDDEN,), device=dev, generator=g).to(torch.bfloat16)
     ms = timed(lambda: head(h), steps, warmup, stream, world) / steps
+    gms = timed(lambda: head.greedy(h), steps, warmup, stream, world) / steps
     shard_bytes = (head.r1 - head.r0) * (HIDDEN + 2)
     return {"workload": f"config 4: LM head {VOCAB}x{HIDDEN} int8 split by rows over {world} GPU(s), "
                         "fused softcap, NCCL all-gather of fp32 logits" + (" (no collective at N=1)" if world == 1 else ""),
-            "us_per_token": ms * 1e3, "shard_rows": head.r1 - head.r0,
+            "us_per_token": ms * 1e3, "us_per_token_greedy": gms * 1e3, "shard_rows": head.r1 - head.r0,
             "local_gemv_gbs": shard_bytes / (ms * 1e-3) / 1e9, "allgather_bytes": 4 * world * head.per,
             "steps": steps}
 
@@ -679,7 +680,8 @@ def main():
             head_bytes = VOCAB * HIDDEN + 2 * VOCAB + 2 * HIDDEN + 4 * VOCAB
             head_gbs = head_bytes / (hms * 1e-3) / 1e9
             line["decode_gemv"] = {
-                "metric": "int8 GEMV GB/s, decode chain (config 2: 140 layer GEMVs + LM head 262144x1536, softcap)",
+                "metric": "int8 GEMV GB/s, decode chain (config 2: 140 layer GEMVs + LM head 262144x1536, "
+                          "softcap and greedy argmax fused, one CUDA graph)",
                 "value": world * gbs, "unit": "GB/s", "ms_per_token": per, "bytes_per_token": nbytes,
                 "launches_per_token": launches,
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",

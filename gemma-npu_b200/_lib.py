@@ -89,6 +89,7 @@ SIGNATURES = {
     "w8_dequant_bf16": (_i, [_p, _i64, _p, _p, _p, _i64, _i64, _i64, _p]),
     "w8_int8_linear_bf16": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _i64, _p]),
     "w8_lm_head_f32": (_i, [_p, _p, _p, _f, _p, _i64, _i64, _p]),
+    "w8_lm_head_argmax_f32": (_i, [_p, _p, _p, _f, _p, _i64, _i64, _p, _p]),
 }
 
 _lock = threading.Lock()

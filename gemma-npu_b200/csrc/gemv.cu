@@ -66,18 +66,29 @@ __device__ __forceinline__ void dot16_i8(const uint4& w, const uint64_t (&xp)[8]
   }
 }
 
-// Output of one row: bf16 of the scaled sum, optionally softcapped to fp32.
+// Output of one row: bf16 of the scaled sum, optionally softcapped to fp32; returns the
+// value written (as fp32).
 template <bool LOGITS>
-__device__ __forceinline__ void write_out(void* y, int64_t idx, float acc, __nv_bfloat16 s,
-                                          float cap) {
+__device__ __forceinline__ float write_out(void* y, int64_t idx, float acc, __nv_bfloat16 s,
+                                           float cap) {
   const __nv_bfloat16 v = __float2bfloat16_rn(__fmul_rn(acc, __bfloat162float(s)));
   if constexpr (LOGITS) {
     float f = __bfloat162float(v);
     if (cap > 0.f) f = __fmul_rn(tanhf(__fdiv_rn(f, cap)), cap);
     static_cast<float*>(y)[idx] = f;
+    return f;
   } else {
     static_cast<__nv_bfloat16*>(y)[idx] = v;
+    return __bfloat162float(v);
   }
+}
+
+// Greedy-decode key of a logit: unsigned order = (value, then lower row first), the
+// tie rule of torch.argmax.  The fp32 bits are made monotone (negatives inverted).
+__device__ __forceinline__ unsigned long long argmax_key(float f, int row) {
+  uint32_t u = __float_as_uint(f);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(row));
 }
 
 // J: 16-byte chunks per lane per row; S: warps splitting K; R: rows per team per step.
@@ -85,8 +96,10 @@ template <int J, int S, int R, bool LOGITS>
 __global__ void __launch_bounds__(kGemvThreads)
     int8_gemv_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                      const int8_t* __restrict__ w, int64_t ldw, const __nv_bfloat16* __restrict__ s,
-                     void* __restrict__ y, int64_t ldy, int t_count, int n, int k, float cap) {
+                     void* __restrict__ y, int64_t ldy, int t_count, int n, int k, float cap,
+                     unsigned long long* __restrict__ best) {
   static_assert(kGemvWarps % S == 0, "S must divide the CTA's warps");
+  unsigned long long mine = 0ull;  // best argmax_key this thread wrote (LM head, t_count == 1)
   constexpr int kTeams = kGemvWarps / S;
   __shared__ float red[kTeams][S][R];
   const int warp = threadIdx.x >> 5;
@@ -152,8 +165,10 @@ __global__ void __launch_bounds__(kGemvThreads)
         float v = acc[0];
 #pragma unroll
         for (int r = 1; r < R; ++r) v = lane == r ? acc[r] : v;  // every lane holds every sum
-        if (lane < R && n0 + lane < n)
-          write_out<LOGITS>(y, static_cast<int64_t>(t) * ldy + n0 + lane, v, s[n0 + lane], cap);
+        if (lane < R && n0 + lane < n) {
+          const float f = write_out<LOGITS>(y, static_cast<int64_t>(t) * ldy + n0 + lane, v, s[n0 + lane], cap);
+          if (LOGITS && best != nullptr) mine = max(mine, argmax_key(f, n0 + lane));
+        }
       } else {
         if (lane == 0) {
 #pragma unroll
@@ -165,10 +180,18 @@ __global__ void __launch_bounds__(kGemvThreads)
           float v = red[team][0][lane];
 #pragma unroll
           for (int q = 1; q < S; ++q) v += red[team][q][lane];
-          write_out<LOGITS>(y, static_cast<int64_t>(t) * ldy + n0 + lane, v, s[n0 + lane], cap);
+          const float f = write_out<LOGITS>(y, static_cast<int64_t>(t) * ldy + n0 + lane, v, s[n0 + lane], cap);
+          if (LOGITS && best != nullptr) mine = max(mine, argmax_key(f, n0 + lane));
         }
         asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");
       }
+    }
+  }
+  if constexpr (LOGITS) {
+    if (best != nullptr) {  // one atomic per warp: the greedy token of the whole head
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mine = max(mine, __shfl_xor_sync(0xffffffffu, mine, o));
+      if (lane == 0 && mine != 0ull) atomicMax(best, mine);
     }
   }
 }
@@ -182,7 +205,7 @@ int require_sm100(int* device);
 template <int J, int S, int R, bool LOGITS>
 static int launch_gemv(const __nv_bfloat16* x, int64_t ldx, const int8_t* w, int64_t ldw,
                        const __nv_bfloat16* s, void* y, int64_t ldy, int t, int n, int k, float cap,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, unsigned long long* best) {
   auto kern = w8::int8_gemv_kernel<J, S, R, LOGITS>;
   int sms = 0;
   int st = num_sms(&sms);
@@ -206,13 +229,14 @@ static int launch_gemv(const __nv_bfloat16* x, int64_t ldx, const int8_t* w, int
   attr.val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, kern, x, ldx, w, ldw, s, y, ldy, t, n, k, cap));
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, x, ldx, w, ldw, s, y, ldy, t, n, k, cap, best));
 }
 
 template <bool LOGITS>
 static int gemv_dispatch(const uint16_t* xh, int64_t ldx, const int8_t* w, int64_t ldw,
                          const uint16_t* sh, void* y, int64_t ldy, int64_t t, int64_t n, int64_t k,
-                         float cap, cudaStream_t stream) {
+                         float cap, cudaStream_t stream,
+                         unsigned long long* best = nullptr) {
   W8_CHECK_ARG(t >= 0 && n >= 0 && k >= 0, "negative size");
   W8_CHECK_ARG(t < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31), "size beyond int32 range");
   if (t == 0 || n == 0) return W8_OK;
@@ -240,8 +264,8 @@ static int gemv_dispatch(const uint16_t* xh, int64_t ldx, const int8_t* w, int64
   // a matrix too short to give two CTAs per SM at that R takes one row per team.
 #define W8_GEMV(J, S, R)                                                                      \
   return n < 2 * sms * (w8::kGemvWarps / (S)) * (R)                                            \
-             ? launch_gemv<J, S, 1, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream) \
-             : launch_gemv<J, S, R, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream)
+             ? launch_gemv<J, S, 1, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream, best) \
+             : launch_gemv<J, S, R, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream, best)
   if (k <= 512) W8_GEMV(1, 1, 4);
   if (k <= 1024) W8_GEMV(2, 1, 4);
   if (k <= 1536) W8_GEMV(3, 1, 4);
@@ -268,4 +292,16 @@ extern "C" int w8_lm_head_f32(const uint16_t* x, const int8_t* w, const uint16_t
                               float* logits, int64_t n, int64_t k, w8_stream_t stream) {
   return w8host::gemv_dispatch<true>(x, k, w, k, s, logits, n, 1, n, k, cap,
                                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int w8_lm_head_argmax_f32(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap,
+                                     float* logits, int64_t n, int64_t k, uint64_t* best,
+                                     w8_stream_t stream) {
+  W8_CHECK_ARG(best != nullptr, "null argmax output");
+  W8_CHECK_ALIGN(reinterpret_cast<uintptr_t>(best) % 8 == 0, "argmax output must be 8-byte aligned");
+  W8_CHECK_ARG(n > 0 && n < (1ll << 32) - 1, "n = %lld out of range for the argmax", (long long)n);
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  W8_CUDA_TRY(cudaMemsetAsync(best, 0, sizeof(uint64_t), st));
+  return w8host::gemv_dispatch<true>(x, k, w, k, s, logits, n, 1, n, k, cap, st,
+                                     reinterpret_cast<unsigned long long*>(best));
 }

@@ -377,11 +377,13 @@ def int8_linear(x2d, wq, sw, out=None):
     return out
 
 
-def lm_head_logits(x, wq, sw, cap=0.0, out=None):
+def lm_head_logits(x, wq, sw, cap=0.0, out=None, argmax=False):
     """fp32 [N] logits of one token: cap * tanh(bf16(x @ wq^T * sw) / cap) (cap <= 0: no softcap).
 
     Int8Head.forward (gemma_npu.py:170-172) followed by the final logit softcap
-    (pipeline.py:335-338), fused into the GEMV.
+    (pipeline.py:335-338), fused into the GEMV.  With argmax=True also the greedy token
+    (gemma_npu.py:291, logits.argmax(); ties to the lowest id), folded inside the same
+    kernel: returns (logits, token) with token a 0-dim int64 device tensor.
     """
     _need(isinstance(x, torch.Tensor) and x.is_cuda, "x must be a CUDA tensor")
     x = x.reshape(-1)
@@ -396,6 +398,22 @@ def lm_head_logits(x, wq, sw, cap=0.0, out=None):
     if out is None:
         out = torch.empty((N,), dtype=torch.float32, device=x.device)
     _check_vector(out, "out", torch.float32, N)
-    _lib.call("w8_lm_head_f32", x.data_ptr(), wq.data_ptr(), sw.data_ptr(), float(cap or 0.0),
-              out.data_ptr(), N, K, _stream(x))
-    return out
+    if not argmax:
+        _lib.call("w8_lm_head_f32", x.data_ptr(), wq.data_ptr(), sw.data_ptr(), float(cap or 0.0),
+                  out.data_ptr(), N, K, _stream(x))
+        return out
+    best = torch.empty((1,), dtype=torch.int64, device=x.device)
+    _lib.call("w8_lm_head_argmax_f32", x.data_ptr(), wq.data_ptr(), sw.data_ptr(), float(cap or 0.0),
+              out.data_ptr(), N, K, best.data_ptr(), _stream(x))
+    return out, argmax_token(best)
+
+
+def monotone_bits(f):
+    """fp32 value(s) -> int64 holding the order-preserving 32-bit key of the argmax."""
+    u = f.float().reshape(-1).view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    return torch.where(u >= 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)
+
+
+def argmax_token(best):
+    """Token id (0-dim int64 on the device) from the packed key of w8_lm_head_argmax_f32."""
+    return (0xFFFFFFFF - (best & 0xFFFFFFFF))[0]

@@ -62,3 +62,33 @@ class ShardedInt8Head:
     def __call__(self, h):
         """Full fp32 logits [V] of one hidden row on every rank."""
         return gather_logits(self.local_logits(h), self.full, self.vocab, self.group)
+
+    def greedy(self, h):
+        """The greedy token (gemma_npu.py:291, logits.argmax()) without gathering the logits:
+        each rank folds its shard's argmax inside the head GEMV, re-keys it with the global
+        row id, and one 8-byte all-gather per rank picks the winner (ties: lowest id)."""
+        n = self.r1 - self.r0
+        key = torch.full((1,), -(1 << 63), dtype=torch.int64, device=self.device)
+        if n > 0:
+            _, tok = kernels.lm_head_logits(h, self.wq, self.sw, self.cap, out=self.local[:n], argmax=True)
+            key = merge_key(self._best_high(), tok + self.r0)
+        return greedy_from_keys(key, self.group)
+
+    def _best_high(self):
+        # value half of the last argmax key: recomputed from the stored logits' maximum
+        return kernels.monotone_bits(self.local[: self.r1 - self.r0].max())
+
+
+def merge_key(high, token):
+    """Packed greedy key of (monotone value bits, global token id) as a signed int64: larger
+    is better, ties to the lower id (the value half is re-centred for signed order)."""
+    return (((high.to(torch.int64) & 0xFFFFFFFF) - 0x80000000) << 32) | (0xFFFFFFFF - token.to(torch.int64))
+
+
+def greedy_from_keys(key, group=None):
+    """Winner among the ranks' packed keys: the token id of the largest key."""
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        keys = torch.empty((dist.get_world_size(group),), dtype=torch.int64, device=key.device)
+        dist.all_gather_into_tensor(keys, key.reshape(1), group=group)
+        key = keys.max()
+    return (0xFFFFFFFF - (key.reshape(()) & 0xFFFFFFFF))

@@ -19,6 +19,7 @@
  *   w8_dequant_bf16         pipeline.py:55-57 (_deq), gemma_npu.py:45-47 (_dequant)
  *   w8_int8_linear_bf16     gemma_npu.py:155-156 (cpu_int8_linear = torch._weight_int8pack_mm)
  *   w8_lm_head_f32          gemma_npu.py:170-172 (Int8Head.forward) + pipeline.py:335-338 (softcap)
+ *   w8_lm_head_argmax_f32   the same + the greedy token argmax (gemma_npu.py:291)
  *   w8_gemm_gelu_up_quant   pipeline.py:102-107 (k_gelu) fused onto the gate/up GEMM of
  *                           pipeline.py:233-242 (Prefill.gemm)
  *   w8_rms_quant_bf16       pipeline.py:66-69 (k_in)
@@ -204,6 +205,14 @@ int w8_int8_linear_bf16(const uint16_t* x, int64_t ldx, const int8_t* w, int64_t
  * (pipeline.py:335-338). */
 int w8_lm_head_f32(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap,
                    float* logits, int64_t n, int64_t k, w8_stream_t stream);
+
+/* w8_lm_head_f32 plus the greedy token (gemma_npu.py:291, logits.argmax()): *best gets
+ * (key << 32) | (0xFFFFFFFF - row) of the largest logit, key being its fp32 bits made
+ * monotone, so the token is 0xFFFFFFFF - (*best & 0xFFFFFFFF) and ties resolve to the
+ * lowest row as torch.argmax does.  `best` (8-byte aligned) is cleared on the stream
+ * first; each warp folds its rows into it with one 64-bit atomicMax. */
+int w8_lm_head_argmax_f32(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap,
+                          float* logits, int64_t n, int64_t k, uint64_t* best, w8_stream_t stream);
 
 #ifdef __cplusplus
 }

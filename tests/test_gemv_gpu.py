@@ -80,3 +80,25 @@ def test_full_lm_head_262144(cuda):
     assert max_rel(y.float().cpu().numpy(), cpu_int8.int8_linear(h[None].cpu(), wq.cpu(), s.cpu()).float().numpy()) <= MAX_REL
     # The softcap is applied to the bf16 head output: same argmax as the unfused path.
     assert int(logits.argmax()) == int((torch.tanh(y[0].float() / 30.0) * 30.0).argmax())
+
+
+@pytest.mark.parametrize("cap", [30.0, 0.0])
+def test_lm_head_argmax_equals_torch_argmax(cuda, cap):
+    """The greedy token folded inside the head GEMV equals torch.argmax of the same
+    logits (gemma_npu.py:291), including the lowest-id rule on ties: rows 7 and 100 and
+    200000 are copies of one row (equal logits)."""
+    gen = torch.Generator(device=cuda).manual_seed(11)
+    w = (torch.randn(262144, 1536, device=cuda, generator=gen) * 0.02).to(torch.bfloat16)
+    h = torch.randn(1536, device=cuda, generator=gen).to(torch.bfloat16)
+    wq, sw = w8.quant_rows(w)
+    s = sw.to(torch.bfloat16)
+    top = int(w8.lm_head_logits(h, wq, s, cap).argmax())
+    for r in (7, 100, 200000):
+        wq[r] = wq[top]
+        s[r] = s[top]
+    for _ in range(2):  # the key is cleared by every call
+        logits, tok = w8.lm_head_logits(h, wq, s, cap, argmax=True)
+        assert int(tok) == int(logits.argmax()) == 7
+    # negated scales flip every logit's sign: the monotone key of negative floats
+    logits, tok = w8.lm_head_logits(h, wq[:5000], s[:5000] * -1, cap, argmax=True)
+    assert int(tok) == int(logits.argmax())

@@ -98,3 +98,21 @@ def test_pack_gelu_up_layout():
             assert sp[256 * t + 128 + j].item() == inter + 128 * t + j
             assert wp[256 * t + 128 + j, 3].item() == inter + 128 * t + j
     assert w.shape == wp.shape
+
+
+def test_greedy_key_merge_matches_argmax():
+    """Sharded greedy decode: per-shard keys merged on the host pick torch.argmax's token
+    (largest value, lowest id on ties), for negative, positive and tied logits."""
+    from gemma_npu_b200 import kernels, lm_head
+
+    gen = torch.Generator().manual_seed(0)
+    for v in (torch.randn(1000, generator=gen), -torch.rand(1000, generator=gen) - 1,
+              torch.tensor([1.0, 3.0, 3.0, 2.0, 3.0])):
+        shards = torch.tensor_split(torch.arange(v.numel()), 4)
+        keys = []
+        for idx in shards:
+            local = v[idx]
+            j = int(local.argmax())
+            keys.append(lm_head.merge_key(kernels.monotone_bits(local[j:j + 1])[0], idx[j]))
+        tok = lm_head.greedy_from_keys(torch.stack(keys).max())
+        assert int(tok) == int(v.argmax())

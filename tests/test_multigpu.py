@@ -1,4 +1,5 @@
-"""The column-sharded LM head over NCCL on 2 GPUs equals the single-GPU head.
+"""The column-sharded LM head over NCCL on 2 GPUs equals the single-GPU head, and its
+greedy token (per-shard argmax in the GEMV + an 8-byte all-gather) is the full argmax.
 
 One process per GPU; skipped with fewer than 2 sm_100 devices.  NCCL's in-switch
 reduction (NVLS) is off, so the test uses plain NCCL rings.
@@ -43,7 +44,9 @@ def _worker(rank, world, port, q):
         full_q, full_s = w8.quant_rows(w)
         want = w8.lm_head_logits(h, full_q, full_s.to(torch.bfloat16), 30.0)
         torch.cuda.synchronize()
-        q.put((rank, bool(torch.equal(got, want)), float((got - want).abs().max())))
+        greedy = int(head.greedy(h))
+        ok = bool(torch.equal(got, want)) and greedy == int(want.argmax())
+        q.put((rank, ok, float((got - want).abs().max())))
     finally:
         dist.destroy_process_group()
 
