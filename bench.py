@@ -462,7 +462,8 @@ def fused_layer(w8, dev, stream, m, steps, warmup, world, layers=35):
 
 def sweep(w8, dev, stream, steps, warmup):
     """Config 3: each projection shape over 35 layers at M in {207, 858, 1878, 3658}, with
-    and without the reference's 512-row padding (TOPS on the unpadded rows)."""
+    and without the reference's 512-row padding (TOPS on the unpadded rows); plus the real
+    E2B shape mix at M = 3658."""
     out = {}
     for m in (207, 858, 1878, 3658):
         mp = -(-m // 512) * 512
@@ -486,6 +487,27 @@ def sweep(w8, dev, stream, steps, warmup):
             row[name] = res
         out[str(m)] = row
         del work
+    # The real E2B shape mix (SURVEY next row 2) at M = 3658, 8 distinct weights per shape.
+    e2b = {"gate_up_x2 24576x1536": (24576, 1536), "down_x2 1536x12288": (1536, 12288),
+           "qkv_global 5120x1536": (5120, 1536), "o_global 1536x4096": (1536, 4096),
+           "q_only 2048x1536": (2048, 1536), "ple_gate 256x1536": (256, 1536), "ple_proj 1536x256": (1536, 256)}
+    m = 3658
+    g = torch.Generator(device=dev).manual_seed(5)
+    mix = {}
+    for name, (n, k) in e2b.items():
+        xq = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=dev, generator=g)
+        ws = [torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev, generator=g) for _ in range(8)]
+        c = torch.empty((m, n), dtype=torch.int32, device=dev)
+
+        def step(xq=xq, ws=ws, c=c):
+            for w in ws:
+                w8.mm_i8_nk(xq, w, c)
+
+        gr = capture(step, stream)
+        ms = timed(lambda: gr.replay(), steps, warmup, stream, 1) / steps
+        del gr
+        mix[name] = {"us_per_gemm": ms * 1e3 / len(ws), "tops": 2 * m * n * k * len(ws) / (ms * 1e-3) / 1e12}
+    out["e2b_mix_m3658"] = mix
     return out
 
 
