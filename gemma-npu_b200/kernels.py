@@ -383,7 +383,8 @@ def lm_head_logits(x, wq, sw, cap=0.0, out=None, argmax=False):
     Int8Head.forward (gemma_npu.py:170-172) followed by the final logit softcap
     (pipeline.py:335-338), fused into the GEMV.  With argmax=True also the greedy token
     (gemma_npu.py:291, logits.argmax(); ties to the lowest id), folded inside the same
-    kernel: returns (logits, token) with token a 0-dim int64 device tensor.
+    kernel: returns (logits, token) with token a 0-dim int64 device tensor (argmax="key":
+    the raw packed key of w8_lm_head_argmax_f32 as an int64 [1] tensor instead).
     """
     _need(isinstance(x, torch.Tensor) and x.is_cuda, "x must be a CUDA tensor")
     x = x.reshape(-1)
@@ -405,7 +406,7 @@ def lm_head_logits(x, wq, sw, cap=0.0, out=None, argmax=False):
     best = torch.empty((1,), dtype=torch.int64, device=x.device)
     _lib.call("w8_lm_head_argmax_f32", x.data_ptr(), wq.data_ptr(), sw.data_ptr(), float(cap or 0.0),
               out.data_ptr(), N, K, best.data_ptr(), _stream(x))
-    return out, argmax_token(best)
+    return out, (argmax_token(best) if argmax != "key" else best)
 
 
 def monotone_bits(f):

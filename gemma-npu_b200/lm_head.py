@@ -68,21 +68,24 @@ class ShardedInt8Head:
         each rank folds its shard's argmax inside the head GEMV, re-keys it with the global
         row id, and one 8-byte all-gather per rank picks the winner (ties: lowest id)."""
         n = self.r1 - self.r0
-        key = torch.full((1,), -(1 << 63), dtype=torch.int64, device=self.device)
         if n > 0:
-            _, tok = kernels.lm_head_logits(h, self.wq, self.sw, self.cap, out=self.local[:n], argmax=True)
-            key = merge_key(self._best_high(), tok + self.r0)
+            _, best = kernels.lm_head_logits(h, self.wq, self.sw, self.cap, out=self.local[:n], argmax="key")
+            key = shard_key(best, self.r0)
+        else:
+            key = torch.full((1,), -(1 << 63), dtype=torch.int64, device=self.device)
         return greedy_from_keys(key, self.group)
 
-    def _best_high(self):
-        # value half of the last argmax key: recomputed from the stored logits' maximum
-        return kernels.monotone_bits(self.local[: self.r1 - self.r0].max())
+
+def shard_key(best, r0):
+    """A shard's packed key (unsigned: monotone value bits << 32 | 2^32 - 1 - local row) as a
+    signed-comparable int64 with the global row id r0 + local row."""
+    return (best - r0) ^ (-(1 << 63))
 
 
 def merge_key(high, token):
-    """Packed greedy key of (monotone value bits, global token id) as a signed int64: larger
-    is better, ties to the lower id (the value half is re-centred for signed order)."""
-    return (((high.to(torch.int64) & 0xFFFFFFFF) - 0x80000000) << 32) | (0xFFFFFFFF - token.to(torch.int64))
+    """Signed-comparable packed key of (monotone value bits, global token id): larger is
+    better, ties to the lower id."""
+    return (((high.to(torch.int64) & 0xFFFFFFFF) << 32) | (0xFFFFFFFF - token.to(torch.int64))) ^ (-(1 << 63))
 
 
 def greedy_from_keys(key, group=None):
