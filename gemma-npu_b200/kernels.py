@@ -13,6 +13,7 @@ quant/dequant glue of `pipeline.py` / `gemma_npu.py`:
     post_norm_quant(y, res, ..)  pipeline.py:95-99, 110-114 (k_post_attn / k_post_ff)
     attn_out_quant(o)            pipeline.py:88-92     (k_attn_out)
     qkv_norm_rope(y, cos, sin,..)pipeline.py:72-86     (k_qkv)
+    attention_prefill(q, k, v, W)pipeline.py:139-180   (full / sliding-window attention)
 
 Every function validates dtype/shape/layout on the host, passes raw device
 pointers and torch's current CUDA stream to the C ABI, and raises a W8Error
@@ -293,6 +294,26 @@ def qkv_norm_rope(y, cos, sin, qw, kw, eps, heads, kv_heads, head_dim, shared=Fa
     if shared:
         return q, q, q
     return q, out[heads: heads + kv_heads], out[heads + kv_heads:]
+
+
+def attention_prefill(q, k, v, window=0, out=None):
+    """Prefill attention of one prompt from position 0 (pipeline.py:139-180): causal, with
+    a sliding window when window > 0, scale 1.0, grouped-query heads.  q bf16 [H, T, D],
+    k, v [KV, T, D] (unit stride along D; any head / token pitch); returns o [H, T, D]."""
+    for t_, name in ((q, "q"), (k, "k"), (v, "v")):
+        _need(isinstance(t_, torch.Tensor) and t_.is_cuda and t_.dtype == torch.bfloat16 and t_.dim() == 3
+              and t_.stride(2) == 1, f"{name} must be a bf16 CUDA tensor [heads, T, D] with unit stride along D")
+    H, T, D = q.shape
+    KV = k.shape[0]
+    _need(tuple(k.shape) == (KV, T, D) and tuple(v.shape) == (KV, T, D), "k and v must be [KV, T, D]")
+    if out is None:
+        out = torch.empty((H, T, D), dtype=torch.bfloat16, device=q.device)
+    _need(out.dtype == torch.bfloat16 and tuple(out.shape) == (H, T, D) and out.stride(2) == 1,
+          f"out must be bf16 ({H}, {T}, {D})")
+    _lib.call("w8_attention_prefill_bf16", q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0),
+              k.stride(1), v.data_ptr(), v.stride(0), v.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
+              T, H, KV, D, int(window), _stream(q))
+    return out
 
 
 def attn_out_quant(o, q=None, s=None):

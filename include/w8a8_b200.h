@@ -26,6 +26,7 @@
  *   w8_post_norm_quant_bf16 pipeline.py:95-99 (k_post_attn), :110-114 (k_post_ff)
  *   w8_attn_out_quant_bf16  pipeline.py:88-92 (k_attn_out)
  *   w8_qkv_norm_rope_bf16   pipeline.py:72-86 (k_qkv)
+ *   w8_attention_prefill_bf16 pipeline.py:139-180 (full_attention / sliding_attention)
  */
 #ifndef W8A8_B200_H
 #define W8A8_B200_H
@@ -171,6 +172,20 @@ int w8_qkv_norm_rope_bf16(const uint16_t* y, int64_t ldy, const uint16_t* cos, c
                           int64_t ldcs, const uint16_t* qw, const uint16_t* kw, float eps,
                           uint16_t* out, int64_t ld_head, int64_t ld_tok, int64_t t, int64_t heads,
                           int64_t kv_heads, int64_t head_dim, int shared, w8_stream_t stream);
+
+/* Prefill attention of one prompt from position 0 (pipeline.py:139-180: full_attention,
+ * and sliding_attention with window > 0): o[h] = softmax(q[h] k[h / G]^T, causal, and
+ * key > query - window when window > 0) v[h / G], scale 1.0, G = heads / kv_heads.  bf16
+ * q [heads, T, D], k, v [kv_heads, T, D], o [heads, T, D], element (h, t, d) at
+ * x[h * x_head + t * x_tok + d] (the k_qkv glue's head-major output); fp32 softmax and
+ * accumulation, P rounded to bf16 for the second product.  head_dim 256 or 512; 16-byte
+ * aligned with pitches % 8 == 0.  Replaces local_attn.py / the CPU sdpa calls: within
+ * max-rel 1e-2 of them. */
+int w8_attention_prefill_bf16(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k,
+                              int64_t k_head, int64_t k_tok, const uint16_t* v, int64_t v_head,
+                              int64_t v_tok, uint16_t* o, int64_t o_head, int64_t o_tok, int64_t t,
+                              int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t window,
+                              w8_stream_t stream);
 
 /* ---- quantisation ------------------------------------------------------ */
 

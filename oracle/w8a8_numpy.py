@@ -169,3 +169,27 @@ def k_qkv(acc, sx, sw, cos, sin, qw, kw, eps, nh, kv, d, shared):
     k = rope(bf16_round(rms(k, kw, eps)), cos, sin).transpose(1, 0, 2)
     v = bf16_round(rms(v, None, eps)).transpose(1, 0, 2)
     return q, k, v
+
+
+def attention(q, k, v, window=0):
+    """Prefill attention of one prompt (pipeline.py:139-180 with q_start = 0): scale 1.0,
+    causal, and with window W > 0 each query sees only the W keys up to itself
+    (sliding_attention's mask: key <= query, query - key < W).  q [H, T, D], k, v [KV, T, D]
+    (grouped-query: head h reads KV head h // (H / KV)); float64 softmax, unrounded result."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    nh, t, _ = q.shape
+    group = nh // k.shape[0]
+    pos = np.arange(t)
+    allowed = pos[None, :] <= pos[:, None]
+    if window:
+        allowed &= (pos[:, None] - pos[None, :]) < window
+    out = np.empty_like(q)
+    for h in range(nh):
+        s = q[h] @ k[h // group].T
+        s = np.where(allowed, s, -np.inf)
+        s -= s.max(axis=1, keepdims=True)
+        p = np.exp(s)
+        out[h] = (p / p.sum(axis=1, keepdims=True)) @ v[h // group]
+    return out

@@ -15,6 +15,8 @@ repository) and records, on seeded inputs:
   gelu_up   pipeline.k_gelu (pipeline.py:102-107): dequant, gelu_tanh(gate) * up, int8 quant
   k_in, k_post_attn, k_post_ff, k_attn_out, k_qkv(_shared)
             the RMSNorm / residual / RoPE glue of pipeline.py:66-99, 110-114 (eager bodies)
+  attn_sliding, attn_full
+            pipeline.sliding_attention / full_attention (pipeline.py:139-180), q_start = 0
 
 The weight of the GEMM, GEMV and head cases is the one stored in wquant.npz
 (q [N,K] int8, s bf16 [N]); the GEMM's B operand is its transpose.  The outputs
@@ -167,6 +169,17 @@ def main(ref_dir):
             acc=acc.numpy(), sx=sxa.numpy(), sw=swa.numpy(), cos=bf16_bits(cos), sin=bf16_bits(sin), qw=bf16_bits(qw),
             kw=bf16_bits(kw), eps=np.float32(eps), dims=np.array([nh, kv, hd, int(shared)], np.int32),
             q=bf16_bits(qq), k=bf16_bits(kk), v=bf16_bits(vv))
+
+    # ---- prefill attention (pipeline.py:139-180), one prompt from position 0: sliding
+    # window 512 (head_dim 256) and full causal (head_dim 512), 2 query heads on 1 KV head
+    for name, (at, ad, win) in {"attn_sliding": (640, 256, 512), "attn_full": (200, 512, 0)}.items():
+        aq = torch.randn(2, at, ad).to(torch.bfloat16)
+        ak = torch.randn(1, at, ad).to(torch.bfloat16)
+        av = torch.randn(1, at, ad).to(torch.bfloat16)
+        scale = ad ** -0.25  # keep the logits O(1) at scale 1.0, as q_norm / k_norm do
+        aq, ak = (aq.float() * scale).to(torch.bfloat16), (ak.float() * scale).to(torch.bfloat16)
+        ao = pipeline.sliding_attention(aq, ak, av, 0, win) if win else pipeline.full_attention(aq, ak, av, 0)
+        out[name] = dict(q=bf16_bits(aq), k=bf16_bits(ak), v=bf16_bits(av), window=np.int32(win), o=bf16_bits(ao))
 
     for name, arrays in out.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)

@@ -1,0 +1,75 @@
+"""Prefill attention (pipeline.py:139-180) on the GPU against the reference's own outputs
+(tests/golden/attn_*.npz, made by pipeline.sliding_attention / full_attention) and the
+float64 oracle (oracle/w8a8_numpy.attention).
+
+Tolerance: normwise max-rel <= 1e-2 (the north-star bound for bf16 outputs); the kernel
+rounds P to bf16 before P @ V as flash attention does, the reference's CPU kernels keep
+other roundings (the oracle itself is within 3e-3 of the reference's outputs).
+"""
+import numpy as np
+import pytest
+import torch
+
+import gemma_npu_b200 as w8
+from oracle import w8a8_numpy as ref
+
+pytestmark = pytest.mark.gpu
+MAX_REL = 1e-2
+
+
+def bf16(bits, dev):
+    return torch.from_numpy(bits.astype(np.uint16).view(np.int16)).view(torch.bfloat16).to(dev)
+
+
+def max_rel(a, b):
+    return float(np.abs(np.asarray(a, np.float64) - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.mark.parametrize("name", ["attn_sliding", "attn_full"])
+def test_golden(cuda, golden, name):
+    g = golden(name)
+    o = w8.attention_prefill(bf16(g["q"], cuda), bf16(g["k"], cuda), bf16(g["v"], cuda), int(g["window"]))
+    assert max_rel(o.float().cpu().numpy(), ref.bf16_bits_to_f32(g["o"])) <= MAX_REL
+
+
+# (T, H, KV, D, window): Gemma E2B sliding (D 256, W 512) and full (D 512) layers at the
+# config-1 length, ragged T, more KV heads, a window longer than the prompt.
+SHAPES = [(3658, 8, 1, 256, 512), (3658, 8, 1, 512, 0), (1000, 4, 2, 256, 0), (77, 2, 1, 256, 512),
+          (700, 8, 8, 512, 128)]
+
+
+@pytest.mark.parametrize("t,h,kv,d,window", SHAPES)
+def test_matches_oracle(cuda, t, h, kv, d, window):
+    gen = torch.Generator(device=cuda).manual_seed(t + d + window)
+    scale = d ** -0.25  # logits O(1) at scale 1.0, as q_norm / k_norm keep them
+    q = (torch.randn((h, t, d), device=cuda, generator=gen) * scale).to(torch.bfloat16)
+    k = (torch.randn((kv, t, d), device=cuda, generator=gen) * scale).to(torch.bfloat16)
+    v = torch.randn((kv, t, d), device=cuda, generator=gen).to(torch.bfloat16)
+    o = w8.attention_prefill(q, k, v, window)
+    torch.cuda.synchronize()
+    # oracle on a sample of query rows (full rows of keys), every head
+    rows = sorted({0, 1, t - 1} | set(torch.randint(0, t, (13,), generator=torch.Generator().manual_seed(t)).tolist()))
+    qn, kn, vn = q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy()
+    group = h // kv
+    for hh in range(h):
+        s = qn[hh, rows].astype(np.float64) @ kn[hh // group].T.astype(np.float64)
+        pos = np.arange(t)
+        r = np.asarray(rows)[:, None]
+        allowed = (pos[None, :] <= r) & ((r - pos[None, :]) < window if window else True)
+        s = np.where(allowed, s, -np.inf)
+        p = np.exp(s - s.max(axis=1, keepdims=True))
+        want = (p / p.sum(axis=1, keepdims=True)) @ vn[hh // group].astype(np.float64)
+        assert max_rel(o[hh, rows].float().cpu().numpy(), want) <= MAX_REL
+
+
+def test_strided_views(cuda):
+    """q / k / v as slices of the k_qkv glue's head-major buffer, o into a wider buffer."""
+    t, h, kv, d = 300, 4, 1, 256
+    gen = torch.Generator(device=cuda).manual_seed(1)
+    buf = (torch.randn((h + 2 * kv, t, d), device=cuda, generator=gen) * d ** -0.25).to(torch.bfloat16)
+    q, k, v = buf[:h], buf[h:h + kv], buf[h + kv:]
+    big = torch.zeros((h, t + 10, d), dtype=torch.bfloat16, device=cuda)
+    o = w8.attention_prefill(q, k, v, 0, out=big[:, 5:5 + t])
+    want = w8.attention_prefill(q.contiguous(), k.contiguous(), v.contiguous(), 0)
+    assert torch.equal(o, want)
+    assert not big[:, :5].any() and not big[:, 5 + t:].any()
