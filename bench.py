@@ -460,6 +460,31 @@ def fused_layer(w8, dev, stream, m, steps, warmup, world, layers=35):
             "unfused": "int32 GEMMs + dequant / quant kernels + the reference's glue as torch ops on the same GPU"}
 
 
+def attention_bench(w8, dev, stream, m, steps, warmup, world):
+    """SURVEY next row 4: prefill attention of one prompt on the GPU (pipeline.py:139-180),
+    Gemma E2B layer types: sliding window 512 with head_dim 256 (28 of 35 layers) and full
+    causal with head_dim 512 (7 layers), 8 query heads on 1 KV head.  TFLOP/s counts the
+    useful products (keys each query may see), 4 * H * D per (query, key)."""
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(3)
+    for name, d, win in (("sliding_w512_d256", 256, 512), ("full_d512", 512, 0)):
+        sc = d ** -0.25
+        q = (torch.randn((8, m, d), device=dev, generator=g) * sc).to(torch.bfloat16)
+        k = (torch.randn((1, m, d), device=dev, generator=g) * sc).to(torch.bfloat16)
+        v = torch.randn((1, m, d), device=dev, generator=g).to(torch.bfloat16)
+        o = torch.empty_like(q)
+        gr = capture(lambda: w8.attention_prefill(q, k, v, win, out=o), stream)
+        ms = timed(lambda: gr.replay(), steps, warmup, stream, world) / steps
+        del gr
+        pos = torch.arange(m, dtype=torch.float64)
+        pairs = float(torch.clamp(pos + 1, max=win).sum()) if win else m * (m + 1) / 2
+        out[name] = {"us": ms * 1e3, "tflops": 4 * 8 * d * pairs / (ms * 1e-3) / 1e12}
+    out["per_prefill_ms"] = (28 * out["sliding_w512_d256"]["us"] + 7 * out["full_d512"]["us"]) / 1e3
+    out["workload"] = (f"one prompt of {m} tokens, 8 query heads on 1 KV head; per_prefill_ms = 28 sliding + "
+                       "7 full layers; bf16 mma.sync flash attention")
+    return out
+
+
 def sweep(w8, dev, stream, steps, warmup):
     """Config 3: each projection shape over 35 layers at M in {207, 858, 1878, 3658}, with
     and without the reference's 512-row padding (TOPS on the unpadded rows); plus the real
@@ -716,6 +741,7 @@ def main():
         if not args.no_fused and args.only is None:
             line["fused_gelu_up"] = fused_gelu_up(w8, work, dev, stream, 10, 3, world)
             line["fused_layer"] = fused_layer(w8, dev, stream, args.m, 5, 3, world)
+            line["attention"] = attention_bench(w8, dev, stream, args.m, 10, 3, world)
         if not args.no_config4 and args.only is None:
             line["config4"] = {"prompts_dp": prompts_dp(w8, dev, stream, world, rank, 3, 3),
                                "lm_head_sharded": sharded_head(w8, dev, stream, world, 50, 5, pk)}
