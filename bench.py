@@ -636,6 +636,7 @@ def main():
     ap.add_argument("--sweep", action="store_true", help="config 3: per-shape M sweep, padded vs unpadded (own JSON line)")
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 prompts / sharded LM head objects")
     ap.add_argument("--no-fused", action="store_true", help="skip the fused gate/up glue object")
+    ap.add_argument("--no-attention", action="store_true", help="skip the prefill attention object")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -741,6 +742,7 @@ def main():
         if not args.no_fused and args.only is None:
             line["fused_gelu_up"] = fused_gelu_up(w8, work, dev, stream, 10, 3, world)
             line["fused_layer"] = fused_layer(w8, dev, stream, args.m, 5, 3, world)
+        if not args.no_attention and args.only is None:
             line["attention"] = attention_bench(w8, dev, stream, args.m, 10, 3, world)
         if not args.no_config4 and args.only is None:
             line["config4"] = {"prompts_dp": prompts_dp(w8, dev, stream, world, rank, 3, 3),

@@ -12,8 +12,8 @@
 // query rows.  Per 64-key tile: S = Q K^T (fragments from swizzled shared memory with
 // ldmatrix), online softmax in registers (log2 domain, exp2), O += P V with P reused from
 // the S accumulators as the A operand.  Key tiles outside the causal / window range are
-// skipped; the boundary tiles are masked.  D = 512 (full-attention layers) runs as two
-// 256-column halves of O, each recomputing S.
+// skipped; the boundary tiles are masked.  D = 512 (full-attention layers) runs two
+// groups of 4 warps, one per 256-column half of O, sharing one S through shared memory.
 #include "common.cuh"
 
 namespace w8 {
@@ -48,11 +48,11 @@ __device__ __forceinline__ void cp_async_wait_all() {
 
 // rows x D bf16 from global (row pitch `pitch`, rows >= `valid_rows` zero-filled) into a
 // swizzled tile; columns [c0, c0 + D) of the source.
-template <int D, int ROWS>
+template <int D, int ROWS, int PARTS>
 __device__ __forceinline__ void load_tile(uint32_t base, const __nv_bfloat16* src, int64_t pitch, int valid_rows,
                                           int c0) {
   constexpr int kChunks = ROWS * D / 8;
-  for (int i = threadIdx.x; i < kChunks; i += 32 * kAttnWarps) {
+  for (int i = threadIdx.x; i < kChunks; i += 32 * kAttnWarps * PARTS) {
     const int r = i / (D / 8), c = i % (D / 8);
     const bool ok = r < valid_rows;
     const __nv_bfloat16* p = src + (ok ? static_cast<int64_t>(r) * pitch : 0) + c0 + c * 8;
@@ -87,25 +87,35 @@ __device__ __forceinline__ float exp2_approx(float x) {
   return y;
 }
 
+// PARTS = D / 256 warp groups of 4 warps; group gi owns output columns [256 gi, 256 gi + 256)
+// of the CTA's 64 queries.  Group 0 computes S and the softmax; with two groups it hands P
+// (bf16) and the per-row rescale factors over through shared memory, so S is computed
+// once for D = 512.
 template <int D>
-__global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(32 * kAttnWarps * (D / kAttnDO)) attention_kernel(const AttnArgs a) {
+  constexpr int PARTS = D / kAttnDO;
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t sq = smem_u32(smem);
   const uint32_t sk = sq + kAttnBM * D * 2;
   const uint32_t sv = sk + kAttnBN * D * 2;
+  const uint32_t sp = sv + kAttnBN * D * 2;  // P [64 queries x 64 keys] bf16 (PARTS > 1)
+  float* stat = reinterpret_cast<float*>(smem + (kAttnBM + 2 * kAttnBN) * D * 2 + kAttnBM * kAttnBN * 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * kAttnBM;
+  const int wg = warp / kAttnWarps, wr = warp % kAttnWarps;  // warp group, warp within it
+  // Heaviest query tiles (most keys under the causal mask) are scheduled first.
+  const int q0 = (gridDim.x - 1 - blockIdx.x) * kAttnBM;
   const int head = blockIdx.y;
-  const int c0 = blockIdx.z * kAttnDO;  // output columns of this CTA
+  const int c0 = wg * kAttnDO;  // this group's output columns
   const int kvh = head / (a.heads / a.kv_heads);
   const __nv_bfloat16* qh = a.q + head * a.q_head + static_cast<int64_t>(q0) * a.q_tok;
   const __nv_bfloat16* kh = a.k + kvh * a.k_head;
   const __nv_bfloat16* vh = a.v + kvh * a.v_head;
 
-  load_tile<D, kAttnBM>(sq, qh, a.q_tok, a.t - q0, 0);
+  load_tile<D, kAttnBM, PARTS>(sq, qh, a.q_tok, a.t - q0, 0);
 
   const int g = lane >> 2, qd = lane & 3;  // mma fragment row group / column pair
-  const int row_a = q0 + warp * 16 + g, row_b = row_a + 8;
+  const int lr_a = wr * 16 + g, lr_b = lr_a + 8;  // rows within the CTA's 64
+  const int row_a = q0 + lr_a, row_b = q0 + lr_b;
   float o[kAttnDO / 8][4];
 #pragma unroll
   for (int j = 0; j < kAttnDO / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
@@ -116,64 +126,91 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const AttnAr
   const int first_key = a.window > 0 ? max(0, q0 - a.window + 1) : 0;
   for (int kt = first_key / kAttnBN; kt * kAttnBN <= last_key; ++kt) {
     const int k0 = kt * kAttnBN;
-    __syncthreads();  // the previous tile's K / V are consumed
-    load_tile<D, kAttnBN>(sk, kh + static_cast<int64_t>(k0) * a.k_tok, a.k_tok, a.t - k0, 0);
-    load_tile<kAttnDO, kAttnBN>(sv, vh + static_cast<int64_t>(k0) * a.v_tok, a.v_tok, a.t - k0, c0);
+    __syncthreads();  // the previous tile's K / V / P are consumed
+    load_tile<D, kAttnBN, PARTS>(sk, kh + static_cast<int64_t>(k0) * a.k_tok, a.k_tok, a.t - k0, 0);
+    load_tile<D, kAttnBN, PARTS>(sv, vh + static_cast<int64_t>(k0) * a.v_tok, a.v_tok, a.t - k0, 0);
     cp_async_wait_all();
     __syncthreads();
 
-    // S = Q K^T for this warp's 16 rows x 64 keys.
-    float s[kAttnBN / 8][4];
-#pragma unroll
-    for (int j = 0; j < kAttnBN / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll 4
-    for (int kk = 0; kk < D / 16; ++kk) {
-      uint32_t af[4];
-      ldsm_x4(tile_addr<D>(sq, warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * kk + (lane >> 4)), af);
-#pragma unroll
-      for (int jj = 0; jj < kAttnBN / 16; ++jj) {
-        uint32_t bf[4];
-        ldsm_x4(tile_addr<D>(sk, jj * 16 + (lane & 7) + 8 * (lane >> 4), 2 * kk + ((lane >> 3) & 1)), bf);
-        mma_bf16(s[2 * jj], af, bf[0], bf[1]);
-        mma_bf16(s[2 * jj + 1], af, bf[2], bf[3]);
-      }
-    }
-    // Mask (causal, window, keys past T), then the online softmax in the log2 domain.
-    float mx_a = -INFINITY, mx_b = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < kAttnBN / 8; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = k0 + j * 8 + 2 * qd + (e & 1);
-        const int row = e < 2 ? row_a : row_b;
-        float v = s[j][e] * kLog2e;
-        if (key > row || key >= a.t || (a.window > 0 && row - key >= a.window)) v = -INFINITY;
-        s[j][e] = v;
-        if (e < 2) mx_a = fmaxf(mx_a, v); else mx_b = fmaxf(mx_b, v);
-      }
-#pragma unroll
-    for (int sh = 1; sh <= 2; sh <<= 1) {
-      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, sh));
-      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, sh));
-    }
-    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-    const float ref_a = mn_a == -INFINITY ? 0.f : mn_a, ref_b = mn_b == -INFINITY ? 0.f : mn_b;
-    const float corr_a = exp2_approx(m_a - ref_a), corr_b = exp2_approx(m_b - ref_b);
-    m_a = mn_a;
-    m_b = mn_b;
-    float sum_a = 0.f, sum_b = 0.f;
     uint32_t p[kAttnBN / 8][2];
+    float corr_a = 1.f, corr_b = 1.f;
+    if (wg == 0) {
+      // S = Q K^T for this warp's 16 rows x 64 keys.
+      float s[kAttnBN / 8][4];
 #pragma unroll
-    for (int j = 0; j < kAttnBN / 8; ++j) {
-      const float p0 = exp2_approx(s[j][0] - ref_a), p1 = exp2_approx(s[j][1] - ref_a);
-      const float p2 = exp2_approx(s[j][2] - ref_b), p3 = exp2_approx(s[j][3] - ref_b);
-      sum_a += p0 + p1;
-      sum_b += p2 + p3;
-      p[j][0] = pack_bf16(p0, p1);
-      p[j][1] = pack_bf16(p2, p3);
+      for (int j = 0; j < kAttnBN / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll 4
+      for (int kk = 0; kk < D / 16; ++kk) {
+        uint32_t af[4];
+        ldsm_x4(tile_addr<D>(sq, wr * 16 + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * kk + (lane >> 4)), af);
+#pragma unroll
+        for (int jj = 0; jj < kAttnBN / 16; ++jj) {
+          uint32_t bf[4];
+          ldsm_x4(tile_addr<D>(sk, jj * 16 + (lane & 7) + 8 * (lane >> 4), 2 * kk + ((lane >> 3) & 1)), bf);
+          mma_bf16(s[2 * jj], af, bf[0], bf[1]);
+          mma_bf16(s[2 * jj + 1], af, bf[2], bf[3]);
+        }
+      }
+      // Mask (causal, window, keys past T), then the online softmax in the log2 domain.
+      float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kAttnBN / 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = k0 + j * 8 + 2 * qd + (e & 1);
+          const int row = e < 2 ? row_a : row_b;
+          float v = s[j][e] * kLog2e;
+          if (key > row || key >= a.t || (a.window > 0 && row - key >= a.window)) v = -INFINITY;
+          s[j][e] = v;
+          if (e < 2) mx_a = fmaxf(mx_a, v); else mx_b = fmaxf(mx_b, v);
+        }
+#pragma unroll
+      for (int sh = 1; sh <= 2; sh <<= 1) {
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, sh));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, sh));
+      }
+      const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+      const float ref_a = mn_a == -INFINITY ? 0.f : mn_a, ref_b = mn_b == -INFINITY ? 0.f : mn_b;
+      corr_a = exp2_approx(m_a - ref_a);
+      corr_b = exp2_approx(m_b - ref_b);
+      m_a = mn_a;
+      m_b = mn_b;
+      float sum_a = 0.f, sum_b = 0.f;
+#pragma unroll
+      for (int j = 0; j < kAttnBN / 8; ++j) {
+        const float p0 = exp2_approx(s[j][0] - ref_a), p1 = exp2_approx(s[j][1] - ref_a);
+        const float p2 = exp2_approx(s[j][2] - ref_b), p3 = exp2_approx(s[j][3] - ref_b);
+        sum_a += p0 + p1;
+        sum_b += p2 + p3;
+        p[j][0] = pack_bf16(p0, p1);
+        p[j][1] = pack_bf16(p2, p3);
+      }
+      l_a = l_a * corr_a + sum_a;
+      l_b = l_b * corr_b + sum_b;
+      if constexpr (PARTS > 1) {
+        // Hand P and the rescale factors to the other group(s): P[row][key] in a
+        // swizzled [64 x 64] bf16 tile (the A operand layout ldmatrix reads below).
+#pragma unroll
+        for (int j = 0; j < kAttnBN / 8; ++j) {
+          const uint32_t col_bytes = (j * 8 + 2 * qd) * 2;
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(tile_addr<kAttnBN>(sp, lr_a, j) + (col_bytes & 15)),
+                       "r"(p[j][0]));
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(tile_addr<kAttnBN>(sp, lr_b, j) + (col_bytes & 15)),
+                       "r"(p[j][1]));
+        }
+        if (qd == 0) {
+          stat[lr_a] = corr_a;
+          stat[lr_b] = corr_b;
+        }
+      }
     }
-    l_a = l_a * corr_a + sum_a;
-    l_b = l_b * corr_b + sum_b;
+    if constexpr (PARTS > 1) {
+      __syncthreads();  // P and the factors are in shared memory
+      if (wg != 0) {
+        corr_a = stat[lr_a];
+        corr_b = stat[lr_b];
+      }
+    }
 #pragma unroll
     for (int j = 0; j < kAttnDO / 8; ++j) {
       o[j][0] *= corr_a;
@@ -181,24 +218,42 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(const AttnAr
       o[j][2] *= corr_b;
       o[j][3] *= corr_b;
     }
-    // O += P V.
+    // O += P V over this group's 256 columns.
 #pragma unroll
     for (int kk = 0; kk < kAttnBN / 16; ++kk) {
-      const uint32_t af[4] = {p[2 * kk][0], p[2 * kk][1], p[2 * kk + 1][0], p[2 * kk + 1][1]};
+      uint32_t af[4];
+      if constexpr (PARTS == 1) {
+        af[0] = p[2 * kk][0];
+        af[1] = p[2 * kk][1];
+        af[2] = p[2 * kk + 1][0];
+        af[3] = p[2 * kk + 1][1];
+      } else {
+        ldsm_x4(tile_addr<kAttnBN>(sp, wr * 16 + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * kk + (lane >> 4)), af);
+      }
 #pragma unroll
       for (int jj = 0; jj < kAttnDO / 16; ++jj) {
         uint32_t bf[4];
-        ldsm_x4_t(tile_addr<kAttnDO>(sv, kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * jj + (lane >> 4)), bf);
+        ldsm_x4_t(tile_addr<D>(sv, kk * 16 + (lane & 7) + 8 * ((lane >> 3) & 1), c0 / 8 + 2 * jj + (lane >> 4)), bf);
         mma_bf16(o[2 * jj], af, bf[0], bf[1]);
         mma_bf16(o[2 * jj + 1], af, bf[2], bf[3]);
       }
     }
   }
-  // Row sums live spread over the quad: reduce, normalise, store bf16.
+  // Row sums live spread over group 0's quads: reduce, share, normalise, store bf16.
 #pragma unroll
   for (int sh = 1; sh <= 2; sh <<= 1) {
     l_a += __shfl_xor_sync(0xffffffffu, l_a, sh);
     l_b += __shfl_xor_sync(0xffffffffu, l_b, sh);
+  }
+  if constexpr (PARTS > 1) {
+    __syncthreads();
+    if (wg == 0 && qd == 0) {
+      stat[kAttnBM + lr_a] = l_a;
+      stat[kAttnBM + lr_b] = l_b;
+    }
+    __syncthreads();
+    l_a = stat[kAttnBM + lr_a];
+    l_b = stat[kAttnBM + lr_b];
   }
   const float inv_a = l_a > 0.f ? 1.f / l_a : 0.f, inv_b = l_b > 0.f ? 1.f / l_b : 0.f;
   __nv_bfloat16* oh = a.o + head * a.o_head + c0;
@@ -222,7 +277,7 @@ int require_sm100(int* device);
 
 template <int D>
 static int attention_go(const w8::AttnArgs& a, cudaStream_t stream) {
-  constexpr int smem = (w8::kAttnBM + w8::kAttnBN) * D * 2 + w8::kAttnBN * w8::kAttnDO * 2;
+  constexpr int smem = (w8::kAttnBM + 2 * w8::kAttnBN) * D * 2 + w8::kAttnBM * w8::kAttnBN * 2 + 2 * w8::kAttnBM * 4;
   auto kern = w8::attention_kernel<D>;
   static bool done[64] = {};
   int device = 0;
@@ -232,9 +287,8 @@ static int attention_go(const w8::AttnArgs& a, cudaStream_t stream) {
     W8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     done[device] = true;
   }
-  const dim3 grid(static_cast<unsigned>((a.t + w8::kAttnBM - 1) / w8::kAttnBM), static_cast<unsigned>(a.heads),
-                  D / w8::kAttnDO);
-  kern<<<grid, 32 * w8::kAttnWarps, smem, stream>>>(a);
+  const dim3 grid(static_cast<unsigned>((a.t + w8::kAttnBM - 1) / w8::kAttnBM), static_cast<unsigned>(a.heads), 1);
+  kern<<<grid, 32 * w8::kAttnWarps * (D / w8::kAttnDO), smem, stream>>>(a);
   return cuda_status(cudaGetLastError());
 }
 
