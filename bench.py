@@ -460,6 +460,66 @@ def fused_layer(w8, dev, stream, m, steps, warmup, world, layers=35):
             "unfused": "int32 GEMMs + dequant / quant kernels + the reference's glue as torch ops on the same GPU"}
 
 
+def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35):
+    """One prompt through every decoder layer's linear set, glue and attention on the GPU:
+    k_in, qkv GEMM + k_qkv, attention, k_attn_out, o GEMM + k_post_attn, gate/up GEMM +
+    k_gelu, down GEMM + k_post_ff.  Gemma E2B attention layout: every 5th layer full causal
+    with head_dim 512 (qkv 5120 x 1536, o 1536 x 4096), the others sliding window 512 with
+    head_dim 256; 8 query heads on 1 KV head; no KV sharing and no per-layer-input (PLE)
+    branch.  Random weights; the residual stream is carried from layer to layer."""
+    eps, nh, kv, hid = 1e-6, 8, 1, 1536
+    g = torch.Generator(device=dev).manual_seed(91)
+
+    def wq(n, k):
+        return w8.quant_rows(torch.randn((n, k), device=dev, generator=g, dtype=torch.bfloat16) * 0.02)
+
+    def nw(n):
+        return (1 + 0.1 * torch.randn((n,), device=dev, generator=g)).to(torch.bfloat16)
+
+    def rope(d, base):
+        ang = torch.arange(m, device=dev)[:, None].float() * (base ** (-torch.arange(0, d, 2, device=dev).float() / d))[None]
+        ang = torch.cat([ang, ang], dim=-1)
+        return ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+
+    tables = {256: rope(256, 1e4), 512: rope(512, 1e6)}
+    L = []
+    for i in range(layers):
+        d, win = (512, 0) if i % 5 == 4 else (256, 512)
+        L.append(dict(d=d, win=win, qkv=wq((nh + 2 * kv) * d, hid), o=wq(hid, nh * d),
+                      gup=w8.pack_gelu_up(*wq(12288, hid)), dn=wq(hid, 6144), w_in=nw(hid), qn=nw(d), kn=nw(d),
+                      w_post=nw(hid), w_pre=nw(hid), w_pff=nw(hid)))
+    h0 = torch.randn((m, hid), device=dev, generator=g).to(torch.bfloat16)
+    h = torch.empty_like(h0)
+
+    def step():
+        h.copy_(h0)
+        for l in L:
+            d = l["d"]
+            xq, sx = w8.rms_quant(h, l["w_in"], eps)
+            y = w8.gemm_dequant(xq, l["qkv"][0], sx, l["qkv"][1])
+            q, k, v = w8.qkv_norm_rope(y, *tables[d], l["qn"], l["kn"], eps, nh, kv, d)
+            o = w8.attention_prefill(q, k, v, l["win"])
+            xq, sx = w8.attn_out_quant(o)
+            y = w8.gemm_dequant(xq, l["o"][0], sx, l["o"][1])
+            _, xq, sx = w8.post_norm_quant(y, h, l["w_post"], l["w_pre"], eps, h=h)
+            xq, sx = w8.gelu_up_quant(xq, sx, *l["gup"])
+            y = w8.gemm_dequant(xq, l["dn"][0], sx, l["dn"][1])
+            w8.post_norm_quant(y, h, l["w_pff"], None, eps, h=h)
+
+    gr = capture(step, stream)
+    ms = timed(lambda: gr.replay(), steps, warmup, stream, world) / steps
+    del gr
+    assert torch.isfinite(h.float()).all()
+    linear_ops = sum(2 * m * (l["qkv"][0].numel() + l["o"][0].numel() + l["gup"][0].numel() + l["dn"][0].numel())
+                     for l in L)
+    return {"workload": f"{layers} decoder layers of one {m}-token prompt on the GPU (linear set + glue + attention; "
+                        "every 5th layer full attention with head_dim 512, others sliding window 512 / head_dim 256; "
+                        "no KV sharing, no PLE branch)",
+            "ms_per_prefill": ms, "linear_tops": linear_ops / (ms * 1e-3) / 1e12,
+            "reference": "the reference keeps its NPU busy 2.38 s per 3658-token prefill (README.md:61-62), its CPU "
+                         "attention on top"}
+
+
 def attention_bench(w8, dev, stream, m, steps, warmup, world):
     """SURVEY next row 4: prefill attention of one prompt on the GPU (pipeline.py:139-180),
     Gemma E2B layer types: sliding window 512 with head_dim 256 (28 of 35 layers) and full
@@ -744,6 +804,7 @@ def main():
             line["fused_layer"] = fused_layer(w8, dev, stream, args.m, 5, 3, world)
         if not args.no_attention and args.only is None:
             line["attention"] = attention_bench(w8, dev, stream, args.m, 10, 3, world)
+            line["prefill_gpu"] = prefill_gpu(w8, dev, stream, args.m, 3, 3, world)
         if not args.no_config4 and args.only is None:
             line["config4"] = {"prompts_dp": prompts_dp(w8, dev, stream, world, rank, 3, 3),
                                "lm_head_sharded": sharded_head(w8, dev, stream, world, 50, 5, pk)}

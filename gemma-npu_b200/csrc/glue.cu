@@ -13,8 +13,8 @@
 // lane-then-warp tree (ATen's CPU order differs), so the last bit of the mean may differ
 // from the reference: a bf16 output can move by one bf16 step, an int8 code by one.
 //
-// One warp per row, the row in registers (N <= 2048, N % 8 == 0, 16-byte rows), eight
-// rows per 256-thread CTA: no shared memory and no block barrier.
+// One warp per row, the row in registers (N <= 2048, N % 8 == 0, 16-byte rows; H * D <= 4096
+// for k_attn_out), eight rows per 256-thread CTA; the norm weights staged in shared memory.
 #include "common.cuh"
 #include "rowquant.cuh"
 
@@ -22,6 +22,7 @@ namespace w8 {
 
 constexpr int kGlueWarps = 8;
 constexpr int kGlueMaxVecs = 8;  // 16-byte vectors per lane: N <= 32 * 8 * 8 = 2048
+constexpr int kGlueMaxVecsAttn = 16;  // k_attn_out rows: H * D <= 4096 (head_dim 512 layers)
 
 enum GlueMode : int { kGlueIn = 0, kGluePost1 = 1, kGluePost2 = 2, kGlueAttnOut = 3 };
 
@@ -97,9 +98,10 @@ __device__ __forceinline__ float rbf16(float v) { return __bfloat162float(__floa
 template <int MODE>
 __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, int nv, const uint4* w1s,
                                          const uint4* w2s) {
-  uint4 v[kGlueMaxVecs];
+  constexpr int kMax = MODE == kGlueAttnOut ? kGlueMaxVecsAttn : kGlueMaxVecs;
+  uint4 v[kMax];
 #pragma unroll
-  for (int i = 0; i < kGlueMaxVecs; ++i) {
+  for (int i = 0; i < kMax; ++i) {
     const int vi = lane + 32 * i;
     if (vi < nv) {
       if constexpr (MODE == kGlueAttnOut) {
@@ -114,12 +116,12 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
     uint4 res[MODE == kGlueIn ? 1 : kGlueMaxVecs];
     if constexpr (MODE != kGlueIn) {
 #pragma unroll
-      for (int i = 0; i < kGlueMaxVecs; ++i)
+      for (int i = 0; i < kMax; ++i)
         if (lane + 32 * i < nv) res[i] = ld16(a.res + static_cast<int64_t>(row) * a.ldr + (lane + 32 * i) * 8);
     }
     const float r1 = rms_factor(v, nv, lane, a.n, a.eps);
 #pragma unroll
-    for (int i = 0; i < kGlueMaxVecs; ++i) {
+    for (int i = 0; i < kMax; ++i) {
       const int vi = lane + 32 * i;
       if (vi < nv) {
         float x[8], w[8];
@@ -140,7 +142,7 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
     if constexpr (MODE == kGluePost2) {
       const float r2 = rms_factor(v, nv, lane, a.n, a.eps);
 #pragma unroll
-      for (int i = 0; i < kGlueMaxVecs; ++i) {
+      for (int i = 0; i < kMax; ++i) {
         const int vi = lane + 32 * i;
         if (vi < nv) {
           float x[8], w[8];
@@ -156,7 +158,7 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
   // _quant of the row.
   float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < kGlueMaxVecs; ++i)
+  for (int i = 0; i < kMax; ++i)
     if (lane + 32 * i < nv) {
       float x[8];
       unpack8(v[i], x);
@@ -168,7 +170,7 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
   const float rc = __frcp_rn(sc);
   if (lane == 0) a.s[row] = sc;
 #pragma unroll
-  for (int i = 0; i < kGlueMaxVecs; ++i) {
+  for (int i = 0; i < kMax; ++i) {
     const int vi = lane + 32 * i;
     if (vi < nv) {
       float x[8];
@@ -324,8 +326,9 @@ static int glue_go(Kernel kern, const w8::GlueArgs& a, cudaStream_t stream) {
 static int glue_launch(int mode, const w8::GlueArgs& a, cudaStream_t stream) {
   W8_CHECK_ARG(a.t >= 0 && a.n >= 0, "negative size");
   if (a.t == 0) return W8_OK;
-  W8_CHECK_ARG(a.n > 0 && a.n % 8 == 0 && a.n <= 32 * 8 * w8::kGlueMaxVecs,
-               "row length %d must be a multiple of 8 and at most %d", a.n, 32 * 8 * w8::kGlueMaxVecs);
+  const int max_n = 32 * 8 * (mode == w8::kGlueAttnOut ? w8::kGlueMaxVecsAttn : w8::kGlueMaxVecs);
+  W8_CHECK_ARG(a.n > 0 && a.n % 8 == 0 && a.n <= max_n, "row length %d must be a multiple of 8 and at most %d", a.n,
+               max_n);
   W8_CHECK_ARG(a.x != nullptr && a.q != nullptr && a.s != nullptr, "null pointer");
   W8_CHECK_ALIGN(aligned(a.x, 16) && a.ldx % 8 == 0, "x must be 16-byte aligned with a pitch %% 8 == 0");
   W8_CHECK_ALIGN(aligned(a.q, 8) && a.ldq % 8 == 0 && a.ldq >= a.n, "q must be 8-byte aligned, ldq %% 8 == 0, ldq >= n");

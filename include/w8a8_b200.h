@@ -155,7 +155,8 @@ int w8_post_norm_quant_bf16(const uint16_t* y, int64_t ldy, const uint16_t* res,
 
 /* k_attn_out (pipeline.py:88-92): the attention output o [H, T, D] (bf16; element
  * (h, t, d) at o[h * ld_head + t * ld_tok + d]) quantised per token over its H * D
- * values: q [T, H * D] int8, s [T] fp32.  Bit-exact (no reduction but the absmax). */
+ * values (H * D <= 4096): q [T, H * D] int8, s [T] fp32.  Bit-exact (no reduction but the
+ * absmax). */
 int w8_attn_out_quant_bf16(const uint16_t* o, int64_t ld_head, int64_t ld_tok, int8_t* q,
                            int64_t ldq, float* s, int64_t t, int64_t heads, int64_t head_dim,
                            w8_stream_t stream);

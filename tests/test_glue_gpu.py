@@ -112,9 +112,11 @@ def test_gemm_then_post_norm_matches_oracle(cuda, t, n, two):
     np.testing.assert_allclose(s[rows].cpu().numpy(), sr, rtol=2.0 ** -7)
 
 
-def test_attn_out_strided_bit_exact(cuda):
-    """o as attention produces it ([H, T, D], here a slice of a wider buffer)."""
-    H, T, D = 8, 1000, 256
+@pytest.mark.parametrize("d", [256, 512])
+def test_attn_out_strided_bit_exact(cuda, d):
+    """o as attention produces it ([H, T, D], here a slice of a wider buffer); D = 512 is a
+    full-attention layer (H * D = 4096)."""
+    H, T, D = 8, 1000, d
     gen = torch.Generator(device=cuda).manual_seed(3)
     big = torch.randn((H, T + 24, D), device=cuda, generator=gen).to(torch.bfloat16)
     o = big[:, 10:10 + T]
