@@ -533,15 +533,18 @@ def attention_bench(w8, dev, stream, m, steps, warmup, world):
         k = (torch.randn((1, m, d), device=dev, generator=g) * sc).to(torch.bfloat16)
         v = torch.randn((1, m, d), device=dev, generator=g).to(torch.bfloat16)
         o = torch.empty_like(q)
-        gr = capture(lambda: w8.attention_prefill(q, k, v, win, out=o), stream)
-        ms = timed(lambda: gr.replay(), steps, warmup, stream, world) / steps
-        del gr
         pos = torch.arange(m, dtype=torch.float64)
         pairs = float(torch.clamp(pos + 1, max=win).sum()) if win else m * (m + 1) / 2
-        out[name] = {"us": ms * 1e3, "tflops": 4 * 8 * d * pairs / (ms * 1e-3) / 1e12}
+        for sched in ("tc", "mma"):
+            gr = capture(lambda: w8.attention_prefill(q, k, v, win, out=o, schedule=sched), stream)
+            ms = timed(lambda: gr.replay(), steps, warmup, stream, world) / steps
+            del gr
+            key = name if sched == "tc" else name + "_mma"
+            out[key] = {"us": ms * 1e3, "tflops": 4 * 8 * d * pairs / (ms * 1e-3) / 1e12}
     out["per_prefill_ms"] = (28 * out["sliding_w512_d256"]["us"] + 7 * out["full_d512"]["us"]) / 1e3
+    out["per_prefill_ms_mma"] = (28 * out["sliding_w512_d256_mma"]["us"] + 7 * out["full_d512_mma"]["us"]) / 1e3
     out["workload"] = (f"one prompt of {m} tokens, 8 query heads on 1 KV head; per_prefill_ms = 28 sliding + "
-                       "7 full layers; bf16 mma.sync flash attention")
+                       "7 full layers; tcgen05 flash attention (the *_mma keys: the mma.sync schedule)")
     return out
 
 

@@ -294,12 +294,18 @@ static int attention_go(const w8::AttnArgs& a, cudaStream_t stream) {
 
 }  // namespace w8host
 
-extern "C" int w8_attention_prefill_bf16(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k,
-                                         int64_t k_head, int64_t k_tok, const uint16_t* v, int64_t v_head,
-                                         int64_t v_tok, uint16_t* o, int64_t o_head, int64_t o_tok, int64_t t,
-                                         int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t window,
-                                         w8_stream_t stream) {
-  using namespace w8host;
+namespace w8host {
+
+int attention_tc(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k, int64_t k_head,
+                 int64_t k_tok, const uint16_t* v, int64_t v_head, int64_t v_tok, uint16_t* o, int64_t o_head,
+                 int64_t o_tok, int64_t t, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t window,
+                 int device, cudaStream_t stream);
+
+// Argument checks shared by both schedules, then the tcgen05 one (tc) or the mma.sync one.
+static int attention_entry(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k, int64_t k_head,
+                           int64_t k_tok, const uint16_t* v, int64_t v_head, int64_t v_tok, uint16_t* o,
+                           int64_t o_head, int64_t o_tok, int64_t t, int64_t heads, int64_t kv_heads,
+                           int64_t head_dim, int64_t window, w8_stream_t stream, bool tc) {
   W8_CHECK_ARG(t >= 0 && t < (1ll << 31) && heads >= 0 && kv_heads >= 0 && window >= 0, "bad size");
   if (t == 0 || heads == 0) return W8_OK;
   W8_CHECK_ARG(head_dim == 256 || head_dim == 512, "head_dim = %lld must be 256 or 512", (long long)head_dim);
@@ -316,6 +322,9 @@ extern "C" int w8_attention_prefill_bf16(const uint16_t* q, int64_t q_head, int6
   int device = 0;
   const int st = require_sm100(&device);
   if (st != W8_OK) return st;
+  if (tc)
+    return attention_tc(q, q_head, q_tok, k, k_head, k_tok, v, v_head, v_tok, o, o_head, o_tok, t, heads, kv_heads,
+                        head_dim, window, device, reinterpret_cast<cudaStream_t>(stream));
   w8::AttnArgs a;
   a.q = reinterpret_cast<const __nv_bfloat16*>(q);
   a.k = reinterpret_cast<const __nv_bfloat16*>(k);
@@ -329,4 +338,24 @@ extern "C" int w8_attention_prefill_bf16(const uint16_t* q, int64_t q_head, int6
   a.window = static_cast<int>(window);
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return head_dim == 256 ? attention_go<256>(a, s) : attention_go<512>(a, s);
+}
+
+}  // namespace w8host
+
+extern "C" int w8_attention_prefill_bf16(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k,
+                                         int64_t k_head, int64_t k_tok, const uint16_t* v, int64_t v_head,
+                                         int64_t v_tok, uint16_t* o, int64_t o_head, int64_t o_tok, int64_t t,
+                                         int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t window,
+                                         w8_stream_t stream) {
+  return w8host::attention_entry(q, q_head, q_tok, k, k_head, k_tok, v, v_head, v_tok, o, o_head, o_tok, t, heads,
+                                 kv_heads, head_dim, window, stream, true);
+}
+
+extern "C" int w8_attention_prefill_mma_bf16(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k,
+                                             int64_t k_head, int64_t k_tok, const uint16_t* v, int64_t v_head,
+                                             int64_t v_tok, uint16_t* o, int64_t o_head, int64_t o_tok, int64_t t,
+                                             int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t window,
+                                             w8_stream_t stream) {
+  return w8host::attention_entry(q, q_head, q_tok, k, k_head, k_tok, v, v_head, v_tok, o, o_head, o_tok, t, heads,
+                                 kv_heads, head_dim, window, stream, false);
 }

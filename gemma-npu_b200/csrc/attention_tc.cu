@@ -1,0 +1,494 @@
+// Prefill attention on the 5th-generation tensor cores (tcgen05, accumulators in TMEM): the
+// contract of attention.cu (pipeline.py:139-180, full_attention / sliding_attention with
+// q_start = 0: causal, window W > 0 or none, scale 1.0, grouped-query heads, bf16 in and
+// out, fp32 softmax and accumulation) on a schedule built for sm_100a.
+//
+// One CTA per (128 queries, head, 256-column half of the output): warp 0 loads with TMA,
+// warp 1 issues the MMAs, warps 2-5 run the softmax with one thread per query row (= TMEM
+// lane).  Per 64-key tile j:
+//   S_j  = Q K_j^T     tcgen05.mma kind::f16 (bf16 x bf16 -> fp32), two S buffers in TMEM
+//   P_j  = 2^(S_j log2(e) - m)   softmax threads: tcgen05.ld the row, mask, row max m and
+//                                sum l, P_j (bf16) into shared memory in the MMA A layout
+//   O   += P_j V_j     tcgen05.mma, O [128 x 256] fp32 in TMEM
+// The MMA warp issues S_{j+1} before O += P_j V_j, so the tensor core computes the next
+// scores while the softmax threads work on these.  A row's reference maximum m moves only
+// when the tile maximum exceeds it by more than 8 (log2 units): P is then <= 2^8 (exact
+// range in bf16 and fp32), O is rescaled in TMEM (tcgen05.ld / st) only on such moves, and
+// the final O / l is the same softmax.  head_dim 512 runs two CTAs per query tile, one per
+// output half, each computing the full S (the TMEM of one SM holds S and a 256-column O,
+// not a 512-column one).
+//
+// Shared memory: Q resident (head_dim / 64 swizzled [128 x 64] blocks), a ring of 16 KB
+// slots each holding 64 keys x 128 columns of K or V (two swizzled [64 x 64] blocks; loaded
+// in the order the MMA warp consumes them: K tiles for S, V tiles for O), and two P buffers.
+// Every mbarrier wait is bounded; on a timeout the kernel records W8_ERR_DEVICE_TIMEOUT,
+// drains its own copies and MMAs, frees TMEM and returns.
+#include "common.cuh"
+
+#include <mutex>
+
+namespace w8 {
+
+__device__ int g_attn_status = 0;
+
+constexpr int kTcBM = 128;                  // queries per CTA (TMEM lanes)
+constexpr int kTcBN = 64;                   // keys per tile
+constexpr int kTcDV = 256;                  // output columns per CTA
+constexpr int kTcThreads = 192;             // TMA warp, MMA warp, 4 softmax warps
+constexpr int kSlotBytes = kTcBN * 128 * 2; // 64 keys x 128 bf16 columns
+constexpr int kPBytes = kTcBM * kTcBN * 2;  // one P tile
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 2 * kTcBN;       // S buffers at columns 0 and 64, O from 128
+
+template <int D>
+struct TcCfg {
+  static constexpr int kQBytes = kTcBM * D * 2;
+  static constexpr int kSlots = D == 256 ? 8 : 4;
+  static constexpr int kKSlots = D / 128;       // ring slots per K tile
+  static constexpr int kVSlots = kTcDV / 128;   // ring slots per V tile
+  static constexpr int kOffRing = kQBytes;
+  static constexpr int kOffP = kOffRing + kSlots * kSlotBytes;
+  static constexpr int kOffBar = kOffP + 2 * kPBytes;
+  // full[kSlots], empty[kSlots], q_full, s_full[2], s_empty[2], p_full[2], p_empty[2], o_ready
+  static constexpr int kNumBars = 2 * kSlots + 10;
+  static constexpr int kSmem = kOffBar + kNumBars * 8 + 16 + 1024;
+  static_assert(kSmem <= 232448, "shared memory budget exceeded");
+};
+
+struct AttnTcArgs {
+  __nv_bfloat16* o;
+  int64_t o_head, o_tok;
+  int t, heads, kv_heads, window;
+};
+
+// kind::f16 instruction descriptor: bf16 A and B, fp32 D, M x N, A K-major, B K- or MN-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool b_mn_major) {
+  return (1u << 4)                                 // D format: F32
+         | (1u << 7)                               // A format: BF16
+         | (1u << 10)                              // B format: BF16
+         | ((b_mn_major ? 1u : 0u) << 16)          // B major
+         | (static_cast<uint32_t>(n >> 3) << 17)   // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
+}
+
+__device__ __forceinline__ void mma_bf16_tc(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 4-D tiled load (no multicast), completion counted on `bar` in bytes.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int x, int y, int z,
+                                            int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
+// Warp-wide registers -> TMEM, the inverse of tmem_ld_32x32b_x32.
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float ex2_tc(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const AttnTcArgs a) {
+  using C = TcCfg<D>;
+  constexpr int kSplit = D / kTcDV;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw);
+  const uint32_t ring = base + C::kOffRing;
+  const uint32_t bar0 = base + C::kOffBar;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffBar + C::kNumBars * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  auto full_bar = [&](uint32_t s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](uint32_t s) { return bar0 + 8u * (C::kSlots + s); };
+  const uint32_t q_full = bar0 + 8u * (2 * C::kSlots);
+  auto s_full = [&](int b) { return q_full + 8u * (1 + b); };
+  auto s_empty = [&](int b) { return q_full + 8u * (3 + b); };
+  auto p_full = [&](int b) { return q_full + 8u * (5 + b); };
+  auto p_empty = [&](int b) { return q_full + 8u * (7 + b); };
+  const uint32_t o_ready = q_full + 8u * 9;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Heaviest query tiles first: block ids run over (head, half) fastest, query tiles last.
+  const int per_tile = a.heads * kSplit;
+  const int qtiles = gridDim.x / per_tile;
+  const int qt = qtiles - 1 - static_cast<int>(blockIdx.x) / per_tile;
+  const int rest = static_cast<int>(blockIdx.x) % per_tile;
+  const int head = rest / kSplit, half = rest % kSplit;
+  const int q0 = qt * kTcBM;
+  const int kvh = head / (a.heads / a.kv_heads);
+  const int last_key = min(q0 + kTcBM, a.t) - 1;
+  const int first_key = a.window > 0 ? max(0, q0 - a.window + 1) : 0;
+  const int kt0 = first_key / kTcBN;
+  const int ntiles = last_key / kTcBN - kt0 + 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kSlots; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(s_full(b), 1);
+      mbar_init(s_empty(b), 4);  // the four softmax warps
+      mbar_init(p_full(b), 4);
+      mbar_init(p_empty(b), 1);
+    }
+    mbar_init(o_ready, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer: Q once, then the ring in the MMA warp's order
+      mbar_arrive_expect_tx(q_full, C::kQBytes);
+      tma_load_4d(base, &tm_q, q_full, 0, q0, 0, head);
+      uint32_t g = 0;
+      bool ok = true;
+      auto put = [&](const CUtensorMap* m, int key0, int chunk0) {
+        if (!ok) return;
+        const uint32_t slot = g % C::kSlots, use = g / C::kSlots;
+        ok = mbar_wait_bounded(empty_bar(slot), (use & 1u) ^ 1u, abort_flag, &g_attn_status);
+        if (!ok) return;
+        mbar_arrive_expect_tx(full_bar(slot), kSlotBytes);
+        tma_load_4d(ring + slot * kSlotBytes, m, full_bar(slot), 0, key0, chunk0, kvh);
+        ++g;
+      };
+      for (int p = 0; p < C::kKSlots; ++p) put(&tm_k, kt0 * kTcBN, 2 * p);
+      for (int i = 0; i < ntiles && ok; ++i) {
+        if (i + 1 < ntiles)
+          for (int p = 0; p < C::kKSlots; ++p) put(&tm_k, (kt0 + i + 1) * kTcBN, 2 * p);
+        for (int p = 0; p < C::kVSlots; ++p) put(&tm_v, (kt0 + i) * kTcBN, half * (kTcDV / 64) + 2 * p);
+      }
+      // Drain: every copy issued has landed before the CTA may exit.
+      mbar_wait_bounded(q_full, 0, nullptr, &g_attn_status);
+      for (uint32_t h = g > static_cast<uint32_t>(C::kSlots) ? g - C::kSlots : 0; h < g; ++h)
+        mbar_wait_bounded(full_bar(h % C::kSlots), (h / C::kSlots) & 1u, nullptr, &g_attn_status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer
+      constexpr uint32_t id_s = idesc_bf16(kTcBM, kTcBN, false);
+      constexpr uint32_t id_o = idesc_bf16(kTcBM, 128, true);
+      uint32_t g = 0;
+      bool ok = mbar_wait_bounded(q_full, 0, abort_flag, &g_attn_status);
+      auto take = [&]() {
+        const uint32_t slot = g % C::kSlots, use = g / C::kSlots;
+        ok = ok && mbar_wait_bounded(full_bar(slot), use & 1u, abort_flag, &g_attn_status);
+        return slot;
+      };
+      auto issue_s = [&](int i) {
+        const int b = i & 1;
+        ok = ok && mbar_wait_bounded(s_empty(b), ((i >> 1) & 1) ^ 1u, abort_flag, &g_attn_status);
+        for (int p = 0; p < C::kKSlots && ok; ++p) {
+          const uint32_t slot = take();
+          if (!ok) return;
+          tc_fence_after();
+          const uint32_t sk = ring + slot * kSlotBytes;
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16_tc(tmem + b * kTcBN,
+                          smem_desc_sw128(base + (2 * p + c) * (kTcBM * 128) + kk * 32, 16, 1024),
+                          smem_desc_sw128(sk + c * (kTcBN * 128) + kk * 32, 16, 1024), id_s,
+                          (p | c | kk) ? 1u : 0u);
+          mma_commit(empty_bar(slot));
+          ++g;
+        }
+        if (ok) mma_commit(s_full(b));
+      };
+      issue_s(0);
+      for (int i = 0; i < ntiles && ok; ++i) {
+        if (i + 1 < ntiles) issue_s(i + 1);
+        const int b = i & 1;
+        ok = ok && mbar_wait_bounded(p_full(b), (i >> 1) & 1, abort_flag, &g_attn_status);
+        const uint32_t sp = base + C::kOffP + b * kPBytes;
+        for (int p = 0; p < C::kVSlots && ok; ++p) {
+          const uint32_t slot = take();
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t sv = ring + slot * kSlotBytes;
+          // B = V [16 keys x 128 columns] MN-major: 64-column blocks 8 KB apart (LBO),
+          // 8-key groups 1 KB apart (SBO); the next 16 keys start 2 KB further.
+#pragma unroll
+          for (int kk = 0; kk < kTcBN / 16; ++kk)
+            mma_bf16_tc(tmem + kColO + p * 128, smem_desc_sw128(sp + kk * 32, 16, 1024),
+                        smem_desc_sw128(sv + kk * 16 * 128, kTcBN * 128, 1024), id_o, (i | kk) ? 1u : 0u);
+          mma_commit(empty_bar(slot));
+          ++g;
+        }
+        if (ok) mma_commit(p_empty(b));
+      }
+      mma_commit(o_ready);
+      // Drain: no MMA may still write TMEM when it is freed.
+      mbar_wait_bounded(o_ready, 0, nullptr, &g_attn_status);
+    }
+  } else {
+    // ---- softmax: thread = query row q0 + r = TMEM lane r (warp w reads lanes 32 (w % 4) ..)
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int qpos = q0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    constexpr float kLog2e = 1.4426950408889634f;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int i = 0; i < ntiles; ++i) {
+      const int b = i & 1, k0 = (kt0 + i) * kTcBN;
+      ok = mbar_wait_bounded(s_full(b), (i >> 1) & 1, abort_flag, &g_attn_status);
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s0[32], s1[32];
+      tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN, s0);
+      tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN + 32, s1);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_empty(b));  // the S buffer may be overwritten
+      float x[kTcBN];
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kTcBN; ++c) {
+        const int key = k0 + c;
+        float v = __uint_as_float(c < 32 ? s0[c] : s1[c - 32]) * kLog2e;
+        if (key > qpos || key >= a.t || (a.window > 0 && qpos - key >= a.window)) v = -INFINITY;
+        x[c] = v;
+        mt = fmaxf(mt, v);
+      }
+      const bool move = mt > m + 8.f;
+      if (__any_sync(0xffffffffu, move)) {
+        const float mn = move ? mt : m;
+        const float corr = move ? ex2_tc(m - mn) : 1.f;  // m = -inf: 0 (O and l are still 0)
+        if (i > 0) {
+          // O must hold tiles < i before it is rescaled: wait for O += P_{i-1} V_{i-1}.
+          ok = mbar_wait_bounded(p_empty((i - 1) & 1), ((i - 1) >> 1) & 1, abort_flag, &g_attn_status);
+          if (!__all_sync(0xffffffffu, ok)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < kTcDV / 32; ++c) {
+            uint32_t ov[32];
+            tmem_ld_32x32b_x32(tmem + lane_off + kColO + c * 32, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * corr);
+            tmem_st_32x32b_x32(tmem + lane_off + kColO + c * 32, ov);
+          }
+          tmem_wait_st();
+        }
+        l *= corr;
+        m = mn;
+      }
+      const float ref = m == -INFINITY ? 0.f : m;
+      if (i >= 2) {  // P buffer b is free once O += P_{i-2} V_{i-2} completed
+        ok = mbar_wait_bounded(p_empty(b), ((i - 2) >> 1) & 1, abort_flag, &g_attn_status);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+      }
+      // Row r of P in the swizzled K-major layout: 16-byte chunk ch at chunk ch ^ (r % 8).
+      const uint32_t prow = base + C::kOffP + b * kPBytes + r * 128;
+#pragma unroll
+      for (int ch = 0; ch < kTcBN / 8; ++ch) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float p0 = ex2_tc(x[ch * 8 + 2 * j] - ref), p1 = ex2_tc(x[ch * 8 + 2 * j + 1] - ref);
+          l += p0 + p1;
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+          w[j] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        st_shared_v4(prow + ((ch ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full(b));
+    }
+    // ---- O / l -> bf16 (this CTA's 256 output columns of row qpos)
+    if (ok) ok = mbar_wait_bounded(o_ready, 0, abort_flag, &g_attn_status);
+    if (__all_sync(0xffffffffu, ok)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = a.o + head * a.o_head + static_cast<int64_t>(qpos) * a.o_tok + half * kTcDV;
+#pragma unroll 1
+      for (int c = 0; c < kTcDV / 32; ++c) {
+        uint32_t ov[32];
+        tmem_ld_32x32b_x32(tmem + lane_off + kColO + c * 32, ov);
+        tmem_wait_ld();
+        if (qpos < a.t) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(ov[8 * j + 2 * e]) * inv,
+                                                        __uint_as_float(ov[8 * j + 2 * e + 1]) * inv);
+              w[e] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            *reinterpret_cast<uint4*>(orow + c * 32 + j * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace w8
+
+namespace w8host {
+
+using AttnEncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static AttnEncodeFn attn_encode_fn() {
+  static AttnEncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AttnEncodeFn>(p);
+  });
+  return fn;
+}
+
+// A head-major bf16 tensor, element (h, t, d) at ptr[h * ld_head + t * ld_tok + d], viewed in
+// 4-D as (64 columns, token, 64-column block, head): a box {64, rows, blocks, 1} lands in
+// shared memory as `blocks` consecutive 128-byte-swizzled [rows x 64] blocks.
+static int encode_heads(CUtensorMap* map, const void* ptr, int64_t d, int64_t heads, int64_t t, int64_t ld_head,
+                        int64_t ld_tok, uint32_t rows, uint32_t blocks) {
+  AttnEncodeFn enc = attn_encode_fn();
+  if (enc == nullptr) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return W8_ERR_CUDA;
+  }
+  const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(t), static_cast<cuuint64_t>(d / 64),
+                              static_cast<cuuint64_t>(heads)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(ld_tok * 2), 128, static_cast<cuuint64_t>(ld_head * 2)};
+  const cuuint32_t box[4] = {64, rows, blocks, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (attention, 4-D) failed with CUresult %d (t %lld, ld_tok %lld, ld_head %lld)",
+              static_cast<int>(r), static_cast<long long>(t), static_cast<long long>(ld_tok),
+              static_cast<long long>(ld_head));
+    return W8_ERR_CUDA;
+  }
+  return W8_OK;
+}
+
+template <int D>
+static int attention_tc_go(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k, int64_t k_head,
+                           int64_t k_tok, const uint16_t* v, int64_t v_head, int64_t v_tok, uint16_t* o,
+                           int64_t o_head, int64_t o_tok, int64_t t, int64_t heads, int64_t kv_heads,
+                           int64_t window, int device, cudaStream_t stream) {
+  using C = w8::TcCfg<D>;
+  CUtensorMap tq, tk, tv;
+  int st = encode_heads(&tq, q, D, heads, t, q_head, q_tok, w8::kTcBM, D / 64);
+  if (st != W8_OK) return st;
+  st = encode_heads(&tk, k, D, kv_heads, t, k_head, k_tok, w8::kTcBN, 2);
+  if (st != W8_OK) return st;
+  st = encode_heads(&tv, v, D, kv_heads, t, v_head, v_tok, w8::kTcBN, 2);
+  if (st != W8_OK) return st;
+  static bool done[64] = {};
+  if (device < 0 || device >= 64) return W8_ERR_UNSUPPORTED;
+  if (!done[device]) {
+    W8_CUDA_TRY(cudaFuncSetAttribute(w8::attention_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     C::kSmem));
+    done[device] = true;
+  }
+  w8::AttnTcArgs a;
+  a.o = reinterpret_cast<__nv_bfloat16*>(o);
+  a.o_head = o_head;
+  a.o_tok = o_tok;
+  a.t = static_cast<int>(t);
+  a.heads = static_cast<int>(heads);
+  a.kv_heads = static_cast<int>(kv_heads);
+  a.window = static_cast<int>(window);
+  const int64_t blocks = (t + w8::kTcBM - 1) / w8::kTcBM * heads * (D / w8::kTcDV);
+  W8_CHECK_ARG(blocks < (1ll << 31), "too many query tiles");
+  w8::attention_tc_kernel<D><<<static_cast<unsigned>(blocks), w8::kTcThreads, C::kSmem, stream>>>(tq, tk, tv, a);
+  return cuda_status(cudaGetLastError());
+}
+
+// The tcgen05 schedule of w8_attention_prefill_bf16 (arguments checked by the caller).
+int attention_tc(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k, int64_t k_head,
+                 int64_t k_tok, const uint16_t* v, int64_t v_head, int64_t v_tok, uint16_t* o, int64_t o_head,
+                 int64_t o_tok, int64_t t, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t window,
+                 int device, cudaStream_t stream) {
+  if (head_dim == 256)
+    return attention_tc_go<256>(q, q_head, q_tok, k, k_head, k_tok, v, v_head, v_tok, o, o_head, o_tok, t, heads,
+                                kv_heads, window, device, stream);
+  return attention_tc_go<512>(q, q_head, q_tok, k, k_head, k_tok, v, v_head, v_tok, o, o_head, o_tok, t, heads,
+                              kv_heads, window, device, stream);
+}
+
+// Read (and optionally clear) the attention kernel's sticky device status.
+int attention_device_status(int clear, int* out) {
+  int v = 0;
+  W8_CUDA_TRY(cudaMemcpyFromSymbol(&v, w8::g_attn_status, sizeof(int)));
+  if (clear) {
+    const int zero = 0;
+    W8_CUDA_TRY(cudaMemcpyToSymbol(w8::g_attn_status, &zero, sizeof(int)));
+  }
+  *out = v;
+  return W8_OK;
+}
+
+}  // namespace w8host

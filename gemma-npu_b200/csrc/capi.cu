@@ -66,6 +66,7 @@ int num_sms(int* out) {
 }
 
 int gemm_device_status(int clear, int* out);
+int attention_device_status(int clear, int* out);
 
 }  // namespace w8host
 
@@ -92,5 +93,8 @@ extern "C" int w8_device_status(int clear) {
   int v = W8_OK;
   st = w8host::gemm_device_status(clear, &v);
   if (st != W8_OK) return st;
-  return v;
+  int va = W8_OK;
+  st = w8host::attention_device_status(clear, &va);
+  if (st != W8_OK) return st;
+  return v != W8_OK ? v : va;
 }

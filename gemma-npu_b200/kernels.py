@@ -296,10 +296,12 @@ def qkv_norm_rope(y, cos, sin, qw, kw, eps, heads, kv_heads, head_dim, shared=Fa
     return q, out[heads: heads + kv_heads], out[heads + kv_heads:]
 
 
-def attention_prefill(q, k, v, window=0, out=None):
+def attention_prefill(q, k, v, window=0, out=None, schedule="tc"):
     """Prefill attention of one prompt from position 0 (pipeline.py:139-180): causal, with
     a sliding window when window > 0, scale 1.0, grouped-query heads.  q bf16 [H, T, D],
-    k, v [KV, T, D] (unit stride along D; any head / token pitch); returns o [H, T, D]."""
+    k, v [KV, T, D] (unit stride along D; any head / token pitch); returns o [H, T, D].
+    schedule "tc" runs the tcgen05 kernel, "mma" the warp-level mma.sync one."""
+    _need(schedule in ("tc", "mma"), "schedule must be 'tc' or 'mma'")
     for t_, name in ((q, "q"), (k, "k"), (v, "v")):
         _need(isinstance(t_, torch.Tensor) and t_.is_cuda and t_.dtype == torch.bfloat16 and t_.dim() == 3
               and t_.stride(2) == 1, f"{name} must be a bf16 CUDA tensor [heads, T, D] with unit stride along D")
@@ -310,7 +312,8 @@ def attention_prefill(q, k, v, window=0, out=None):
         out = torch.empty((H, T, D), dtype=torch.bfloat16, device=q.device)
     _need(out.dtype == torch.bfloat16 and tuple(out.shape) == (H, T, D) and out.stride(2) == 1,
           f"out must be bf16 ({H}, {T}, {D})")
-    _lib.call("w8_attention_prefill_bf16", q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0),
+    entry = "w8_attention_prefill_bf16" if schedule == "tc" else "w8_attention_prefill_mma_bf16"
+    _lib.call(entry, q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0),
               k.stride(1), v.data_ptr(), v.stride(0), v.stride(1), out.data_ptr(), out.stride(0), out.stride(1),
               T, H, KV, D, int(window), _stream(q))
     return out

@@ -181,12 +181,19 @@ int w8_qkv_norm_rope_bf16(const uint16_t* y, int64_t ldy, const uint16_t* cos, c
  * x[h * x_head + t * x_tok + d] (the k_qkv glue's head-major output); fp32 softmax and
  * accumulation, P rounded to bf16 for the second product.  head_dim 256 or 512; 16-byte
  * aligned with pitches % 8 == 0.  Replaces local_attn.py / the CPU sdpa calls: within
- * max-rel 1e-2 of them. */
+ * max-rel 1e-2 of them.  Runs on tcgen05 (TMEM accumulators, TMA-fed). */
 int w8_attention_prefill_bf16(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k,
                               int64_t k_head, int64_t k_tok, const uint16_t* v, int64_t v_head,
                               int64_t v_tok, uint16_t* o, int64_t o_head, int64_t o_tok, int64_t t,
                               int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t window,
                               w8_stream_t stream);
+/* The same contract on warp-level mma.sync tiles (no TMA, no TMEM): a second, independent
+ * schedule, kept as a cross-check of the tcgen05 one. */
+int w8_attention_prefill_mma_bf16(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k,
+                                  int64_t k_head, int64_t k_tok, const uint16_t* v, int64_t v_head,
+                                  int64_t v_tok, uint16_t* o, int64_t o_head, int64_t o_tok, int64_t t,
+                                  int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t window,
+                                  w8_stream_t stream);
 
 /* ---- quantisation ------------------------------------------------------ */
 
