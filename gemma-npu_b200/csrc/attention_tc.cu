@@ -3,54 +3,60 @@
 // q_start = 0: causal, window W > 0 or none, scale 1.0, grouped-query heads, bf16 in and
 // out, fp32 softmax and accumulation) on a schedule built for sm_100a.
 //
-// One CTA per (128 queries, head, 256-column half of the output): warp 0 loads with TMA,
-// warp 1 issues the MMAs, warps 2-5 run the softmax with one thread per query row (= TMEM
-// lane).  Per 64-key tile j:
-//   S_j  = Q K_j^T     tcgen05.mma kind::f16 (bf16 x bf16 -> fp32), two S buffers in TMEM
-//   P_j  = 2^(S_j log2(e) - m)   softmax threads: tcgen05.ld the row, mask, row max m and
-//                                sum l, P_j (bf16) into shared memory in the MMA A layout
-//   O   += P_j V_j     tcgen05.mma, O [128 x 256] fp32 in TMEM
-// The MMA warp issues S_{j+1} before O += P_j V_j, so the tensor core computes the next
-// scores while the softmax threads work on these.  A row's reference maximum m moves only
-// when the tile maximum exceeds it by more than 8 (log2 units): P is then <= 2^8 (exact
-// range in bf16 and fp32), O is rescaled in TMEM (tcgen05.ld / st) only on such moves, and
-// the final O / l is the same softmax.  head_dim 512 runs two CTAs per query tile, one per
-// output half, each computing the full S (the TMEM of one SM holds S and a 256-column O,
-// not a 512-column one).
+// A CTA owns 128 query rows and one 256-column half of the output.  The rows are PK heads
+// of one KV group times 128 / PK consecutive queries (grouped-query packing: the heads that
+// share a K / V stream read it once), PK the largest power of two <= 16 dividing the group
+// size.  Warp 0 loads with TMA, warp 1 issues the MMAs, warps 2-5 run the softmax with one
+// thread per row (= TMEM lane).  Per 128-key tile j:
+//   S_j  = Q K_j^T     tcgen05.mma kind::f16 (bf16 x bf16 -> fp32), M 128 x N 128, into one
+//                      of two 128-column S buffers in TMEM
+//   P_j  = 2^(S_j log2(e) - m)   softmax threads: tcgen05.ld the row, mask (boundary tiles
+//                      only), row max m and sum l; P_j (bf16 pairs) is stored back into the
+//                      first 64 columns of its S buffer with tcgen05.st
+//   O   += P_j V_j     tcgen05.mma with A = P_j read from TMEM, N 256, O fp32 in TMEM
+// The MMA warp issues S_{j+1} before O += P_j V_j, so while the softmax threads work on
+// S_j the tensor core runs O += P_{j-1} V_{j-1} and S_{j+1}; tcgen05.mma operations of a
+// CTA execute in issue order, so S_{j+2} overwrites P_j only after O += P_j V_j read it.
+// A row's reference maximum m moves only when the tile maximum exceeds it by more than 8
+// (log2 units): P is then <= 2^8, O is rescaled in TMEM (tcgen05.ld / st) only on such
+// moves, and the final O / l is the same softmax.  head_dim 512 runs two CTAs per row
+// block, one per output half, each computing the full S (TMEM holds two S buffers and a
+// 256-column O, not a 512-column one).
 //
-// Shared memory: Q resident (head_dim / 64 swizzled [128 x 64] blocks), a ring of 16 KB
-// slots each holding 64 keys x 128 columns of K or V (two swizzled [64 x 64] blocks; loaded
-// in the order the MMA warp consumes them: K tiles for S, V tiles for O), and two P buffers.
-// Every mbarrier wait is bounded; on a timeout the kernel records W8_ERR_DEVICE_TIMEOUT,
-// drains its own copies and MMAs, frees TMEM and returns.
+// Shared memory: Q resident (head_dim / 64 swizzled [128 x 64] blocks) and a ring of 16 KB
+// slots loaded in the order the MMA warp consumes them: K slots of 128 keys x 64 columns
+// (one per 64 columns of S's reduction), V slots of 32 keys x 256 columns (four swizzled
+// [32 x 64] blocks, the MN-major B operand of two N = 256 MMAs).  Every mbarrier wait is
+// bounded; on a timeout the kernel records W8_ERR_DEVICE_TIMEOUT, drains its own copies
+// and MMAs, frees TMEM and returns.
 #include "common.cuh"
 
+#include <algorithm>
 #include <mutex>
 
 namespace w8 {
 
 __device__ int g_attn_status = 0;
 
-constexpr int kTcBM = 128;                  // queries per CTA (TMEM lanes)
-constexpr int kTcBN = 64;                   // keys per tile
+constexpr int kTcBM = 128;                  // rows per CTA (TMEM lanes)
+constexpr int kTcBN = 128;                  // keys per tile
 constexpr int kTcDV = 256;                  // output columns per CTA
 constexpr int kTcThreads = 192;             // TMA warp, MMA warp, 4 softmax warps
-constexpr int kSlotBytes = kTcBN * 128 * 2; // 64 keys x 128 bf16 columns
-constexpr int kPBytes = kTcBM * kTcBN * 2;  // one P tile
+constexpr int kSlotBytes = 16384;           // K: 128 keys x 64 columns; V: 32 keys x 256 columns
+constexpr int kVKeys = 32;                  // keys per V slot
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 2 * kTcBN;       // S buffers at columns 0 and 64, O from 128
+constexpr uint32_t kColO = 2 * kTcBN;       // S buffers at columns 0 and 128, O from 256
 
 template <int D>
 struct TcCfg {
   static constexpr int kQBytes = kTcBM * D * 2;
-  static constexpr int kSlots = D == 256 ? 8 : 4;
-  static constexpr int kKSlots = D / 128;       // ring slots per K tile
-  static constexpr int kVSlots = kTcDV / 128;   // ring slots per V tile
+  static constexpr int kSlots = D == 256 ? 10 : 6;
+  static constexpr int kKSlots = D / 64;            // ring slots per K tile
+  static constexpr int kVSlots = kTcBN / kVKeys;    // ring slots per V tile
   static constexpr int kOffRing = kQBytes;
-  static constexpr int kOffP = kOffRing + kSlots * kSlotBytes;
-  static constexpr int kOffBar = kOffP + 2 * kPBytes;
-  // full[kSlots], empty[kSlots], q_full, s_full[2], s_empty[2], p_full[2], p_empty[2], o_ready
-  static constexpr int kNumBars = 2 * kSlots + 10;
+  static constexpr int kOffBar = kOffRing + kSlots * kSlotBytes;
+  // full[kSlots], empty[kSlots], q_full, s_full[2], p_full[2], pv_done[2], o_ready
+  static constexpr int kNumBars = 2 * kSlots + 8;
   static constexpr int kSmem = kOffBar + kNumBars * 8 + 16 + 1024;
   static_assert(kSmem <= 232448, "shared memory budget exceeded");
 };
@@ -59,6 +65,7 @@ struct AttnTcArgs {
   __nv_bfloat16* o;
   int64_t o_head, o_tok;
   int t, heads, kv_heads, window;
+  int pack;  // heads per CTA (PK); 128 / PK queries per CTA
 };
 
 // kind::f16 instruction descriptor: bf16 A and B, fp32 D, M x N, A K-major, B K- or MN-major.
@@ -71,13 +78,25 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool b_mn_major)
          | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
 }
 
-__device__ __forceinline__ void mma_bf16_tc(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+// D[tmem] (+)= A[smem desc] * B[smem desc], bf16 -> fp32.
+__device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                             uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]: A is M x K with row i in lane i, K packed two bf16
+// per 32-bit column.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -110,6 +129,10 @@ __device__ __forceinline__ float ex2_tc(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h2);
+}
 
 template <int D>
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -129,21 +152,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   auto empty_bar = [&](uint32_t s) { return bar0 + 8u * (C::kSlots + s); };
   const uint32_t q_full = bar0 + 8u * (2 * C::kSlots);
   auto s_full = [&](int b) { return q_full + 8u * (1 + b); };
-  auto s_empty = [&](int b) { return q_full + 8u * (3 + b); };
-  auto p_full = [&](int b) { return q_full + 8u * (5 + b); };
-  auto p_empty = [&](int b) { return q_full + 8u * (7 + b); };
-  const uint32_t o_ready = q_full + 8u * 9;
+  auto p_full = [&](int b) { return q_full + 8u * (3 + b); };
+  auto pv_done = [&](int b) { return q_full + 8u * (5 + b); };
+  const uint32_t o_ready = q_full + 8u * 7;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Heaviest query tiles first: block ids run over (head, half) fastest, query tiles last.
-  const int per_tile = a.heads * kSplit;
-  const int qtiles = gridDim.x / per_tile;
-  const int qt = qtiles - 1 - static_cast<int>(blockIdx.x) / per_tile;
-  const int rest = static_cast<int>(blockIdx.x) % per_tile;
-  const int head = rest / kSplit, half = rest % kSplit;
-  const int q0 = qt * kTcBM;
-  const int kvh = head / (a.heads / a.kv_heads);
-  const int last_key = min(q0 + kTcBM, a.t) - 1;
+  const int pk = a.pack, qb_rows = kTcBM / pk;
+  // Heaviest row blocks first: block ids run over (head group, half) fastest.
+  const int per_block = (a.heads / pk) * kSplit;
+  const int nblocks = gridDim.x / per_block;
+  const int qb = nblocks - 1 - static_cast<int>(blockIdx.x) / per_block;
+  const int rest = static_cast<int>(blockIdx.x) % per_block;
+  const int hg = rest / kSplit, half = rest % kSplit;
+  const int q0 = qb * qb_rows;
+  const int head0 = hg * pk;
+  const int kvh = head0 / (a.heads / a.kv_heads);
+  const int last_key = min(q0 + qb_rows, a.t) - 1;
   const int first_key = a.window > 0 ? max(0, q0 - a.window + 1) : 0;
   const int kt0 = first_key / kTcBN;
   const int ntiles = last_key / kTcBN - kt0 + 1;
@@ -156,9 +180,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_init(q_full, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(s_full(b), 1);
-      mbar_init(s_empty(b), 4);  // the four softmax warps
-      mbar_init(p_full(b), 4);
-      mbar_init(p_empty(b), 1);
+      mbar_init(p_full(b), 4);  // the four softmax warps
+      mbar_init(pv_done(b), 1);
     }
     mbar_init(o_ready, 1);
     *abort_flag = 0;
@@ -180,23 +203,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       // ---- TMA producer: Q once, then the ring in the MMA warp's order
       mbar_arrive_expect_tx(q_full, C::kQBytes);
-      tma_load_4d(base, &tm_q, q_full, 0, q0, 0, head);
+      tma_load_4d(base, &tm_q, q_full, 0, q0, head0, 0);
       uint32_t g = 0;
       bool ok = true;
-      auto put = [&](const CUtensorMap* m, int key0, int chunk0) {
+      auto put = [&](const CUtensorMap* m, int key0, int block0) {
         if (!ok) return;
         const uint32_t slot = g % C::kSlots, use = g / C::kSlots;
         ok = mbar_wait_bounded(empty_bar(slot), (use & 1u) ^ 1u, abort_flag, &g_attn_status);
         if (!ok) return;
         mbar_arrive_expect_tx(full_bar(slot), kSlotBytes);
-        tma_load_4d(ring + slot * kSlotBytes, m, full_bar(slot), 0, key0, chunk0, kvh);
+        tma_load_4d(ring + slot * kSlotBytes, m, full_bar(slot), 0, key0, block0, kvh);
         ++g;
       };
-      for (int p = 0; p < C::kKSlots; ++p) put(&tm_k, kt0 * kTcBN, 2 * p);
+      for (int c = 0; c < C::kKSlots; ++c) put(&tm_k, kt0 * kTcBN, c);
       for (int i = 0; i < ntiles && ok; ++i) {
         if (i + 1 < ntiles)
-          for (int p = 0; p < C::kKSlots; ++p) put(&tm_k, (kt0 + i + 1) * kTcBN, 2 * p);
-        for (int p = 0; p < C::kVSlots; ++p) put(&tm_v, (kt0 + i) * kTcBN, half * (kTcDV / 64) + 2 * p);
+          for (int c = 0; c < C::kKSlots; ++c) put(&tm_k, (kt0 + i + 1) * kTcBN, c);
+        for (int j = 0; j < C::kVSlots; ++j) put(&tm_v, (kt0 + i) * kTcBN + j * kVKeys, half * (kTcDV / 64));
       }
       // Drain: every copy issued has landed before the CTA may exit.
       mbar_wait_bounded(q_full, 0, nullptr, &g_attn_status);
@@ -207,7 +230,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       // ---- MMA issuer
       constexpr uint32_t id_s = idesc_bf16(kTcBM, kTcBN, false);
-      constexpr uint32_t id_o = idesc_bf16(kTcBM, 128, true);
+      constexpr uint32_t id_o = idesc_bf16(kTcBM, kTcDV, true);
       uint32_t g = 0;
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag, &g_attn_status);
       auto take = [&]() {
@@ -215,22 +238,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         ok = ok && mbar_wait_bounded(full_bar(slot), use & 1u, abort_flag, &g_attn_status);
         return slot;
       };
+      // S_i into buffer i % 2.  Buffer i % 2 last held P_{i-2}, read by O += P_{i-2} V_{i-2},
+      // which this thread issued earlier (MMAs execute in issue order).
       auto issue_s = [&](int i) {
         const int b = i & 1;
-        ok = ok && mbar_wait_bounded(s_empty(b), ((i >> 1) & 1) ^ 1u, abort_flag, &g_attn_status);
-        for (int p = 0; p < C::kKSlots && ok; ++p) {
+        for (int c = 0; c < C::kKSlots && ok; ++c) {
           const uint32_t slot = take();
           if (!ok) return;
           tc_fence_after();
           const uint32_t sk = ring + slot * kSlotBytes;
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_bf16_tc(tmem + b * kTcBN,
-                          smem_desc_sw128(base + (2 * p + c) * (kTcBM * 128) + kk * 32, 16, 1024),
-                          smem_desc_sw128(sk + c * (kTcBN * 128) + kk * 32, 16, 1024), id_s,
-                          (p | c | kk) ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16_ss(tmem + b * kTcBN, smem_desc_sw128(base + c * (kTcBM * 128) + kk * 32, 16, 1024),
+                        smem_desc_sw128(sk + kk * 32, 16, 1024), id_s, (c | kk) ? 1u : 0u);
           mma_commit(empty_bar(slot));
           ++g;
         }
@@ -241,68 +261,74 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (i + 1 < ntiles) issue_s(i + 1);
         const int b = i & 1;
         ok = ok && mbar_wait_bounded(p_full(b), (i >> 1) & 1, abort_flag, &g_attn_status);
-        const uint32_t sp = base + C::kOffP + b * kPBytes;
-        for (int p = 0; p < C::kVSlots && ok; ++p) {
+        for (int j = 0; j < C::kVSlots && ok; ++j) {
           const uint32_t slot = take();
           if (!ok) break;
           tc_fence_after();
           const uint32_t sv = ring + slot * kSlotBytes;
-          // B = V [16 keys x 128 columns] MN-major: 64-column blocks 8 KB apart (LBO),
-          // 8-key groups 1 KB apart (SBO); the next 16 keys start 2 KB further.
+          // A = P keys [32 j + 16 h, +16): TMEM columns b * 128 + 16 j + 8 h (bf16 pairs).
+          // B = V [16 keys x 256 columns] MN-major: 64-column blocks 4 KB apart (LBO),
+          // 8-key groups 1 KB apart (SBO); the second 16 keys start 2 KB further.
 #pragma unroll
-          for (int kk = 0; kk < kTcBN / 16; ++kk)
-            mma_bf16_tc(tmem + kColO + p * 128, smem_desc_sw128(sp + kk * 32, 16, 1024),
-                        smem_desc_sw128(sv + kk * 16 * 128, kTcBN * 128, 1024), id_o, (i | kk) ? 1u : 0u);
+          for (int h = 0; h < 2; ++h)
+            mma_bf16_ts(tmem + kColO, tmem + b * kTcBN + 16 * j + 8 * h,
+                        smem_desc_sw128(sv + h * 16 * 128, kVKeys * 128, 1024), id_o, (i | j | h) ? 1u : 0u);
           mma_commit(empty_bar(slot));
           ++g;
         }
-        if (ok) mma_commit(p_empty(b));
+        if (ok) mma_commit(pv_done(b));
       }
       mma_commit(o_ready);
       // Drain: no MMA may still write TMEM when it is freed.
       mbar_wait_bounded(o_ready, 0, nullptr, &g_attn_status);
     }
   } else {
-    // ---- softmax: thread = query row q0 + r = TMEM lane r (warp w reads lanes 32 (w % 4) ..)
+    // ---- softmax: thread = row r = TMEM lane r (warp w reads lanes 32 (w % 4) ..)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int qpos = q0 + r;
+    const int qpos = q0 + r % qb_rows;
+    const int head = head0 + r / qb_rows;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     constexpr float kLog2e = 1.4426950408889634f;
-    float m = -INFINITY, l = 0.f;
+    float m = -INFINITY, l = 0.f;  // m in log2 units
     bool ok = true;
     for (int i = 0; i < ntiles; ++i) {
       const int b = i & 1, k0 = (kt0 + i) * kTcBN;
       ok = mbar_wait_bounded(s_full(b), (i >> 1) & 1, abort_flag, &g_attn_status);
+      // O += P_{i-2} V_{i-2} has completed (it ran before S_i); observing it keeps the
+      // phase of pv_done(b) known for the wait on O += P_{i-1} V_{i-1} below.
+      if (i >= 2) ok = ok && mbar_wait_bounded(pv_done(b), ((i - 2) >> 1) & 1, abort_flag, &g_attn_status);
       if (!__all_sync(0xffffffffu, ok)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t s0[32], s1[32];
-      tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN, s0);
-      tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN + 32, s1);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty(b));  // the S buffer may be overwritten
-      float x[kTcBN];
-      float mt = -INFINITY;
+      uint32_t sv[4][32];
 #pragma unroll
-      for (int c = 0; c < kTcBN; ++c) {
-        const int key = k0 + c;
-        float v = __uint_as_float(c < 32 ? s0[c] : s1[c - 32]) * kLog2e;
-        if (key > qpos || key >= a.t || (a.window > 0 && qpos - key >= a.window)) v = -INFINITY;
-        x[c] = v;
-        mt = fmaxf(mt, v);
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN + 32 * c, sv[c]);
+      tmem_wait_ld();
+      // Boundary tiles (causal diagonal, window edge, keys past T) are masked per element.
+      const bool interior = k0 + kTcBN - 1 <= q0 && k0 + kTcBN <= a.t &&
+                            (a.window == 0 || k0 >= q0 + qb_rows - a.window);
+      if (!interior) {
+#pragma unroll
+        for (int c = 0; c < kTcBN; ++c) {
+          const int key = k0 + c;
+          if (key > qpos || key >= a.t || (a.window > 0 && qpos - key >= a.window))
+            sv[c >> 5][c & 31] = __float_as_uint(-INFINITY);
+        }
       }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kTcBN; ++c) mx = fmaxf(mx, __uint_as_float(sv[c >> 5][c & 31]));
+      const float mt = mx * kLog2e;
       const bool move = mt > m + 8.f;
       if (__any_sync(0xffffffffu, move)) {
         const float mn = move ? mt : m;
         const float corr = move ? ex2_tc(m - mn) : 1.f;  // m = -inf: 0 (O and l are still 0)
         if (i > 0) {
           // O must hold tiles < i before it is rescaled: wait for O += P_{i-1} V_{i-1}.
-          ok = mbar_wait_bounded(p_empty((i - 1) & 1), ((i - 1) >> 1) & 1, abort_flag, &g_attn_status);
+          ok = mbar_wait_bounded(pv_done((i - 1) & 1), ((i - 1) >> 1) & 1, abort_flag, &g_attn_status);
           if (!__all_sync(0xffffffffu, ok)) {
             ok = false;
             break;
@@ -317,39 +343,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * corr);
             tmem_st_32x32b_x32(tmem + lane_off + kColO + c * 32, ov);
           }
-          tmem_wait_st();
         }
         l *= corr;
         m = mn;
       }
       const float ref = m == -INFINITY ? 0.f : m;
-      if (i >= 2) {  // P buffer b is free once O += P_{i-2} V_{i-2} completed
-        ok = mbar_wait_bounded(p_empty(b), ((i - 2) >> 1) & 1, abort_flag, &g_attn_status);
-        if (!__all_sync(0xffffffffu, ok)) {
-          ok = false;
-          break;
-        }
-      }
-      // Row r of P in the swizzled K-major layout: 16-byte chunk ch at chunk ch ^ (r % 8).
-      const uint32_t prow = base + C::kOffP + b * kPBytes + r * 128;
+      // P (bf16 pairs) into columns [0, 64) of this S buffer, over the S values just read.
 #pragma unroll
-      for (int ch = 0; ch < kTcBN / 8; ++ch) {
-        uint32_t w[4];
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pw[32];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float p0 = ex2_tc(x[ch * 8 + 2 * j] - ref), p1 = ex2_tc(x[ch * 8 + 2 * j + 1] - ref);
+        for (int e = 0; e < 32; ++e) {
+          const int c = 64 * h + 2 * e;
+          const float p0 = ex2_tc(fmaf(__uint_as_float(sv[c >> 5][c & 31]), kLog2e, -ref));
+          const float p1 = ex2_tc(fmaf(__uint_as_float(sv[(c + 1) >> 5][(c + 1) & 31]), kLog2e, -ref));
           l += p0 + p1;
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-          w[j] = *reinterpret_cast<uint32_t*>(&h2);
+          pw[e] = pack_bf16x2(p0, p1);
         }
-        st_shared_v4(prow + ((ch ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
+        tmem_st_32x32b_x32(tmem + lane_off + b * kTcBN + 32 * h, pw);
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full(b));
     }
-    // ---- O / l -> bf16 (this CTA's 256 output columns of row qpos)
+    // ---- O / l -> bf16 (this CTA's 256 output columns of row r)
     if (ok) ok = mbar_wait_bounded(o_ready, 0, abort_flag, &g_attn_status);
     if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
@@ -365,11 +383,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int j = 0; j < 4; ++j) {
             uint32_t w[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(ov[8 * j + 2 * e]) * inv,
-                                                        __uint_as_float(ov[8 * j + 2 * e + 1]) * inv);
-              w[e] = *reinterpret_cast<uint32_t*>(&h2);
-            }
+            for (int e = 0; e < 4; ++e)
+              w[e] = pack_bf16x2(__uint_as_float(ov[8 * j + 2 * e]) * inv, __uint_as_float(ov[8 * j + 2 * e + 1]) * inv);
             *reinterpret_cast<uint4*>(orow + c * 32 + j * 8) = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
@@ -406,20 +421,36 @@ static AttnEncodeFn attn_encode_fn() {
   return fn;
 }
 
-// A head-major bf16 tensor, element (h, t, d) at ptr[h * ld_head + t * ld_tok + d], viewed in
-// 4-D as (64 columns, token, 64-column block, head): a box {64, rows, blocks, 1} lands in
-// shared memory as `blocks` consecutive 128-byte-swizzled [rows x 64] blocks.
+// 4-D tiled map over a head-major bf16 tensor (element (h, t, d) at ptr[h * ld_head +
+// t * ld_tok + d]) with 128-byte swizzled boxes of 64 columns.  kv layout: dimensions
+// (64 columns, token, 64-column block, head); a box {64, rows, blocks, 1} lands in shared
+// memory as `blocks` consecutive [rows x 64] blocks.  q layout: dimensions (64 columns,
+// token, head, 64-column block); a box {64, rows, heads, blocks} lands as `blocks`
+// consecutive [heads * rows x 64] blocks, row = head * rows + token.
 static int encode_heads(CUtensorMap* map, const void* ptr, int64_t d, int64_t heads, int64_t t, int64_t ld_head,
-                        int64_t ld_tok, uint32_t rows, uint32_t blocks) {
+                        int64_t ld_tok, bool q_layout, uint32_t rows, uint32_t box_heads, uint32_t blocks) {
   AttnEncodeFn enc = attn_encode_fn();
   if (enc == nullptr) {
     set_error("cuTensorMapEncodeTiled is not available from the driver");
     return W8_ERR_CUDA;
   }
-  const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(t), static_cast<cuuint64_t>(d / 64),
-                              static_cast<cuuint64_t>(heads)};
-  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(ld_tok * 2), 128, static_cast<cuuint64_t>(ld_head * 2)};
-  const cuuint32_t box[4] = {64, rows, blocks, 1};
+  const cuuint64_t tok_stride = static_cast<cuuint64_t>(ld_tok * 2), head_stride = static_cast<cuuint64_t>(ld_head * 2);
+  cuuint64_t dims[4], strides[3];
+  cuuint32_t box[4];
+  dims[0] = 64;
+  dims[1] = static_cast<cuuint64_t>(t);
+  strides[0] = tok_stride;
+  box[0] = 64;
+  box[1] = rows;
+  if (q_layout) {
+    dims[2] = static_cast<cuuint64_t>(heads), dims[3] = static_cast<cuuint64_t>(d / 64);
+    strides[1] = head_stride, strides[2] = 128;
+    box[2] = box_heads, box[3] = blocks;
+  } else {
+    dims[2] = static_cast<cuuint64_t>(d / 64), dims[3] = static_cast<cuuint64_t>(heads);
+    strides[1] = 128, strides[2] = head_stride;
+    box[2] = blocks, box[3] = 1;
+  }
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -439,12 +470,16 @@ static int attention_tc_go(const uint16_t* q, int64_t q_head, int64_t q_tok, con
                            int64_t o_head, int64_t o_tok, int64_t t, int64_t heads, int64_t kv_heads,
                            int64_t window, int device, cudaStream_t stream) {
   using C = w8::TcCfg<D>;
+  // Heads per CTA: the largest power of two <= 16 dividing the query-group size.
+  const int64_t group = heads / kv_heads;
+  const int pack = static_cast<int>(std::min<int64_t>(group & -group, 16));
+  const uint32_t rows = static_cast<uint32_t>(w8::kTcBM / pack);
   CUtensorMap tq, tk, tv;
-  int st = encode_heads(&tq, q, D, heads, t, q_head, q_tok, w8::kTcBM, D / 64);
+  int st = encode_heads(&tq, q, D, heads, t, q_head, q_tok, true, rows, static_cast<uint32_t>(pack), D / 64);
   if (st != W8_OK) return st;
-  st = encode_heads(&tk, k, D, kv_heads, t, k_head, k_tok, w8::kTcBN, 2);
+  st = encode_heads(&tk, k, D, kv_heads, t, k_head, k_tok, false, w8::kTcBN, 1, 1);
   if (st != W8_OK) return st;
-  st = encode_heads(&tv, v, D, kv_heads, t, v_head, v_tok, w8::kTcBN, 2);
+  st = encode_heads(&tv, v, D, kv_heads, t, v_head, v_tok, false, w8::kVKeys, 1, w8::kTcDV / 64);
   if (st != W8_OK) return st;
   static bool done[64] = {};
   if (device < 0 || device >= 64) return W8_ERR_UNSUPPORTED;
@@ -461,8 +496,9 @@ static int attention_tc_go(const uint16_t* q, int64_t q_head, int64_t q_tok, con
   a.heads = static_cast<int>(heads);
   a.kv_heads = static_cast<int>(kv_heads);
   a.window = static_cast<int>(window);
-  const int64_t blocks = (t + w8::kTcBM - 1) / w8::kTcBM * heads * (D / w8::kTcDV);
-  W8_CHECK_ARG(blocks < (1ll << 31), "too many query tiles");
+  a.pack = pack;
+  const int64_t blocks = (t + rows - 1) / rows * (heads / pack) * (D / w8::kTcDV);
+  W8_CHECK_ARG(blocks < (1ll << 31), "too many query blocks");
   w8::attention_tc_kernel<D><<<static_cast<unsigned>(blocks), w8::kTcThreads, C::kSmem, stream>>>(tq, tk, tv, a);
   return cuda_status(cudaGetLastError());
 }
