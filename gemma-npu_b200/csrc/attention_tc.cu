@@ -3,32 +3,38 @@
 // q_start = 0: causal, window W > 0 or none, scale 1.0, grouped-query heads, bf16 in and
 // out, fp32 softmax and accumulation) on a schedule built for sm_100a.
 //
-// A CTA owns 128 query rows and one 256-column half of the output.  The rows are PK heads
-// of one KV group times 128 / PK consecutive queries (grouped-query packing: the heads that
-// share a K / V stream read it once), PK the largest power of two <= 16 dividing the group
-// size.  Warp 0 loads with TMA, warp 1 issues the MMAs, warps 2-5 run the softmax with one
-// thread per row (= TMEM lane).  Per 128-key tile j:
-//   S_j  = Q K_j^T     tcgen05.mma kind::f16 (bf16 x bf16 -> fp32), M 128 x N 128, into one
-//                      of two 128-column S buffers in TMEM
+// A cluster of two CTAs on two SMs (tcgen05 cta_group::2) owns 256 query rows and one
+// 256-column half of the output; each CTA holds 128 of the rows (its TMEM lanes).  The rows
+// of a CTA are PK heads of one KV group times 128 / PK consecutive queries (grouped-query
+// packing: heads that share a K / V stream read it once), PK the largest power of two
+// <= 16 dividing the group size; the two CTAs take consecutive query blocks.  Per CTA,
+// warp 0 loads with TMA, warps 2-5 run the softmax with one thread per row; warp 1 of
+// the even CTA issues the pair's MMAs.  Per 128-key tile j:
+//   S_j  = Q K_j^T     tcgen05.mma kind::f16 (bf16 x bf16 -> fp32), M 256 x N 128, into one
+//                      of two 128-column S buffers in each CTA's TMEM; each CTA stages 64
+//                      of the 128 keys (the B operand is split along N)
 //   P_j  = 2^(S_j log2(e) - m)   softmax threads: tcgen05.ld the row, mask (boundary tiles
 //                      only), row max m and sum l; P_j (bf16 pairs) is stored back into the
 //                      first 64 columns of its S buffer with tcgen05.st
-//   O   += P_j V_j     tcgen05.mma with A = P_j read from TMEM, N 256, O fp32 in TMEM
+//   O   += P_j V_j     tcgen05.mma with A = P_j read from TMEM, M 256 x N 256, O fp32 in
+//                      TMEM; each CTA stages 128 of V's 256 columns
+// Splitting both B operands across the pair halves the K / V bytes every SM loads per
+// MMA, which is what bounds a single-CTA schedule (its TMA copies, not its MMAs).
 // The MMA warp issues S_{j+1} before O += P_j V_j, so while the softmax threads work on
-// S_j the tensor core runs O += P_{j-1} V_{j-1} and S_{j+1}; tcgen05.mma operations of a
-// CTA execute in issue order, so S_{j+2} overwrites P_j only after O += P_j V_j read it.
+// S_j the tensor cores run O += P_{j-1} V_{j-1} and S_{j+1}; tcgen05.mma operations
+// execute in issue order, so S_{j+2} overwrites P_j only after O += P_j V_j read it.
 // A row's reference maximum m moves only when the tile maximum exceeds it by more than 8
 // (log2 units): P is then <= 2^8, O is rescaled in TMEM (tcgen05.ld / st) only on such
-// moves, and the final O / l is the same softmax.  head_dim 512 runs two CTAs per row
+// moves, and the final O / l is the same softmax.  head_dim 512 runs two clusters per row
 // block, one per output half, each computing the full S (TMEM holds two S buffers and a
 // 256-column O, not a 512-column one).
 //
-// Shared memory: Q resident (head_dim / 64 swizzled [128 x 64] blocks) and a ring of 16 KB
-// slots loaded in the order the MMA warp consumes them: K slots of 128 keys x 64 columns
-// (one per 64 columns of S's reduction), V slots of 32 keys x 256 columns (four swizzled
-// [32 x 64] blocks, the MN-major B operand of two N = 256 MMAs).  Every mbarrier wait is
-// bounded; on a timeout the kernel records W8_ERR_DEVICE_TIMEOUT, drains its own copies
-// and MMAs, frees TMEM and returns.
+// Shared memory per CTA: its Q rows resident (head_dim / 64 swizzled [128 x 64] blocks)
+// and a ring of 16 KB slots of 64 keys x 128 columns (two swizzled [64 x 64] blocks),
+// loaded in the order the MMAs consume them: for S the CTA's 64 keys of the tile, 128
+// columns of the reduction per slot; for O its 128 columns of V, 64 keys per slot.  Every
+// mbarrier wait is bounded; on a timeout the kernel records W8_ERR_DEVICE_TIMEOUT, drains
+// its own copies and MMAs, frees TMEM and returns.
 #include "common.cuh"
 
 #include <algorithm>
@@ -38,21 +44,20 @@ namespace w8 {
 
 __device__ int g_attn_status = 0;
 
-constexpr int kTcBM = 128;                  // rows per CTA (TMEM lanes)
+constexpr int kTcBM = 128;                  // rows per CTA (TMEM lanes); 256 per pair
 constexpr int kTcBN = 128;                  // keys per tile
-constexpr int kTcDV = 256;                  // output columns per CTA
+constexpr int kTcDV = 256;                  // output columns per pair
 constexpr int kTcThreads = 192;             // TMA warp, MMA warp, 4 softmax warps
-constexpr int kSlotBytes = 16384;           // K: 128 keys x 64 columns; V: 32 keys x 256 columns
-constexpr int kVKeys = 32;                  // keys per V slot
+constexpr int kSlotBytes = 32768;           // K: 64 keys x 256 columns; V: 128 keys x 128 columns
+constexpr int kKeysPerCta = kTcBN / 2;      // keys of a tile each CTA stages for S
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 2 * kTcBN;       // S buffers at columns 0 and 128, O from 256
 
 template <int D>
 struct TcCfg {
   static constexpr int kQBytes = kTcBM * D * 2;
-  static constexpr int kSlots = D == 256 ? 10 : 6;
-  static constexpr int kKSlots = D / 64;            // ring slots per K tile
-  static constexpr int kVSlots = kTcBN / kVKeys;    // ring slots per V tile
+  static constexpr int kSlots = D == 256 ? 5 : 3;
+  static constexpr int kKSlots = D / 256;                // slots per K tile (per CTA)
   static constexpr int kOffRing = kQBytes;
   static constexpr int kOffBar = kOffRing + kSlots * kSlotBytes;
   // full[kSlots], empty[kSlots], q_full, s_full[2], p_full[2], pv_done[2], o_ready
@@ -78,33 +83,35 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool b_mn_major)
          | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc], bf16 -> fp32.
-__device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
+// Pair MMA, D[tmem] (+)= A[smem desc] * B[smem desc], bf16 -> fp32; the descriptors name
+// the same shared-memory offsets in both CTAs.
+__device__ __forceinline__ void mma_bf16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// D[tmem] (+)= A[tmem] * B[smem desc]: A is M x K with row i in lane i, K packed two bf16
-// per 32-bit column.
-__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
+// Pair MMA with A read from TMEM: each CTA's A rows in its lanes, K packed two bf16 per
+// 32-bit column.
+__device__ __forceinline__ void mma_bf16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
-// 4-D tiled load (no multicast), completion counted on `bar` in bytes.
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int x, int y, int z,
-                                            int w) {
+// 4-D tiled load (no multicast) into this CTA's shared memory, completion counted on `bar`,
+// a shared::cluster barrier address that may lie in the peer CTA.
+__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const CUtensorMap* m, uint32_t bar, int x, int y,
+                                                 int z, int w) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
@@ -124,6 +131,20 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// mbar_wait_bounded with a non-blocking probe first: a phase that completed already costs
+// one test instead of a suspended try-wait.
+__device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0 || mbar_wait_bounded(bar, parity, abort_flag, status);
+}
+
 __device__ __forceinline__ float ex2_tc(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -135,7 +156,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const AttnTcArgs a) {
   using C = TcCfg<D>;
@@ -157,30 +178,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t o_ready = q_full + 8u * 7;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = the CTA that issues the MMAs
+  const uint32_t peer = rank ^ 1u;
   const int pk = a.pack, qb_rows = kTcBM / pk;
-  // Heaviest row blocks first: block ids run over (head group, half) fastest.
-  const int per_block = (a.heads / pk) * kSplit;
-  const int nblocks = gridDim.x / per_block;
-  const int qb = nblocks - 1 - static_cast<int>(blockIdx.x) / per_block;
-  const int rest = static_cast<int>(blockIdx.x) % per_block;
+  // Heaviest row blocks first: pair ids run over (head group, half) fastest.
+  const int per_pair = (a.heads / pk) * kSplit;
+  const int npairs = (gridDim.x >> 1) / per_pair;
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int pb = npairs - 1 - pair / per_pair;
+  const int rest = pair % per_pair;
   const int hg = rest / kSplit, half = rest % kSplit;
-  const int q0 = qb * qb_rows;
+  const int pq0 = pb * 2 * qb_rows;                           // first query of the pair
+  const int q0 = pq0 + static_cast<int>(rank) * qb_rows;      // first query of this CTA
   const int head0 = hg * pk;
   const int kvh = head0 / (a.heads / a.kv_heads);
-  const int last_key = min(q0 + qb_rows, a.t) - 1;
-  const int first_key = a.window > 0 ? max(0, q0 - a.window + 1) : 0;
+  const int last_key = min(pq0 + 2 * qb_rows, a.t) - 1;      // the pair shares its key tiles
+  const int first_key = a.window > 0 ? max(0, pq0 - a.window + 1) : 0;
   const int kt0 = first_key / kTcBN;
   const int ntiles = last_key / kTcBN - kt0 + 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kSlots; ++s) {
-      mbar_init(full_bar(s), 1);
-      mbar_init(empty_bar(s), 1);
+      mbar_init(full_bar(s), 1);   // leader: one arrive.expect_tx + both CTAs' bytes
+      mbar_init(empty_bar(s), 1);  // both: one MMA commit
     }
     mbar_init(q_full, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(s_full(b), 1);
-      mbar_init(p_full(b), 4);  // the four softmax warps
+      mbar_init(p_full(b), 8);  // leader: the softmax warps of both CTAs
       mbar_init(pv_done(b), 1);
     }
     mbar_init(o_ready, 1);
@@ -191,52 +216,74 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     prefetch_tmap(&tm_v);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---- TMA producer: Q once, then the ring in the MMA warp's order
-      mbar_arrive_expect_tx(q_full, C::kQBytes);
-      tma_load_4d(base, &tm_q, q_full, 0, q0, head0, 0);
+      // ---- TMA producer (both CTAs): Q once, then the ring in the MMA order; every copy
+      // completes on the leader's barrier, which expects both CTAs' bytes.
+      const uint32_t q_full_l = mapa_shared(q_full, 0);
+      if (rank == 0) mbar_arrive_expect_tx(q_full, 2 * C::kQBytes);
+      tma_load_4d_pair(base, &tm_q, q_full_l, 0, q0, head0, 0);
       uint32_t g = 0;
       bool ok = true;
       auto put = [&](const CUtensorMap* m, int key0, int block0) {
         if (!ok) return;
         const uint32_t slot = g % C::kSlots, use = g / C::kSlots;
-        ok = mbar_wait_bounded(empty_bar(slot), (use & 1u) ^ 1u, abort_flag, &g_attn_status);
+        ok = wait_phase(empty_bar(slot), (use & 1u) ^ 1u, abort_flag, &g_attn_status);
         if (!ok) return;
-        mbar_arrive_expect_tx(full_bar(slot), kSlotBytes);
-        tma_load_4d(ring + slot * kSlotBytes, m, full_bar(slot), 0, key0, block0, kvh);
+        if (rank == 0) mbar_arrive_expect_tx(full_bar(slot), 2 * kSlotBytes);
+        tma_load_4d_pair(ring + slot * kSlotBytes, m, mapa_shared(full_bar(slot), 0), 0, key0, block0, kvh);
         ++g;
       };
-      for (int c = 0; c < C::kKSlots; ++c) put(&tm_k, kt0 * kTcBN, c);
+      // K: this CTA's 64 keys of the tile, 256 columns of the reduction per slot.  V: all
+      // 128 keys of the tile, this CTA's 128 of the half's 256 columns.
+      const int kk0 = static_cast<int>(rank) * kKeysPerCta;
+      const int vb0 = half * (kTcDV / 64) + static_cast<int>(rank) * 2;
+      for (int c = 0; c < C::kKSlots; ++c) put(&tm_k, kt0 * kTcBN + kk0, 4 * c);
       for (int i = 0; i < ntiles && ok; ++i) {
         if (i + 1 < ntiles)
-          for (int c = 0; c < C::kKSlots; ++c) put(&tm_k, (kt0 + i + 1) * kTcBN, c);
-        for (int j = 0; j < C::kVSlots; ++j) put(&tm_v, (kt0 + i) * kTcBN + j * kVKeys, half * (kTcDV / 64));
+          for (int c = 0; c < C::kKSlots; ++c) put(&tm_k, (kt0 + i + 1) * kTcBN + kk0, 4 * c);
+        put(&tm_v, (kt0 + i) * kTcBN, vb0);
       }
-      // Drain: every copy issued has landed before the CTA may exit.
-      mbar_wait_bounded(q_full, 0, nullptr, &g_attn_status);
-      for (uint32_t h = g > static_cast<uint32_t>(C::kSlots) ? g - C::kSlots : 0; h < g; ++h)
-        mbar_wait_bounded(full_bar(h % C::kSlots), (h / C::kSlots) & 1u, nullptr, &g_attn_status);
+      // Every copy issued was awaited by the leader's MMA thread unless a wait gave up
+      // (after seconds); then give the last copies time to land before the CTA may exit.
+      if (!ok) {
+        const unsigned long long t0 = globaltimer();
+        while (globaltimer() - t0 < 50000ull) {
+        }
+      }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---- MMA issuer
-      constexpr uint32_t id_s = idesc_bf16(kTcBM, kTcBN, false);
-      constexpr uint32_t id_o = idesc_bf16(kTcBM, kTcDV, true);
+    if (rank == 0 && lane == 0) {
+      // ---- MMA issuer (leader CTA only)
+      constexpr uint32_t id_s = idesc_bf16(2 * kTcBM, kTcBN, false);
+      constexpr uint32_t id_o = idesc_bf16(2 * kTcBM, kTcDV, true);
+      const uint32_t empty_p0 = mapa_shared(empty_bar(0), peer);
+      const uint32_t s_full_p0 = mapa_shared(s_full(0), peer);
+      const uint32_t pv_done_p0 = mapa_shared(pv_done(0), peer);
+      // Descriptors of the operand bases; an offset of o bytes adds o / 16 (no carry out of
+      // the 14-bit address field below 256 KB).
+      const uint64_t q_desc = smem_desc_sw128(base, 16, 1024);
+      const uint64_t k_desc = smem_desc_sw128(ring, 16, 1024);
+      const uint64_t v_desc = smem_desc_sw128(ring, kTcBN * 128, 1024);
       uint32_t g = 0;
-      bool ok = mbar_wait_bounded(q_full, 0, abort_flag, &g_attn_status);
+      bool ok = wait_phase(q_full, 0, abort_flag, &g_attn_status);
       auto take = [&]() {
         const uint32_t slot = g % C::kSlots, use = g / C::kSlots;
-        ok = ok && mbar_wait_bounded(full_bar(slot), use & 1u, abort_flag, &g_attn_status);
+        ok = ok && wait_phase(full_bar(slot), use & 1u, abort_flag, &g_attn_status);
         return slot;
+      };
+      auto release = [&](uint32_t slot) {
+        mma_commit_pair(empty_bar(slot));
+        mma_commit_pair(empty_p0 + 8u * slot);
+        ++g;
       };
       // S_i into buffer i % 2.  Buffer i % 2 last held P_{i-2}, read by O += P_{i-2} V_{i-2},
       // which this thread issued earlier (MMAs execute in issue order).
@@ -246,49 +293,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint32_t slot = take();
           if (!ok) return;
           tc_fence_after();
-          const uint32_t sk = ring + slot * kSlotBytes;
+          // Slot: 4 blocks of [64 keys x 64 columns]; Q block 4 c + h holds the same columns.
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_bf16_ss(tmem + b * kTcBN, smem_desc_sw128(base + c * (kTcBM * 128) + kk * 32, 16, 1024),
-                        smem_desc_sw128(sk + kk * 32, 16, 1024), id_s, (c | kk) ? 1u : 0u);
-          mma_commit(empty_bar(slot));
-          ++g;
+          for (int h = 0; h < 4; ++h)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16_ss_pair(tmem + b * kTcBN, q_desc + (((4 * c + h) * (kTcBM * 128) + kk * 32) >> 4),
+                               k_desc + ((slot * kSlotBytes + h * (kKeysPerCta * 128) + kk * 32) >> 4), id_s,
+                               (c | h | kk) ? 1u : 0u);
+          release(slot);
         }
-        if (ok) mma_commit(s_full(b));
+        if (ok) {
+          mma_commit_pair(s_full(b));
+          mma_commit_pair(s_full_p0 + 8u * b);
+        }
       };
       issue_s(0);
       for (int i = 0; i < ntiles && ok; ++i) {
         if (i + 1 < ntiles) issue_s(i + 1);
         const int b = i & 1;
-        ok = ok && mbar_wait_bounded(p_full(b), (i >> 1) & 1, abort_flag, &g_attn_status);
-        for (int j = 0; j < C::kVSlots && ok; ++j) {
-          const uint32_t slot = take();
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t sv = ring + slot * kSlotBytes;
-          // A = P keys [32 j + 16 h, +16): TMEM columns b * 128 + 16 j + 8 h (bf16 pairs).
-          // B = V [16 keys x 256 columns] MN-major: 64-column blocks 4 KB apart (LBO),
-          // 8-key groups 1 KB apart (SBO); the second 16 keys start 2 KB further.
+        ok = ok && wait_phase(p_full(b), (i >> 1) & 1, abort_flag, &g_attn_status);
+        const uint32_t slot = take();
+        if (!ok) break;
+        tc_fence_after();
+        // A = P keys [16 s, 16 s + 16): TMEM columns b * 128 + 8 s (bf16 pairs).  B = V
+        // [16 keys x 128 columns] per CTA, MN-major: the two 64-column blocks 16 KB apart
+        // (LBO), 8-key groups 1 KB apart (SBO); the next 16 keys 2 KB further.
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-            mma_bf16_ts(tmem + kColO, tmem + b * kTcBN + 16 * j + 8 * h,
-                        smem_desc_sw128(sv + h * 16 * 128, kVKeys * 128, 1024), id_o, (i | j | h) ? 1u : 0u);
-          mma_commit(empty_bar(slot));
-          ++g;
-        }
-        if (ok) mma_commit(pv_done(b));
+        for (int s = 0; s < kTcBN / 16; ++s)
+          mma_bf16_ts_pair(tmem + kColO, tmem + b * kTcBN + 8 * s, v_desc + ((slot * kSlotBytes + s * 16 * 128) >> 4),
+                           id_o, (i | s) ? 1u : 0u);
+        release(slot);
+        mma_commit_pair(pv_done(b));
+        mma_commit_pair(pv_done_p0 + 8u * b);
       }
-      mma_commit(o_ready);
+      mma_commit_pair(o_ready);
+      mma_commit_pair(mapa_shared(o_ready, peer));
       // Drain: no MMA may still write TMEM when it is freed.
       mbar_wait_bounded(o_ready, 0, nullptr, &g_attn_status);
     }
   } else {
-    // ---- softmax: thread = row r = TMEM lane r (warp w reads lanes 32 (w % 4) ..)
+    // ---- softmax (both CTAs): thread = row r = TMEM lane r (warp w reads lanes 32 (w % 4) ..)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int qpos = q0 + r % qb_rows;
     const int head = head0 + r / qb_rows;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t p_full_l0 = mapa_shared(p_full(0), 0);
     constexpr float kLog2e = 1.4426950408889634f;
     float m = -INFINITY, l = 0.f;  // m in log2 units
     bool ok = true;
@@ -365,9 +416,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full(b));
+      if (lane == 0) mbar_arrive_cluster(p_full_l0 + 8u * b);
     }
-    // ---- O / l -> bf16 (this CTA's 256 output columns of row r)
+    // ---- O / l -> bf16 (this CTA's rows, the pair's 256 output columns)
     if (ok) ok = mbar_wait_bounded(o_ready, 0, abort_flag, &g_attn_status);
     if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
@@ -391,11 +442,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   }
+  __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still touch its barriers, TMEM or copies
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc_pair(tmem, kTmemCols);
   }
 }
 
@@ -477,9 +530,9 @@ static int attention_tc_go(const uint16_t* q, int64_t q_head, int64_t q_tok, con
   CUtensorMap tq, tk, tv;
   int st = encode_heads(&tq, q, D, heads, t, q_head, q_tok, true, rows, static_cast<uint32_t>(pack), D / 64);
   if (st != W8_OK) return st;
-  st = encode_heads(&tk, k, D, kv_heads, t, k_head, k_tok, false, w8::kTcBN, 1, 1);
+  st = encode_heads(&tk, k, D, kv_heads, t, k_head, k_tok, false, w8::kKeysPerCta, 1, 4);
   if (st != W8_OK) return st;
-  st = encode_heads(&tv, v, D, kv_heads, t, v_head, v_tok, false, w8::kVKeys, 1, w8::kTcDV / 64);
+  st = encode_heads(&tv, v, D, kv_heads, t, v_head, v_tok, false, w8::kTcBN, 1, 2);
   if (st != W8_OK) return st;
   static bool done[64] = {};
   if (device < 0 || device >= 64) return W8_ERR_UNSUPPORTED;
@@ -497,7 +550,8 @@ static int attention_tc_go(const uint16_t* q, int64_t q_head, int64_t q_tok, con
   a.kv_heads = static_cast<int>(kv_heads);
   a.window = static_cast<int>(window);
   a.pack = pack;
-  const int64_t blocks = (t + rows - 1) / rows * (heads / pack) * (D / w8::kTcDV);
+  // Two CTAs (a cluster) per 2 * rows queries, head group and output half.
+  const int64_t blocks = 2 * ((t + 2 * rows - 1) / (2 * rows)) * (heads / pack) * (D / w8::kTcDV);
   W8_CHECK_ARG(blocks < (1ll << 31), "too many query blocks");
   w8::attention_tc_kernel<D><<<static_cast<unsigned>(blocks), w8::kTcThreads, C::kSmem, stream>>>(tq, tk, tv, a);
   return cuda_status(cudaGetLastError());
