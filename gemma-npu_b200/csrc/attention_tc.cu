@@ -117,6 +117,15 @@ __device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
+// 4-D tiled store shared -> global (bulk-group completion); the box is clipped at the
+// tensor bounds.  Coordinates are non-negative and x = 0.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* m, uint32_t src, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(src), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+
 // Warp-wide registers -> TMEM, the inverse of tmem_ld_32x32b_x32.
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -158,7 +167,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 template <int D>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const AttnTcArgs a) {
+                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                        const AttnTcArgs a) {
   using C = TcCfg<D>;
   constexpr int kSplit = D / kTcDV;
   extern __shared__ uint8_t smem_raw[];
@@ -214,6 +224,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     prefetch_tmap(&tm_q);
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
+    prefetch_tmap(&tm_o);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
@@ -337,7 +348,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int qpos = q0 + r % qb_rows;
-    const int head = head0 + r / qb_rows;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t p_full_l0 = mapa_shared(p_full(0), 0);
     constexpr float kLog2e = 1.4426950408889634f;
@@ -354,24 +364,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t sv[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN + 32 * c, sv[c]);
-      tmem_wait_ld();
-      // Boundary tiles (causal diagonal, window edge, keys past T) are masked per element.
+      // Pass 1: the row maximum.  Boundary tiles (causal diagonal, window edge, keys past T)
+      // mask per element and write the masked row back, so pass 2 needs no masks.
       const bool interior = k0 + kTcBN - 1 <= q0 && k0 + kTcBN <= a.t &&
                             (a.window == 0 || k0 >= q0 + qb_rows - a.window);
-      if (!interior) {
+      float mx;
+      {
+        uint32_t sv[4][32];
 #pragma unroll
-        for (int c = 0; c < kTcBN; ++c) {
-          const int key = k0 + c;
-          if (key > qpos || key >= a.t || (a.window > 0 && qpos - key >= a.window))
-            sv[c >> 5][c & 31] = __float_as_uint(-INFINITY);
+        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN + 32 * c, sv[c]);
+        tmem_wait_ld();
+        if (!interior) {
+          // valid keys: lo <= key <= hi
+          const int hi = min(qpos, a.t - 1) - k0;
+          const int lo = a.window > 0 ? qpos - a.window + 1 - k0 : -1;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int key = 32 * c + e;
+              if (key < lo || key > hi) sv[c][e] = __float_as_uint(-INFINITY);
+            }
+            tmem_st_32x32b_x32(tmem + lane_off + b * kTcBN + 32 * c, sv[c]);
+          }
+          tmem_wait_st();
         }
-      }
-      float mx = -INFINITY;
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < kTcBN; ++c) mx = fmaxf(mx, __uint_as_float(sv[c >> 5][c & 31]));
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], __uint_as_float(sv[c][e]));
+        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      }
       const float mt = mx * kLog2e;
       const bool move = mt > m + 8.f;
       if (__any_sync(0xffffffffu, move)) {
@@ -399,47 +423,72 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         m = mn;
       }
       const float ref = m == -INFINITY ? 0.f : m;
-      // P (bf16 pairs) into columns [0, 64) of this S buffer, over the S values just read.
-#pragma unroll
+      // Pass 2: P (bf16 pairs) into columns [0, 64) of this S buffer, 64 keys at a time; the
+      // P words of keys [64 h, 64 h + 64) land on S columns already consumed.
+      float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
       for (int h = 0; h < 2; ++h) {
+        uint32_t sv[2][32];
+        tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN + 64 * h, sv[0]);
+        tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN + 64 * h + 32, sv[1]);
+        tmem_wait_ld();
         uint32_t pw[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const int c = 64 * h + 2 * e;
-          const float p0 = ex2_tc(fmaf(__uint_as_float(sv[c >> 5][c & 31]), kLog2e, -ref));
-          const float p1 = ex2_tc(fmaf(__uint_as_float(sv[(c + 1) >> 5][(c + 1) & 31]), kLog2e, -ref));
-          l += p0 + p1;
+          const float p0 = ex2_tc(fmaf(__uint_as_float(sv[e >> 4][(2 * e) & 31]), kLog2e, -ref));
+          const float p1 = ex2_tc(fmaf(__uint_as_float(sv[e >> 4][(2 * e + 1) & 31]), kLog2e, -ref));
+          l4[e & 3] += p0 + p1;
           pw[e] = pack_bf16x2(p0, p1);
         }
         tmem_st_32x32b_x32(tmem + lane_off + b * kTcBN + 32 * h, pw);
       }
+      l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(p_full_l0 + 8u * b);
     }
-    // ---- O / l -> bf16 (this CTA's rows, the pair's 256 output columns)
+    // ---- O / l -> bf16 rows staged in shared memory (the ring is idle once O is final)
+    // in the output map's box layout, then one TMA store (rows past T are clipped).
     if (ok) ok = mbar_wait_bounded(o_ready, 0, abort_flag, &g_attn_status);
-    if (__all_sync(0xffffffffu, ok)) {
+    const bool good = __all_sync(0xffffffffu, ok);
+    if (good) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = a.o + head * a.o_head + static_cast<int64_t>(qpos) * a.o_tok + half * kTcDV;
 #pragma unroll 1
       for (int c = 0; c < kTcDV / 32; ++c) {
         uint32_t ov[32];
         tmem_ld_32x32b_x32(tmem + lane_off + kColO + c * 32, ov);
         tmem_wait_ld();
-        if (qpos < a.t) {
+        // columns 32 c .. 32 c + 31: block c / 2, 16-byte chunks 4 (c % 2) .. + 3
+        const uint32_t row = ring + (c >> 1) * (kTcBM * 128) + r * 128;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t w[4];
+        for (int j = 0; j < 4; ++j) {
+          uint32_t w[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              w[e] = pack_bf16x2(__uint_as_float(ov[8 * j + 2 * e]) * inv, __uint_as_float(ov[8 * j + 2 * e + 1]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + j * 8) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
+          for (int e = 0; e < 4; ++e)
+            w[e] = pack_bf16x2(__uint_as_float(ov[8 * j + 2 * e]) * inv, __uint_as_float(ov[8 * j + 2 * e + 1]) * inv);
+          const int chunk = 4 * (c & 1) + j;
+          st_shared_v4(row + ((chunk ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
         }
       }
+      fence_proxy_async_smem();
+    }
+    // All four softmax warps meet here on every path; the tile is stored only if each of
+    // them staged its rows.
+    uint32_t all_good;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.and.pred p, 1, 128, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(all_good)
+        : "r"(good ? 1u : 0u)
+        : "memory");
+    if (all_good && warp == 2 && lane == 0) {
+      tma_store_4d(&tm_o, ring, 0, q0, head0, half * (kTcDV / 64));
+      bulk_commit_group();
+      bulk_wait_group<0>();
     }
   }
   __syncwarp();
@@ -534,6 +583,9 @@ static int attention_tc_go(const uint16_t* q, int64_t q_head, int64_t q_tok, con
   if (st != W8_OK) return st;
   st = encode_heads(&tv, v, D, kv_heads, t, v_head, v_tok, false, w8::kTcBN, 1, 2);
   if (st != W8_OK) return st;
+  CUtensorMap to;
+  st = encode_heads(&to, o, D, heads, t, o_head, o_tok, true, rows, static_cast<uint32_t>(pack), w8::kTcDV / 64);
+  if (st != W8_OK) return st;
   static bool done[64] = {};
   if (device < 0 || device >= 64) return W8_ERR_UNSUPPORTED;
   if (!done[device]) {
@@ -553,7 +605,7 @@ static int attention_tc_go(const uint16_t* q, int64_t q_head, int64_t q_tok, con
   // Two CTAs (a cluster) per 2 * rows queries, head group and output half.
   const int64_t blocks = 2 * ((t + 2 * rows - 1) / (2 * rows)) * (heads / pack) * (D / w8::kTcDV);
   W8_CHECK_ARG(blocks < (1ll << 31), "too many query blocks");
-  w8::attention_tc_kernel<D><<<static_cast<unsigned>(blocks), w8::kTcThreads, C::kSmem, stream>>>(tq, tk, tv, a);
+  w8::attention_tc_kernel<D><<<static_cast<unsigned>(blocks), w8::kTcThreads, C::kSmem, stream>>>(tq, tk, tv, to, a);
   return cuda_status(cudaGetLastError());
 }
 
