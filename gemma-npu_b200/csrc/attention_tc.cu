@@ -47,7 +47,8 @@ __device__ int g_attn_status = 0;
 constexpr int kTcBM = 128;                  // rows per CTA (TMEM lanes); 256 per pair
 constexpr int kTcBN = 128;                  // keys per tile
 constexpr int kTcDV = 256;                  // output columns per pair
-constexpr int kTcThreads = 192;             // TMA warp, MMA warp, 4 softmax warps
+constexpr int kTcSoftWarps = 8;             // two per TMEM lane quarter, 64 keys each
+constexpr int kTcThreads = 32 * (2 + kTcSoftWarps);  // TMA warp, MMA warp, softmax warps
 constexpr int kSlotBytes = 32768;           // K: 64 keys x 256 columns; V: 128 keys x 128 columns
 constexpr int kKeysPerCta = kTcBN / 2;      // keys of a tile each CTA stages for S
 constexpr uint32_t kTmemCols = 512;
@@ -62,7 +63,8 @@ struct TcCfg {
   static constexpr int kOffBar = kOffRing + kSlots * kSlotBytes;
   // full[kSlots], empty[kSlots], q_full, s_full[2], p_full[2], pv_done[2], o_ready
   static constexpr int kNumBars = 2 * kSlots + 8;
-  static constexpr int kSmem = kOffBar + kNumBars * 8 + 16 + 1024;
+  static constexpr int kOffXch = kOffBar + kNumBars * 8 + 16;  // float [2][128]: the partner's row max / sum
+  static constexpr int kSmem = kOffXch + 2 * kTcBM * 4 + 1024;
   static_assert(kSmem <= 232448, "shared memory budget exceeded");
 };
 
@@ -215,7 +217,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     mbar_init(q_full, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(s_full(b), 1);
-      mbar_init(p_full(b), 8);  // leader: the softmax warps of both CTAs
+      mbar_init(p_full(b), 2 * kTcSoftWarps);  // leader: the softmax warps of both CTAs
       mbar_init(pv_done(b), 1);
     }
     mbar_init(o_ready, 1);
@@ -344,58 +346,59 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       mbar_wait_bounded(o_ready, 0, nullptr, &g_attn_status);
     }
   } else {
-    // ---- softmax (both CTAs): thread = row r = TMEM lane r (warp w reads lanes 32 (w % 4) ..)
+    // ---- softmax (both CTAs): row r = TMEM lane r is shared by warps w and w + 4 (warp w
+    // may access lanes 32 (w % 4) ..), each taking 64 of the tile's 128 keys and 128 of
+    // the 256 output columns; the two exchange their row maxima (and at the end their
+    // sums) through shared memory under a 64-thread named barrier.
     const int quarter = warp & 3;
+    const int hv = (warp - 2) >> 2;  // which half of the keys / output columns
     const int r = quarter * 32 + lane;
     const int qpos = q0 + r % qb_rows;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t p_full_l0 = mapa_shared(p_full(0), 0);
+    volatile float* xch = reinterpret_cast<volatile float*>(smem + C::kOffXch);
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory"); };
     constexpr float kLog2e = 1.4426950408889634f;
-    float m = -INFINITY, l = 0.f;  // m in log2 units
+    float m = -INFINITY, l = 0.f;  // m in log2 units, l over this warp's keys
     bool ok = true;
+    // Every warp runs every iteration and meets its partner at the same pair barriers on
+    // every path: after a timeout it only skips its waits and its work.
     for (int i = 0; i < ntiles; ++i) {
       const int b = i & 1, k0 = (kt0 + i) * kTcBN;
-      ok = mbar_wait_bounded(s_full(b), (i >> 1) & 1, abort_flag, &g_attn_status);
+      if (ok) ok = mbar_wait_bounded(s_full(b), (i >> 1) & 1, abort_flag, &g_attn_status);
       // O += P_{i-2} V_{i-2} has completed (it ran before S_i); observing it keeps the
       // phase of pv_done(b) known for the wait on O += P_{i-1} V_{i-1} below.
-      if (i >= 2) ok = ok && mbar_wait_bounded(pv_done(b), ((i - 2) >> 1) & 1, abort_flag, &g_attn_status);
-      if (!__all_sync(0xffffffffu, ok)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // Pass 1: the row maximum.  Boundary tiles (causal diagonal, window edge, keys past T)
-      // mask per element and write the masked row back, so pass 2 needs no masks.
-      const bool interior = k0 + kTcBN - 1 <= q0 && k0 + kTcBN <= a.t &&
-                            (a.window == 0 || k0 >= q0 + qb_rows - a.window);
-      float mx;
-      {
-        uint32_t sv[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN + 32 * c, sv[c]);
+      if (ok && i >= 2) ok = mbar_wait_bounded(pv_done(b), ((i - 2) >> 1) & 1, abort_flag, &g_attn_status);
+      ok = __all_sync(0xffffffffu, ok);
+      uint32_t sv[2][32];
+      float mx = -INFINITY;
+      if (ok) {
+        tc_fence_after();
+        tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN + 64 * hv, sv[0]);
+        tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN + 64 * hv + 32, sv[1]);
         tmem_wait_ld();
+        // Boundary tiles (causal diagonal, window edge, keys past T) are masked per element.
+        const bool interior = k0 + kTcBN - 1 <= q0 && k0 + kTcBN <= a.t &&
+                              (a.window == 0 || k0 >= q0 + qb_rows - a.window);
         if (!interior) {
-          // valid keys: lo <= key <= hi
-          const int hi = min(qpos, a.t - 1) - k0;
-          const int lo = a.window > 0 ? qpos - a.window + 1 - k0 : -1;
+          const int hi = min(qpos, a.t - 1) - k0 - 64 * hv;  // valid keys: lo <= key <= hi
+          const int lo = a.window > 0 ? qpos - a.window + 1 - k0 - 64 * hv : -1;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int key = 32 * c + e;
-              if (key < lo || key > hi) sv[c][e] = __float_as_uint(-INFINITY);
-            }
-            tmem_st_32x32b_x32(tmem + lane_off + b * kTcBN + 32 * c, sv[c]);
-          }
-          tmem_wait_st();
+          for (int c = 0; c < 64; ++c)
+            if (c < lo || c > hi) sv[c >> 5][c & 31] = __float_as_uint(-INFINITY);
         }
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], __uint_as_float(sv[c][e]));
+        for (int c = 0; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(sv[c >> 5][c & 31]));
         mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       }
+      xch[hv * kTcBM + r] = mx;
+      tc_fence_before();
+      pair_sync();  // both halves of S are in registers and both maxima are posted
+      tc_fence_after();
+      mx = fmaxf(mx, xch[(hv ^ 1) * kTcBM + r]);
+      pair_sync();  // the partner's maximum is read before either posts the next one
+      if (!ok) continue;
       const float mt = mx * kLog2e;
       const bool move = mt > m + 8.f;
       if (__any_sync(0xffffffffu, move)) {
@@ -404,44 +407,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         if (i > 0) {
           // O must hold tiles < i before it is rescaled: wait for O += P_{i-1} V_{i-1}.
           ok = mbar_wait_bounded(pv_done((i - 1) & 1), ((i - 1) >> 1) & 1, abort_flag, &g_attn_status);
-          if (!__all_sync(0xffffffffu, ok)) {
-            ok = false;
-            break;
-          }
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) continue;
           tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < kTcDV / 32; ++c) {
+          for (int c = 0; c < kTcDV / 64; ++c) {
             uint32_t ov[32];
-            tmem_ld_32x32b_x32(tmem + lane_off + kColO + c * 32, ov);
+            const uint32_t col = kColO + 128 * hv + c * 32;
+            tmem_ld_32x32b_x32(tmem + lane_off + col, ov);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * corr);
-            tmem_st_32x32b_x32(tmem + lane_off + kColO + c * 32, ov);
+            tmem_st_32x32b_x32(tmem + lane_off + col, ov);
           }
         }
         l *= corr;
         m = mn;
       }
       const float ref = m == -INFINITY ? 0.f : m;
-      // Pass 2: P (bf16 pairs) into columns [0, 64) of this S buffer, 64 keys at a time; the
-      // P words of keys [64 h, 64 h + 64) land on S columns already consumed.
+      // P (bf16 pairs) of this warp's 64 keys into columns [32 hv, 32 hv + 32) of the S
+      // buffer: S values both warps already hold in registers (first pair barrier).
       float l4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        uint32_t sv[2][32];
-        tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN + 64 * h, sv[0]);
-        tmem_ld_32x32b_x32(tmem + lane_off + b * kTcBN + 64 * h + 32, sv[1]);
-        tmem_wait_ld();
-        uint32_t pw[32];
+      uint32_t pw[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float p0 = ex2_tc(fmaf(__uint_as_float(sv[e >> 4][(2 * e) & 31]), kLog2e, -ref));
-          const float p1 = ex2_tc(fmaf(__uint_as_float(sv[e >> 4][(2 * e + 1) & 31]), kLog2e, -ref));
-          l4[e & 3] += p0 + p1;
-          pw[e] = pack_bf16x2(p0, p1);
-        }
-        tmem_st_32x32b_x32(tmem + lane_off + b * kTcBN + 32 * h, pw);
+      for (int e = 0; e < 32; ++e) {
+        const float p0 = ex2_tc(fmaf(__uint_as_float(sv[e >> 4][(2 * e) & 31]), kLog2e, -ref));
+        const float p1 = ex2_tc(fmaf(__uint_as_float(sv[e >> 4][(2 * e + 1) & 31]), kLog2e, -ref));
+        l4[e & 3] += p0 + p1;
+        pw[e] = pack_bf16x2(p0, p1);
       }
+      tmem_st_32x32b_x32(tmem + lane_off + b * kTcBN + 32 * hv, pw);
       l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
       tmem_wait_st();
       tc_fence_before();
@@ -452,38 +447,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     // in the output map's box layout, then one TMA store (rows past T are clipped).
     if (ok) ok = mbar_wait_bounded(o_ready, 0, abort_flag, &g_attn_status);
     const bool good = __all_sync(0xffffffffu, ok);
+    // The row sum over both halves of the keys (the pair barriers stay matched on every path).
+    xch[hv * kTcBM + r] = l;
+    pair_sync();
+    const float lt = l + xch[(hv ^ 1) * kTcBM + r];
     if (good) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < kTcDV / 32; ++c) {
+      for (int c = 0; c < kTcDV / 64; ++c) {
         uint32_t ov[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + kColO + c * 32, ov);
+        const int col = 128 * hv + c * 32;  // this warp's columns col .. col + 31
+        tmem_ld_32x32b_x32(tmem + lane_off + kColO + col, ov);
         tmem_wait_ld();
-        // columns 32 c .. 32 c + 31: block c / 2, 16-byte chunks 4 (c % 2) .. + 3
-        const uint32_t row = ring + (c >> 1) * (kTcBM * 128) + r * 128;
+        // block col / 64, 16-byte chunks 4 (col / 32 % 2) .. + 3
+        const uint32_t row = ring + (col >> 6) * (kTcBM * 128) + r * 128;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e)
             w[e] = pack_bf16x2(__uint_as_float(ov[8 * j + 2 * e]) * inv, __uint_as_float(ov[8 * j + 2 * e + 1]) * inv);
-          const int chunk = 4 * (c & 1) + j;
+          const int chunk = 4 * ((col >> 5) & 1) + j;
           st_shared_v4(row + ((chunk ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
         }
       }
       fence_proxy_async_smem();
     }
-    // All four softmax warps meet here on every path; the tile is stored only if each of
-    // them staged its rows.
+    // All softmax warps meet here on every path; the tile is stored only if each of them
+    // staged its rows.
     uint32_t all_good;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.u32 q, %1, 0;\n\t"
-        "bar.red.and.pred p, 1, 128, q;\n\t"
+        "bar.red.and.pred p, 5, %2, q;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(all_good)
-        : "r"(good ? 1u : 0u)
+        : "r"(good ? 1u : 0u), "n"(32 * kTcSoftWarps)
         : "memory");
     if (all_good && warp == 2 && lane == 0) {
       tma_store_4d(&tm_o, ring, 0, q0, head0, half * (kTcDV / 64));
