@@ -700,6 +700,8 @@ def main():
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 prompts / sharded LM head objects")
     ap.add_argument("--no-fused", action="store_true", help="skip the fused gate/up glue object")
     ap.add_argument("--no-attention", action="store_true", help="skip the prefill attention object")
+    ap.add_argument("--only-attention", action="store_true",
+                    help="time only the prefill attention object (--steps / --warmup replays; profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -722,6 +724,11 @@ def main():
     try:
         pk = peaks()
         stream = torch.cuda.Stream(device=dev)
+        if args.only_attention:
+            att = attention_bench(w8, dev, stream, args.m, args.steps, args.warmup, world)
+            if rank == 0:
+                print(json.dumps({"attention": att}), flush=True)
+            return
         if args.sweep:
             table = sweep(w8, dev, stream, args.steps, args.warmup)
             if rank == 0:

@@ -441,7 +441,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(p_full_l0 + 8u * b);
+      // The leader's own warps release at CTA scope; the peer's P must be ordered at
+      // cluster scope before the leader's MMA reads it.
+      if (lane == 0) {
+        if (rank == 0)
+          mbar_arrive(p_full(b));
+        else
+          mbar_arrive_cluster(p_full_l0 + 8u * b);
+      }
     }
     // ---- O / l -> bf16 rows staged in shared memory (the ring is idle once O is final)
     // in the output map's box layout, then one TMA store (rows past T are clipped).
