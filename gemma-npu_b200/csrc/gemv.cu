@@ -7,15 +7,17 @@
 // logit softcap of the prefill (pipeline.py:335-338): cap * tanh(float(y) / cap).
 //
 // The kernel is HBM-bound: every weight byte is read once with 16-byte non-allocating
-// loads, coalesced across the warp.  The activation row is converted to fp32 once per
-// thread and kept in registers: lane l of the warp owning K-slice `sl` multiplies the
-// 16 consecutive k of chunk c, k = ((sl*J + c)*32 + l)*16 .. +15, of every weight row it
-// visits.  S warps ("a team") split K; the team's partial sums meet in shared memory,
-// and lane r of the team's first warp finishes row r (scale, bf16, softcap, store).
-// int8 -> fp32 uses the exponent trick: byte b (offset to b+128) is placed in the
-// mantissa of 2^23 with one PRMT and the bias removed exactly; the bias subtraction and
-// the multiply-add use sm_100's packed f32x2 instructions (two bytes per instruction),
-// which keeps the kernel off the issue limit at full HBM rate.
+// loads, coalesced across the warp.  Each activation row is held as 16-bit fixed point
+// over its own range, x_q = rint(x * 32767 / max|x|) (every CTA derives the same scale),
+// split into a signed high byte and an unsigned low byte (x_q = 256 hi + lo) and kept in
+// registers: lane l of the warp owning K-slice `sl` multiplies the 16 consecutive k of
+// chunk c, k = ((sl*J + c)*32 + l)*16 .. +15, of every weight row it visits.  Every 4
+// weight bytes take two dp4a instructions into exact int32 sums, so the kernel issues
+// about a quarter of the instructions of an fp32 dot product and is left bound by HBM.
+// One rounding at the end: y = bf16(s * (256 sum_hi + sum_lo) * max|x| / 32767).  The
+// fixed point costs at most max|x| / 65534 per element of x, far inside the GEMV's
+// max-rel 1e-2 bound.  S warps ("a team") split K; the team's partial sums meet in shared
+// memory, and lane r of the team's first warp finishes row r (scale, bf16, softcap, store).
 // Weight loads of the first row batch are issued before waiting for the previous kernel
 // of the stream (programmatic dependent launch): only the activation row depends on it.
 #include "common.cuh"
@@ -31,39 +33,6 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
-}
-
-// Two fp32 values in one 64-bit register pair, for sm_100's packed f32x2 instructions.
-__device__ __forceinline__ uint64_t pack_f32x2(uint32_t lo, uint32_t hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
-  return r;
-}
-__device__ __forceinline__ float sum_f32x2(uint64_t v) {
-  float lo, hi;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-  return lo + hi;
-}
-
-// (acc0, acc1) += the 16 signed bytes of `w` times x (8 packed pairs of fp32).
-// Byte b, offset to u = b + 128, is placed in the mantissa of 2^23 with one PRMT
-// (2^23 + u, exact); one packed add of -(2^23 + 128) per two bytes leaves b exactly,
-// and one packed FMA per two bytes accumulates: 9 instructions per 4 bytes.
-__device__ __forceinline__ void dot16_i8(const uint4& w, const uint64_t (&xp)[8], uint64_t& acc0,
-                                         uint64_t& acc1) {
-  const uint64_t neg_bias = pack_f32x2(0xCB000080u, 0xCB000080u);  // -(2^23 + 128) twice
-  const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t u = words[j] ^ 0x80808080u;
-    const uint64_t f01 = pack_f32x2(__byte_perm(u, 0x4B000000u, 0x7540), __byte_perm(u, 0x4B000000u, 0x7541));
-    const uint64_t f23 = pack_f32x2(__byte_perm(u, 0x4B000000u, 0x7542), __byte_perm(u, 0x4B000000u, 0x7543));
-    uint64_t d01, d23;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d01) : "l"(f01), "l"(neg_bias));
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d23) : "l"(f23), "l"(neg_bias));
-    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc0) : "l"(d01), "l"(xp[2 * j]));
-    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc1) : "l"(d23), "l"(xp[2 * j + 1]));
-  }
 }
 
 // Output of one row: bf16 of the scaled sum, optionally softcapped to fp32; returns the
@@ -92,16 +61,40 @@ __device__ __forceinline__ unsigned long long argmax_key(float f, int row) {
 }
 
 // J: 16-byte chunks per lane per row; S: warps splitting K; R: rows per team per step.
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// (hi, lo) += the 16 signed weight bytes of w times the lane's 16 x codes.
+__device__ __forceinline__ void dot16_q(const uint4& w, const uint32_t (&xh)[4], const uint32_t (&xl)[4], int& hi,
+                                        int& lo) {
+  hi = dp4a_ss(w.x, xh[0], hi);
+  lo = dp4a_su(w.x, xl[0], lo);
+  hi = dp4a_ss(w.y, xh[1], hi);
+  lo = dp4a_su(w.y, xl[1], lo);
+  hi = dp4a_ss(w.z, xh[2], hi);
+  lo = dp4a_su(w.z, xl[2], lo);
+  hi = dp4a_ss(w.w, xh[3], hi);
+  lo = dp4a_su(w.w, xl[3], lo);
+}
+
 template <int J, int S, int R, bool LOGITS>
 __global__ void __launch_bounds__(kGemvThreads)
     int8_gemv_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
-                     const int8_t* __restrict__ w, int64_t ldw, const __nv_bfloat16* __restrict__ s,
-                     void* __restrict__ y, int64_t ldy, int t_count, int n, int k, float cap,
-                     unsigned long long* __restrict__ best) {
+                         const int8_t* __restrict__ w, int64_t ldw, const __nv_bfloat16* __restrict__ s,
+                         void* __restrict__ y, int64_t ldy, int t_count, int n, int k, float cap,
+                         unsigned long long* __restrict__ best) {
   static_assert(kGemvWarps % S == 0, "S must divide the CTA's warps");
   unsigned long long mine = 0ull;  // best argmax_key this thread wrote (LM head, t_count == 1)
   constexpr int kTeams = kGemvWarps / S;
   __shared__ float red[kTeams][S][R];
+  __shared__ float amax_w[kGemvWarps];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int team = warp / S;
@@ -128,20 +121,54 @@ __global__ void __launch_bounds__(kGemvThreads)
   pdl_wait();
 
   for (int t = 0; t < t_count; ++t) {
-    // This lane's slice of the activation row, in fp32 pairs (bf16 -> fp32 is exact).
-    uint64_t xp[J][8];
+    const __nv_bfloat16* xt = x + static_cast<int64_t>(t) * ldx;
+    // This lane's 16-element pieces of the row; the team's lanes cover all of K, so the
+    // row maximum is a warp reduction, plus one exchange among the team's S warps.
+    uint32_t words[J][8];
+    __nv_bfloat162 am2 = __floats2bfloat162_rn(0.f, 0.f);  // |x| maxima, two lanes of bf16
 #pragma unroll
     for (int c = 0; c < J; ++c) {
       const int k0 = ((sl * J + c) * 32 + lane) * 16;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) words[c][i] = 0u;
       if (k0 < k) {
-        const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * ldx + k0);
+        const uint4* p = reinterpret_cast<const uint4*>(xt + k0);
         const uint4 a = __ldg(p), b = __ldg(p + 1);
-        const uint32_t words[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        words[c][0] = a.x, words[c][1] = a.y, words[c][2] = a.z, words[c][3] = a.w;
+        words[c][4] = b.x, words[c][5] = b.y, words[c][6] = b.z, words[c][7] = b.w;
+      }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) xp[c][i] = pack_f32x2(words[i] << 16, words[i] & 0xFFFF0000u);
-      } else {
+      for (int i = 0; i < 8; ++i) am2 = __hmax2(am2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&words[c][i])));
+    }
+    float am = fmaxf(__low2float(am2), __high2float(am2));
 #pragma unroll
-        for (int i = 0; i < 8; ++i) xp[c][i] = 0ull;
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    if constexpr (S > 1) {
+      if (lane == 0) amax_w[warp] = am;
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");
+      am = amax_w[team * S];
+#pragma unroll
+      for (int q = 1; q < S; ++q) am = fmaxf(am, amax_w[team * S + q]);
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");  // read before reuse
+    }
+    const float qs = am > 0.f ? 32767.f / am : 0.f;  // x -> code
+    const float dq = am > 0.f ? am / 32767.f : 0.f;  // code -> x
+    // Codes: fma(x, qs, 1.5 * 2^23) rounds x * qs to the nearest integer (one rounding),
+    // whose two's complement low 16 bits are the float's low 16 bits; byte permutes gather
+    // the low bytes (unsigned lo) and the high bytes (signed hi) of four codes per word.
+    constexpr float kMagic = 12582912.f;
+    uint32_t xh[J][4], xl[J][4];
+#pragma unroll
+    for (int c = 0; c < J; ++c) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t w0 = words[c][2 * q], w1 = words[c][2 * q + 1];
+        const uint32_t u0 = __float_as_uint(fmaf(__uint_as_float(w0 << 16), qs, kMagic));
+        const uint32_t u1 = __float_as_uint(fmaf(__uint_as_float(w0 & 0xFFFF0000u), qs, kMagic));
+        const uint32_t u2 = __float_as_uint(fmaf(__uint_as_float(w1 << 16), qs, kMagic));
+        const uint32_t u3 = __float_as_uint(fmaf(__uint_as_float(w1 & 0xFFFF0000u), qs, kMagic));
+        xl[c][q] = __byte_perm(__byte_perm(u0, u1, 0x0040), __byte_perm(u2, u3, 0x0040), 0x5410);
+        xh[c][q] = __byte_perm(__byte_perm(u0, u1, 0x0051), __byte_perm(u2, u3, 0x0051), 0x5410);
       }
     }
 
@@ -150,15 +177,15 @@ __global__ void __launch_bounds__(kGemvThreads)
       float acc[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        uint64_t a0 = 0ull, a1 = 0ull;
+        int hi = 0, lo = 0;
 #pragma unroll
-        for (int c = 0; c < J; ++c) dot16_i8(wv[r][c], xp[c], a0, a1);
-        acc[r] = sum_f32x2(a0) + sum_f32x2(a1);
+        for (int c = 0; c < J; ++c) dot16_q(wv[r][c], xh[c], xl[c], hi, lo);
+        // The lane's exact sum (|.| < 2^31 for J <= 4), then one fp32 warp reduction.
+        float v = static_cast<float>(256 * hi + lo);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        acc[r] = v * dq;
       }
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
 
       // Lane r finishes row n0 + r (scale, bf16 rounding, softcap, store), in parallel.
       if constexpr (S == 1) {
