@@ -379,8 +379,8 @@ def int8_linear(x2d, wq, sw, out=None):
     """bf16 [T,N] = (x2d @ wq^T) * sw: the weight-only int8 GEMV of decode.
 
     The reference's cpu_int8_linear (gemma_npu.py:155-156), i.e.
-    torch._weight_int8pack_mm(x_bf16, wq [N,K] int8, sw [N] bf16), with fp32
-    accumulation on the GPU.
+    torch._weight_int8pack_mm(x_bf16, wq [N,K] int8, sw [N] bf16), within max-rel 1e-2:
+    the GPU holds each row of x as 16-bit fixed point and sums exactly in int32.
     """
     _need(isinstance(x2d, torch.Tensor) and x2d.is_cuda, "x2d must be a CUDA tensor; there is no CPU path")
     if x2d.dtype != torch.bfloat16:
