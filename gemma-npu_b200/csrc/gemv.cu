@@ -7,15 +7,15 @@
 // logit softcap of the prefill (pipeline.py:335-338): cap * tanh(float(y) / cap).
 //
 // The kernel is HBM-bound: every weight byte is read once with 16-byte non-allocating
-// loads, coalesced across the warp.  Each activation row is held as 16-bit fixed point
-// over its own range, x_q = rint(x * 32767 / max|x|) (every CTA derives the same scale),
-// split into a signed high byte and an unsigned low byte (x_q = 256 hi + lo) and kept in
-// registers: lane l of the warp owning K-slice `sl` multiplies the 16 consecutive k of
-// chunk c, k = ((sl*J + c)*32 + l)*16 .. +15, of every weight row it visits.  Every 4
-// weight bytes take two dp4a instructions into exact int32 sums, so the kernel issues
-// about a quarter of the instructions of an fp32 dot product and is left bound by HBM.
-// One rounding at the end: y = bf16(s * (256 sum_hi + sum_lo) * max|x| / 32767).  The
-// fixed point costs at most max|x| / 65534 per element of x, far inside the GEMV's
+// loads, coalesced across the warp.  The activation row is held in registers as 16-bit
+// fixed point, each 16-element piece over its own range, x_q = rint(x * 32766 / max|x|),
+// split into a signed high byte and an unsigned low byte (x_q = 256 hi + lo): lane l of
+// the warp owning K-slice `sl` multiplies the 16 consecutive k of chunk c,
+// k = ((sl*J + c)*32 + l)*16 .. +15, of every weight row it visits.  Every 4 weight bytes
+// take two dp4a instructions into exact int32 sums, so the kernel issues about a quarter
+// of the instructions of an fp32 dot product and is left bound by HBM; each piece's sum is
+// scaled once, y = bf16(s * sum_pieces (256 sum_hi + sum_lo) * max|x_piece| / 32766).  The
+// fixed point costs at most max|x_piece| / 65532 per element, far inside the GEMV's
 // max-rel 1e-2 bound.  S warps ("a team") split K; the team's partial sums meet in shared
 // memory, and lane r of the team's first warp finishes row r (scale, bf16, softcap, store).
 // Weight loads of the first row batch are issued before waiting for the previous kernel
@@ -26,6 +26,7 @@ namespace w8 {
 
 constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kGemvSmemCap = 96 * 1024;  // dynamic shared memory per CTA: at most 2 CTAs per SM
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;
@@ -94,7 +95,6 @@ __global__ void __launch_bounds__(kGemvThreads)
   unsigned long long mine = 0ull;  // best argmax_key this thread wrote (LM head, t_count == 1)
   constexpr int kTeams = kGemvWarps / S;
   __shared__ float red[kTeams][S][R];
-  __shared__ float amax_w[kGemvWarps];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int team = warp / S;
@@ -122,47 +122,34 @@ __global__ void __launch_bounds__(kGemvThreads)
 
   for (int t = 0; t < t_count; ++t) {
     const __nv_bfloat16* xt = x + static_cast<int64_t>(t) * ldx;
-    // This lane's 16-element pieces of the row; the team's lanes cover all of K, so the
-    // row maximum is a warp reduction, plus one exchange among the team's S warps.
-    uint32_t words[J][8];
-    __nv_bfloat162 am2 = __floats2bfloat162_rn(0.f, 0.f);  // |x| maxima, two lanes of bf16
+    // This lane's 16-element pieces of the row, each as 16-bit fixed point over its own
+    // range: no reduction across lanes or warps before the dot products.  fma(x, qs,
+    // 1.5 * 2^23) rounds x * qs to the nearest integer (one rounding), whose two's
+    // complement low 16 bits are the float's low 16 bits; byte permutes gather the low
+    // bytes (unsigned lo) and the high bytes (signed hi) of four codes per word.
+    constexpr float kMagic = 12582912.f;
+    uint32_t xh[J][4], xl[J][4];
+    float dq[J];
 #pragma unroll
     for (int c = 0; c < J; ++c) {
       const int k0 = ((sl * J + c) * 32 + lane) * 16;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) words[c][i] = 0u;
+      uint32_t words[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
       if (k0 < k) {
         const uint4* p = reinterpret_cast<const uint4*>(xt + k0);
         const uint4 a = __ldg(p), b = __ldg(p + 1);
-        words[c][0] = a.x, words[c][1] = a.y, words[c][2] = a.z, words[c][3] = a.w;
-        words[c][4] = b.x, words[c][5] = b.y, words[c][6] = b.z, words[c][7] = b.w;
+        words[0] = a.x, words[1] = a.y, words[2] = a.z, words[3] = a.w;
+        words[4] = b.x, words[5] = b.y, words[6] = b.z, words[7] = b.w;
       }
+      __nv_bfloat162 m2 = __habs2(*reinterpret_cast<const __nv_bfloat162*>(&words[0]));
 #pragma unroll
-      for (int i = 0; i < 8; ++i) am2 = __hmax2(am2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&words[c][i])));
-    }
-    float am = fmaxf(__low2float(am2), __high2float(am2));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    if constexpr (S > 1) {
-      if (lane == 0) amax_w[warp] = am;
-      asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");
-      am = amax_w[team * S];
-#pragma unroll
-      for (int q = 1; q < S; ++q) am = fmaxf(am, amax_w[team * S + q]);
-      asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");  // read before reuse
-    }
-    const float qs = am > 0.f ? 32767.f / am : 0.f;  // x -> code
-    const float dq = am > 0.f ? am / 32767.f : 0.f;  // code -> x
-    // Codes: fma(x, qs, 1.5 * 2^23) rounds x * qs to the nearest integer (one rounding),
-    // whose two's complement low 16 bits are the float's low 16 bits; byte permutes gather
-    // the low bytes (unsigned lo) and the high bytes (signed hi) of four codes per word.
-    constexpr float kMagic = 12582912.f;
-    uint32_t xh[J][4], xl[J][4];
-#pragma unroll
-    for (int c = 0; c < J; ++c) {
+      for (int i = 1; i < 8; ++i) m2 = __hmax2(m2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&words[i])));
+      const float am = fmaxf(__low2float(m2), __high2float(m2));
+      // 32766 (not 32767) keeps every code inside int16 under the approximate division.
+      const float qs = am > 0.f ? __fdividef(32766.f, am) : 0.f;
+      dq[c] = am * (1.f / 32766.f);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const uint32_t w0 = words[c][2 * q], w1 = words[c][2 * q + 1];
+        const uint32_t w0 = words[2 * q], w1 = words[2 * q + 1];
         const uint32_t u0 = __float_as_uint(fmaf(__uint_as_float(w0 << 16), qs, kMagic));
         const uint32_t u1 = __float_as_uint(fmaf(__uint_as_float(w0 & 0xFFFF0000u), qs, kMagic));
         const uint32_t u2 = __float_as_uint(fmaf(__uint_as_float(w1 << 16), qs, kMagic));
@@ -177,14 +164,17 @@ __global__ void __launch_bounds__(kGemvThreads)
       float acc[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        int hi = 0, lo = 0;
+        // Each piece's exact int32 sum times its scale, then one fp32 warp reduction.
+        float v = 0.f;
 #pragma unroll
-        for (int c = 0; c < J; ++c) dot16_q(wv[r][c], xh[c], xl[c], hi, lo);
-        // The lane's exact sum (|.| < 2^31 for J <= 4), then one fp32 warp reduction.
-        float v = static_cast<float>(256 * hi + lo);
+        for (int c = 0; c < J; ++c) {
+          int hi = 0, lo = 0;
+          dot16_q(wv[r][c], xh[c], xl[c], hi, lo);
+          v = fmaf(static_cast<float>(256 * hi + lo), dq[c], v);
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        acc[r] = v * dq;
+        acc[r] = v;
       }
 
       // Lane r finishes row n0 + r (scale, bf16 rounding, softcap, store), in parallel.
@@ -237,8 +227,18 @@ static int launch_gemv(const __nv_bfloat16* x, int64_t ldx, const int8_t* w, int
   int sms = 0;
   int st = num_sms(&sms);
   if (st != W8_OK) return st;
+  // The (unused) dynamic shared memory caps residency at two CTAs per SM: with three or
+  // four, a chain of dependent GEMVs ran slower (qkv 2560 x 1536: 3.07 against 3.74 us).
+  int device = 0;
+  W8_CUDA_TRY(cudaGetDevice(&device));
+  static bool done[64] = {};
+  if (device < 0 || device >= 64) return W8_ERR_UNSUPPORTED;
+  if (!done[device]) {
+    W8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, w8::kGemvSmemCap));
+    done[device] = true;
+  }
   int per_sm = 0;
-  W8_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, w8::kGemvThreads, 0));
+  W8_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, w8::kGemvThreads, w8::kGemvSmemCap));
   if (per_sm < 1) per_sm = 1;
   constexpr int rows_per_cta = (w8::kGemvWarps / S) * R;
   const int64_t need = (static_cast<int64_t>(n) + rows_per_cta - 1) / rows_per_cta;
@@ -249,7 +249,7 @@ static int launch_gemv(const __nv_bfloat16* x, int64_t ldx, const int8_t* w, int
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(w8::kGemvThreads, 1, 1);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = w8::kGemvSmemCap;
   cfg.stream = stream;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;

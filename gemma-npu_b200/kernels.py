@@ -380,7 +380,7 @@ def int8_linear(x2d, wq, sw, out=None):
 
     The reference's cpu_int8_linear (gemma_npu.py:155-156), i.e.
     torch._weight_int8pack_mm(x_bf16, wq [N,K] int8, sw [N] bf16), within max-rel 1e-2:
-    the GPU holds each row of x as 16-bit fixed point and sums exactly in int32.
+    the GPU holds x as 16-bit fixed point per 16-element piece and sums exactly in int32.
     """
     _need(isinstance(x2d, torch.Tensor) and x2d.is_cuda, "x2d must be a CUDA tensor; there is no CPU path")
     if x2d.dtype != torch.bfloat16:

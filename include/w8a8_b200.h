@@ -214,7 +214,7 @@ int w8_dequant_bf16(const int32_t* acc, int64_t ldacc, const float* sx, const fl
 /* ---- decode: weight-only int8 GEMV / LM head -------------------------- */
 
 /* y[t,n] (bf16) = bf16(float(s[n]) * sum_k float(x[t,k]) * w[n,k]) within max-rel 1e-2:
- * each row of x as 16-bit fixed point over its own range, exact int32 dot products.
+ * x as 16-bit fixed point over each 16-element piece's range, exact int32 dot products.
  * x bf16 [T,K], w int8 [N,K] row-major, s bf16 [N].  K % 16 == 0, ldw % 16 == 0,
  * ldx % 8 == 0, 16-byte aligned x and w.
  * Replaces cpu_int8_linear (gemma_npu.py:155-156), i.e. torch._weight_int8pack_mm. */

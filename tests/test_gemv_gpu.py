@@ -3,8 +3,8 @@
 Tolerance: normwise max-rel <= 1e-2, i.e.
 max|gpu - ref| <= 1e-2 * max|ref|, against gemma_npu.cpu_int8_linear
 (torch._weight_int8pack_mm, gemma_npu.py:155-156) and Int8Head + softcap
-(gemma_npu.py:170-172, pipeline.py:335-338).  The kernel holds each activation row as
-16-bit fixed point and sums exactly in int32, ATen accumulates in fp32, so bit equality is
+(gemma_npu.py:170-172, pipeline.py:335-338).  The kernel holds the activation row as
+16-bit fixed point (per 16-element piece) and sums exactly in int32, ATen accumulates in fp32, so bit equality is
 not expected.
 """
 import numpy as np
