@@ -78,10 +78,11 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 __device__ __forceinline__ uint4 ld16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
 // pow(mean(x^2) + eps, -0.5) of this warp's row, held packed in v[].
-__device__ __forceinline__ float rms_factor(const uint4 (&v)[kGlueMaxVecs], int nv, int lane, int n, float eps) {
+template <int NV>
+__device__ __forceinline__ float rms_factor(const uint4 (&v)[NV], int nv, int lane, int n, float eps) {
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kGlueMaxVecs; ++i)
+  for (int i = 0; i < NV; ++i)
     if (lane + 32 * i < nv) {
       float f[8];
       unpack8(v[i], f);
@@ -95,10 +96,11 @@ __device__ __forceinline__ float rms_factor(const uint4 (&v)[kGlueMaxVecs], int 
 __device__ __forceinline__ float rbf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // One row of the glue (the warp's registers hold the row between the steps).
-template <int MODE>
+// NV: 16-byte vectors per lane the row may need (row length <= 256 NV).
+template <int MODE, int NV>
 __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, int nv, const uint4* w1s,
                                          const uint4* w2s) {
-  constexpr int kMax = MODE == kGlueAttnOut ? kGlueMaxVecsAttn : kGlueMaxVecs;
+  constexpr int kMax = NV;
   uint4 v[kMax];
 #pragma unroll
   for (int i = 0; i < kMax; ++i) {
@@ -113,13 +115,13 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
     }
   }
   if constexpr (MODE != kGlueAttnOut) {
-    uint4 res[MODE == kGlueIn ? 1 : kGlueMaxVecs];
+    uint4 res[MODE == kGlueIn ? 1 : NV];
     if constexpr (MODE != kGlueIn) {
 #pragma unroll
       for (int i = 0; i < kMax; ++i)
         if (lane + 32 * i < nv) res[i] = ld16(a.res + static_cast<int64_t>(row) * a.ldr + (lane + 32 * i) * 8);
     }
-    const float r1 = rms_factor(v, nv, lane, a.n, a.eps);
+    const float r1 = rms_factor<NV>(v, nv, lane, a.n, a.eps);
 #pragma unroll
     for (int i = 0; i < kMax; ++i) {
       const int vi = lane + 32 * i;
@@ -140,7 +142,7 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
       }
     }
     if constexpr (MODE == kGluePost2) {
-      const float r2 = rms_factor(v, nv, lane, a.n, a.eps);
+      const float r2 = rms_factor<NV>(v, nv, lane, a.n, a.eps);
 #pragma unroll
       for (int i = 0; i < kMax; ++i) {
         const int vi = lane + 32 * i;
@@ -183,11 +185,15 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
   }
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(32 * kGlueWarps, 3) glue_rows_kernel(const GlueArgs a) {
-  // The norm weights are the same for every row: staged once per CTA in shared memory.
-  __shared__ uint4 w1s[MODE == kGlueAttnOut ? 1 : 32 * kGlueMaxVecs];
-  __shared__ uint4 w2s[MODE == kGluePost2 ? 32 * kGlueMaxVecs : 1];
+// Rows of at most 1536 values (the hidden size) keep 4 CTAs (32 warps) per SM resident, so a
+// 3658-token prompt needs no second pass over rows.
+template <int MODE, int NV>
+__global__ void __launch_bounds__(32 * kGlueWarps, NV <= 6 ? 4 : 3) glue_rows_kernel(const GlueArgs a) {
+  pdl_launch_dependents();
+  // The norm weights are the same for every row: staged once per CTA in shared memory,
+  // before waiting for the previous kernel of the stream (they do not depend on it).
+  __shared__ uint4 w1s[MODE == kGlueAttnOut ? 1 : 32 * NV];
+  __shared__ uint4 w2s[MODE == kGluePost2 ? 32 * NV : 1];
   const int nv = a.n / 8;
   if constexpr (MODE != kGlueAttnOut) {
     for (int i = threadIdx.x; i < nv; i += blockDim.x) {
@@ -196,9 +202,10 @@ __global__ void __launch_bounds__(32 * kGlueWarps, 3) glue_rows_kernel(const Glu
     }
     __syncthreads();
   }
+  pdl_wait();  // the rows come from the previous kernel
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int row = blockIdx.x * kGlueWarps + warp; row < a.t; row += gridDim.x * kGlueWarps)
-    glue_row<MODE>(a, row, lane, nv, w1s, w2s);
+    glue_row<MODE, NV>(a, row, lane, nv, w1s, w2s);
 }
 
 // k_qkv (pipeline.py:72-86) after the qkv GEMM with the dequant fused (y = _deq(acc),
@@ -223,6 +230,8 @@ struct QkvArgs {
 };
 
 __global__ void __launch_bounds__(32 * kGlueWarps) qkv_rows_kernel(const QkvArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();  // y comes from the previous kernel
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per_tok = a.shared ? a.heads : a.heads + 2 * a.kv_heads;
   const int64_t job = static_cast<int64_t>(blockIdx.x) * kGlueWarps + warp;
@@ -308,6 +317,24 @@ namespace w8host {
 
 int require_sm100(int* device);
 
+// Launch with programmatic stream serialization: the kernel may start (and stage its
+// constant operands) while the previous kernel of the stream drains; it waits for that
+// kernel (griddepcontrol.wait) before reading its output.
+template <typename Kernel, typename Args>
+static int launch_pdl_glue(Kernel kern, unsigned grid, const Args& a, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(32 * w8::kGlueWarps, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, a));
+}
+
 // One warp per row, at most as many CTAs as fit on the GPU at once (each warp then loops
 // over rows a grid's worth of warps apart).
 template <typename Kernel>
@@ -319,8 +346,7 @@ static int glue_go(Kernel kern, const w8::GlueArgs& a, cudaStream_t stream) {
   const int64_t need = (static_cast<int64_t>(a.t) + w8::kGlueWarps - 1) / w8::kGlueWarps;
   const int64_t cap = static_cast<int64_t>(sms) * (per_sm > 0 ? per_sm : 1);
   const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
-  kern<<<grid, 32 * w8::kGlueWarps, 0, stream>>>(a);
-  return cuda_status(cudaGetLastError());
+  return launch_pdl_glue(kern, grid, a, stream);
 }
 
 static int glue_launch(int mode, const w8::GlueArgs& a, cudaStream_t stream) {
@@ -357,10 +383,19 @@ static int glue_launch(int mode, const w8::GlueArgs& a, cudaStream_t stream) {
   const int st = require_sm100(&device);
   if (st != W8_OK) return st;
   switch (mode) {
-    case w8::kGlueIn: return glue_go(w8::glue_rows_kernel<w8::kGlueIn>, a, stream);
-    case w8::kGluePost1: return glue_go(w8::glue_rows_kernel<w8::kGluePost1>, a, stream);
-    case w8::kGluePost2: return glue_go(w8::glue_rows_kernel<w8::kGluePost2>, a, stream);
-    default: return glue_go(w8::glue_rows_kernel<w8::kGlueAttnOut>, a, stream);
+    case w8::kGlueIn:
+      return a.n <= 1536 ? glue_go(w8::glue_rows_kernel<w8::kGlueIn, 6>, a, stream)
+                         : glue_go(w8::glue_rows_kernel<w8::kGlueIn, w8::kGlueMaxVecs>, a, stream);
+    case w8::kGluePost1:
+      return a.n <= 1536 ? glue_go(w8::glue_rows_kernel<w8::kGluePost1, 6>, a, stream)
+                         : glue_go(w8::glue_rows_kernel<w8::kGluePost1, w8::kGlueMaxVecs>, a, stream);
+    case w8::kGluePost2:
+      return a.n <= 1536 ? glue_go(w8::glue_rows_kernel<w8::kGluePost2, 6>, a, stream)
+                         : glue_go(w8::glue_rows_kernel<w8::kGluePost2, w8::kGlueMaxVecs>, a, stream);
+    default:
+      return a.n <= 32 * 8 * w8::kGlueMaxVecs
+                 ? glue_go(w8::glue_rows_kernel<w8::kGlueAttnOut, w8::kGlueMaxVecs>, a, stream)
+                 : glue_go(w8::glue_rows_kernel<w8::kGlueAttnOut, w8::kGlueMaxVecsAttn>, a, stream);
   }
 }
 
@@ -465,6 +500,5 @@ extern "C" int w8_qkv_norm_rope_bf16(const uint16_t* y, int64_t ldy, const uint1
   a.shared = shared != 0;
   const int64_t jobs = t * per_tok;
   const unsigned grid = static_cast<unsigned>((jobs + w8::kGlueWarps - 1) / w8::kGlueWarps);
-  w8::qkv_rows_kernel<<<grid, 32 * w8::kGlueWarps, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
-  return cuda_status(cudaGetLastError());
+  return launch_pdl_glue(w8::qkv_rows_kernel, grid, a, reinterpret_cast<cudaStream_t>(stream));
 }
