@@ -204,42 +204,76 @@ def timed(replay, steps, warmup, stream, world):
     return ms
 
 
-def e2e_prefill(w8, work, dev, steps, warmup, world):
-    """Host-buffer path: per GEMM, pinned int8 activations -> HBM, GEMM, int32 result -> pinned host."""
+def e2e_prefill(w8, work, dev, steps, warmup, world, dequant=True):
+    """Host-buffer path of the config-1 step through the reference-facing calls: per GEMM,
+    pinned host int8 activations (and, with dequant, their fp32 row scales) -> HBM, the
+    GEMM, the result -> pinned host (one host buffer per projection; every GEMM has its own
+    device output, so no copy out waits for a later GEMM).  dequant=True runs `gemm_dequant` (int32 accumulate
+    plus the _deq epilogue, bf16 out: config 0's full operation); dequant=False runs
+    `mm_i8_nk` (int32 out, the data flow of pipeline.py's Prefill.gemm).  Copies in, GEMMs
+    and copies out run on three streams ordered by events, so PCIe traffic in both
+    directions overlaps the GEMMs."""
     import torch.distributed as dist
 
-    host_in, host_out = {}, {}
-    for xq, wq, c, name in work["calls"]:
-        if name not in host_in:
+    calls = work["calls"]
+    g = torch.Generator(device=dev).manual_seed(7)
+    out_dtype = torch.bfloat16 if dequant else torch.int32
+    host_in, host_sx, host_out, scales, outs = {}, {}, {}, [], []
+    for xq, wq, _, name in calls:
+        if name not in host_in:  # host buffers per projection (each layer's result overwrites the last)
             host_in[name] = xq.cpu().pin_memory()
-            host_out[name] = torch.empty(c.shape, dtype=torch.int32).pin_memory()
-    stream = torch.cuda.current_stream()
-    bi = sum(xq.numel() for xq, _, _, _ in work["calls"])
-    bo = sum(4 * c.numel() for _, _, c, _ in work["calls"])
+            host_sx[name] = (torch.rand((xq.shape[0],), generator=None) * 1e-2 + 1e-3).pin_memory()
+            host_out[name] = torch.empty((xq.shape[0], wq.shape[0]), dtype=out_dtype).pin_memory()
+        sx = torch.empty((xq.shape[0],), dtype=torch.float32, device=dev)
+        sw = torch.rand((wq.shape[0],), device=dev, generator=g) * 1e-3 + 1e-4
+        scales.append((sx, sw))
+        outs.append(torch.empty((xq.shape[0], wq.shape[0]), dtype=out_dtype, device=dev))
+    bi = sum(xq.numel() + (4 * xq.shape[0] if dequant else 0) for xq, _, _, _ in calls)
+    bo = sum(o.numel() * o.element_size() for o in outs)
+    s_in, s_mm, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
     def step():
-        for xq, wq, c, name in work["calls"]:
-            xq.copy_(host_in[name], non_blocking=True)
-            w8.mm_i8_nk(xq, wq, c)
-            host_out[name].copy_(c, non_blocking=True)
-        stream.synchronize()  # the results are on the host when the step ends
+        for i, (xq, wq, _, name) in enumerate(calls):
+            sx, sw = scales[i]
+            with torch.cuda.stream(s_in):
+                xq.copy_(host_in[name], non_blocking=True)
+                if dequant:
+                    sx.copy_(host_sx[name], non_blocking=True)
+                e_in = torch.cuda.Event()
+                e_in.record(s_in)
+            with torch.cuda.stream(s_mm):
+                s_mm.wait_event(e_in)
+                if dequant:
+                    w8.gemm_dequant(xq, wq, sx, sw, out=outs[i])
+                else:
+                    w8.mm_i8_nk(xq, wq, outs[i])
+                e_mm = torch.cuda.Event()
+                e_mm.record(s_mm)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(e_mm)
+                host_out[name].copy_(outs[i], non_blocking=True)
 
     for _ in range(warmup):
         step()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
+    start.record(s_in)
+    s_mm.wait_stream(s_in)
+    s_out.wait_stream(s_in)
     for _ in range(steps):
         step()
-    end.record(stream)
+        torch.cuda.synchronize()  # the results are on the host when the step ends
+    s_in.wait_stream(s_out)
+    end.record(s_in)
     end.synchronize()
     ms = start.elapsed_time(end)
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    del outs, host_out
     return ms / steps, bi, bo
 
 
@@ -781,11 +815,19 @@ def main():
         }
         del graph
         if not args.no_e2e and args.only is None:
-            e_ms, bi, bo = e2e_prefill(w8, work, dev, args.e2e_steps, 1, world)
+            e_ms, bi, bo = e2e_prefill(w8, work, dev, args.e2e_steps, 1, world, dequant=True)
             line["e2e"] = {"value": world * work["ops"] / (e_ms * 1e-3) / 1e12, "unit": "TOPS",
                            "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo, "ms_per_step": e_ms,
                            "steps": args.e2e_steps,
-                           "path": "gemma_npu_b200.mm_i8_nk per GEMM: pinned int8 activations H2D, int32 results D2H"}
+                           "path": "gemma_npu_b200.gemm_dequant per GEMM (int32 accumulate + the _deq epilogue, "
+                                   "config 0's operation): pinned int8 activations + fp32 row scales H2D, bf16 "
+                                   "results D2H; copies in, GEMMs and copies out on three streams"}
+            e_ms, bi, bo = e2e_prefill(w8, work, dev, args.e2e_steps, 1, world, dequant=False)
+            line["e2e_int32"] = {"value": world * work["ops"] / (e_ms * 1e-3) / 1e12, "unit": "TOPS",
+                                 "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo, "ms_per_step": e_ms,
+                                 "steps": args.e2e_steps,
+                                 "path": "gemma_npu_b200.mm_i8_nk per GEMM: pinned int8 activations H2D, int32 results "
+                                         "D2H (pipeline.py's Prefill.gemm data flow); same three-stream pipeline"}
         if not args.no_decode and args.only is None:
             step, nbytes, launches, head = build_decode(w8, work, dev)
             dgraph = capture(step, stream)
