@@ -10,8 +10,9 @@ N(0, 1) quantised per token, seeded per layer, distinct buffers per layer (synth
 no checkpoint is available).  The step is captured once into a CUDA graph and replayed.
 
 `value` is whole-job TOPS with inputs resident in HBM; `e2e` is the same metric through
-the reference-facing API with host buffers (pinned int8 activations copied in, int32
-results copied out every step, as the reference's CPU glue consumes them).  The decode
+the reference-facing API with host buffers (pinned int8 activations and row scales copied
+in, the fused-dequant GEMM, bf16 results copied out every step; `e2e_int32` copies the
+int32 results out instead, as pipeline.py's CPU glue consumes them).  The decode
 weight-only GEMV chain (config 2: the same 140 layer weights + the 262144-wide LM head
 with the softcap fused) is reported beside it in GB/s.
 
