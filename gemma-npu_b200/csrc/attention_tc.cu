@@ -108,7 +108,7 @@ __device__ __forceinline__ void mma_bf16_ts_pair(uint32_t d_tmem, uint32_t a_tme
       : "memory");
 }
 
-// 4-D tiled load (no multicast) into this CTA's shared memory, completion counted on `bar`,
+// 4-D tiled load (plain, one destination CTA) into this CTA's shared memory, completion counted on `bar`,
 // a shared::cluster barrier address that may lie in the peer CTA.
 __device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const CUtensorMap* m, uint32_t bar, int x, int y,
                                                  int z, int w) {
