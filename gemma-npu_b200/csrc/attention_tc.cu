@@ -235,6 +235,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   tc_fence_before();
   cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
   tc_fence_after();
+  // Programmatic dependent launch: the setup above overlapped the previous kernel's tail;
+  // q, k, v (its output) are read only from here on.
+  pdl_launch_dependents();
+  pdl_wait();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
@@ -612,8 +616,17 @@ static int attention_tc_go(const uint16_t* q, int64_t q_head, int64_t q_tok, con
   // Two CTAs (a cluster) per 2 * rows queries, head group and output half.
   const int64_t blocks = 2 * ((t + 2 * rows - 1) / (2 * rows)) * (heads / pack) * (D / w8::kTcDV);
   W8_CHECK_ARG(blocks < (1ll << 31), "too many query blocks");
-  w8::attention_tc_kernel<D><<<static_cast<unsigned>(blocks), w8::kTcThreads, C::kSmem, stream>>>(tq, tk, tv, to, a);
-  return cuda_status(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+  cfg.blockDim = dim3(w8::kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, w8::attention_tc_kernel<D>, tq, tk, tv, to, a));
 }
 
 // The tcgen05 schedule of w8_attention_prefill_bf16 (arguments checked by the caller).
