@@ -533,8 +533,7 @@ def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35):
             d = l["d"]
             y = w8.gemm_dequant(xq, l["qkv"][0], sx, l["qkv"][1])
             q, k, v = w8.qkv_norm_rope(y, *tables[d], l["qn"], l["kn"], eps, nh, kv, d)
-            o = w8.attention_prefill(q, k, v, l["win"])
-            xq, sx = w8.attn_out_quant(o)
+            xq, sx = w8.attention_quant(q, k, v, l["win"])  # attention + k_attn_out
             y = w8.gemm_dequant(xq, l["o"][0], sx, l["o"][1])
             _, xq, sx = w8.post_norm_quant(y, h, l["w_post"], l["w_pre"], eps, h=h)
             xq, sx = w8.gelu_up_quant(xq, sx, *l["gup"])

@@ -87,6 +87,8 @@ SIGNATURES = {
     "w8_attention_prefill_mma_bf16": (_i, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64,
                                            _i64, _i64, _i64, _i64, _i64, _p]),
     "w8_attn_out_quant_bf16": (_i, [_p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _p]),
+    "w8_attention_prefill_quant": (_i, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i64,
+                                        _i64, _p, _i64, _p, _p]),
     "w8_gemm_gelu_up_quant": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _p, _p]),
     "w8_quant_rows_bf16": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _p]),
     "w8_quant_rows_f32": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _p]),

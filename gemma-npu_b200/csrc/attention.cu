@@ -300,6 +300,11 @@ int attention_tc(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_
                  int64_t k_tok, const uint16_t* v, int64_t v_head, int64_t v_tok, uint16_t* o, int64_t o_head,
                  int64_t o_tok, int64_t t, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t window,
                  int device, cudaStream_t stream);
+bool attention_tc_quant_fits(int64_t heads, int64_t kv_heads, int64_t head_dim);
+int attention_tc_quant(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k, int64_t k_head,
+                       int64_t k_tok, const uint16_t* v, int64_t v_head, int64_t v_tok, int64_t t, int64_t heads,
+                       int64_t kv_heads, int64_t window, int8_t* xq, int64_t ldq, float* xs, int device,
+                       cudaStream_t stream);
 
 // Argument checks shared by both schedules, then the tcgen05 one (tc) or the mma.sync one.
 static int attention_entry(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k, int64_t k_head,
@@ -358,4 +363,32 @@ extern "C" int w8_attention_prefill_mma_bf16(const uint16_t* q, int64_t q_head, 
                                              w8_stream_t stream) {
   return w8host::attention_entry(q, q_head, q_tok, k, k_head, k_tok, v, v_head, v_tok, o, o_head, o_tok, t, heads,
                                  kv_heads, head_dim, window, stream, false);
+}
+
+extern "C" int w8_attention_prefill_quant(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k,
+                                          int64_t k_head, int64_t k_tok, const uint16_t* v, int64_t v_head,
+                                          int64_t v_tok, int64_t t, int64_t heads, int64_t kv_heads,
+                                          int64_t head_dim, int64_t window, int8_t* xq, int64_t ldq, float* xs,
+                                          w8_stream_t stream) {
+  using namespace w8host;
+  W8_CHECK_ARG(t >= 0 && t < (1ll << 31) && heads >= 0 && kv_heads >= 0 && window >= 0, "bad size");
+  if (t == 0 || heads == 0) return W8_OK;
+  if (!attention_tc_quant_fits(heads, kv_heads, head_dim)) {
+    set_error("the fused attention + k_attn_out takes head_dim 256, one KV head and a power-of-two head count "
+              "<= 16 (got head_dim %lld, heads %lld, kv_heads %lld)",
+              (long long)head_dim, (long long)heads, (long long)kv_heads);
+    return W8_ERR_UNSUPPORTED;
+  }
+  W8_CHECK_ARG(q != nullptr && k != nullptr && v != nullptr && xq != nullptr && xs != nullptr, "null pointer");
+  W8_CHECK_ALIGN(aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && q_head % 8 == 0 && q_tok % 8 == 0 &&
+                     k_head % 8 == 0 && k_tok % 8 == 0 && v_head % 8 == 0 && v_tok % 8 == 0,
+                 "q, k, v must be 16-byte aligned with pitches %% 8 == 0");
+  W8_CHECK_ALIGN(aligned(xq, 16) && ldq % 16 == 0 && aligned(xs, 4), "xq must be 16-byte aligned, ldq %% 16 == 0");
+  W8_CHECK_ARG(q_tok >= head_dim && k_tok >= head_dim && v_tok >= head_dim && ldq >= heads * head_dim,
+               "pitch too small");
+  int device = 0;
+  const int st = require_sm100(&device);
+  if (st != W8_OK) return st;
+  return attention_tc_quant(q, q_head, q_tok, k, k_head, k_tok, v, v_head, v_tok, t, heads, kv_heads, window, xq,
+                            ldq, xs, device, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -36,6 +36,7 @@
 // mbarrier wait is bounded; on a timeout the kernel records W8_ERR_DEVICE_TIMEOUT, drains
 // its own copies and MMAs, frees TMEM and returns.
 #include "common.cuh"
+#include "rowquant.cuh"
 
 #include <algorithm>
 #include <mutex>
@@ -73,6 +74,11 @@ struct AttnTcArgs {
   int64_t o_head, o_tok;
   int t, heads, kv_heads, window;
   int pack;  // heads per CTA (PK); 128 / PK queries per CTA
+  // k_attn_out fused (head_dim 256, PK = heads): the per-token _quant of the output rows,
+  // q [T, heads * 256] int8 (row pitch ldq) and s [T] fp32, instead of o.
+  int8_t* q;
+  int64_t ldq;
+  float* s;
 };
 
 // kind::f16 instruction descriptor: bf16 A and B, fp32 D, M x N, A K-major, B K- or MN-major.
@@ -454,52 +460,109 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           mbar_arrive_cluster(p_full_l0 + 8u * b);
       }
     }
-    // ---- O / l -> bf16 rows staged in shared memory (the ring is idle once O is final)
-    // in the output map's box layout, then one TMA store (rows past T are clipped).
     if (ok) ok = mbar_wait_bounded(o_ready, 0, abort_flag, &g_attn_status);
     const bool good = __all_sync(0xffffffffu, ok);
     // The row sum over both halves of the keys (the pair barriers stay matched on every path).
     xch[hv * kTcBM + r] = l;
     pair_sync();
     const float lt = l + xch[(hv ^ 1) * kTcBM + r];
-    if (good) {
-      tc_fence_after();
+    auto softmax_sync = [&]() { asm volatile("bar.sync 5, %0;" ::"n"(32 * kTcSoftWarps) : "memory"); };
+    if (a.q != nullptr) {
+      // ---- k_attn_out fused (pipeline.py:88-92): every head of each of this CTA's tokens is
+      // one of its rows, so the token's _quant over heads * 256 values happens here: the
+      // bf16 output values (the ones o would hold), max |.| per token through shared
+      // memory, then the int8 codes with _quant's scale and rounding.
       const float inv = lt > 0.f ? 1.f / lt : 0.f;
-#pragma unroll 1
-      for (int c = 0; c < kTcDV / 64; ++c) {
-        uint32_t ov[32];
-        const int col = 128 * hv + c * 32;  // this warp's columns col .. col + 31
-        tmem_ld_32x32b_x32(tmem + lane_off + kColO + col, ov);
-        tmem_wait_ld();
-        // block col / 64, 16-byte chunks 4 (col / 32 % 2) .. + 3
-        const uint32_t row = ring + (col >> 6) * (kTcBM * 128) + r * 128;
+      uint32_t pw[64];  // this thread's 128 bf16 output values, packed pairs
+      float am = 0.f;
+      if (good) {
+        tc_fence_after();
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t w[4];
+        for (int c = 0; c < kTcDV / 64; ++c) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(tmem + lane_off + kColO + 128 * hv + c * 32, ov);
+          tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            w[e] = pack_bf16x2(__uint_as_float(ov[8 * j + 2 * e]) * inv, __uint_as_float(ov[8 * j + 2 * e + 1]) * inv);
-          const int chunk = 4 * ((col >> 5) & 1) + j;
-          st_shared_v4(row + ((chunk ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
+          for (int e = 0; e < 16; ++e) {
+            const float v0 = __uint_as_float(ov[2 * e]) * inv, v1 = __uint_as_float(ov[2 * e + 1]) * inv;
+            pw[16 * c + e] = pack_bf16x2(v0, v1);
+            const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&pw[16 * c + e]);
+            am = fmaxf(am, fmaxf(fabsf(__low2float(h2)), fabsf(__high2float(h2))));
+          }
         }
       }
-      fence_proxy_async_smem();
-    }
-    // All softmax warps meet here on every path; the tile is stored only if each of them
-    // staged its rows.
-    uint32_t all_good;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 q, %1, 0;\n\t"
-        "bar.red.and.pred p, 5, %2, q;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(all_good)
-        : "r"(good ? 1u : 0u), "n"(32 * kTcSoftWarps)
-        : "memory");
-    if (all_good && warp == 2 && lane == 0) {
-      tma_store_4d(&tm_o, ring, 0, q0, head0, half * (kTcDV / 64));
-      bulk_commit_group();
-      bulk_wait_group<0>();
+      const int qi = r % qb_rows, slot = (r / qb_rows) * 2 + hv;  // token, (head, half)
+      softmax_sync();  // every row sum above is read before xch is reused
+      xch[qi * 2 * pk + slot] = am;
+      softmax_sync();
+      float tam = 0.f;
+      for (int i = 0; i < 2 * pk; ++i) tam = fmaxf(tam, xch[qi * 2 * pk + i]);
+      const float sc = __fdiv_rn(fmaxf(tam, 1e-8f), 127.f);
+      const float rc = __frcp_rn(sc);
+      if (good && qpos < a.t) {
+        const int head = head0 + r / qb_rows;
+        int8_t* dst = a.q + static_cast<int64_t>(qpos) * a.ldq + head * kTcDV + 128 * hv;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {  // 16 values -> 16 bytes
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            int8_t b4[4];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&pw[8 * j + 2 * e + u]);
+              b4[2 * u] = quant_one(__low2float(h2), sc, rc);
+              b4[2 * u + 1] = quant_one(__high2float(h2), sc, rc);
+            }
+            w[e] = pack4(b4);
+          }
+          *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        if (slot == 0) a.s[qpos] = sc;
+      }
+    } else {
+      // ---- O / l -> bf16 rows staged in shared memory (the ring is idle once O is final)
+      // in the output map's box layout, then one TMA store (rows past T are clipped).
+      if (good) {
+        tc_fence_after();
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < kTcDV / 64; ++c) {
+          uint32_t ov[32];
+          const int col = 128 * hv + c * 32;  // this warp's columns col .. col + 31
+          tmem_ld_32x32b_x32(tmem + lane_off + kColO + col, ov);
+          tmem_wait_ld();
+          // block col / 64, 16-byte chunks 4 (col / 32 % 2) .. + 3
+          const uint32_t row = ring + (col >> 6) * (kTcBM * 128) + r * 128;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              w[e] = pack_bf16x2(__uint_as_float(ov[8 * j + 2 * e]) * inv,
+                                 __uint_as_float(ov[8 * j + 2 * e + 1]) * inv);
+            const int chunk = 4 * ((col >> 5) & 1) + j;
+            st_shared_v4(row + ((chunk ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
+          }
+        }
+        fence_proxy_async_smem();
+      }
+      // All softmax warps meet here on every path; the tile is stored only if each of them
+      // staged its rows.
+      uint32_t all_good;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\t"
+          "setp.ne.u32 q, %1, 0;\n\t"
+          "bar.red.and.pred p, 5, %2, q;\n\t"
+          "selp.u32 %0, 1, 0, p;\n\t}"
+          : "=r"(all_good)
+          : "r"(good ? 1u : 0u), "n"(32 * kTcSoftWarps)
+          : "memory");
+      if (all_good && warp == 2 && lane == 0) {
+        tma_store_4d(&tm_o, ring, 0, q0, head0, half * (kTcDV / 64));
+        bulk_commit_group();
+        bulk_wait_group<0>();
+      }
     }
   }
   __syncwarp();
@@ -581,7 +644,8 @@ template <int D>
 static int attention_tc_go(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k, int64_t k_head,
                            int64_t k_tok, const uint16_t* v, int64_t v_head, int64_t v_tok, uint16_t* o,
                            int64_t o_head, int64_t o_tok, int64_t t, int64_t heads, int64_t kv_heads,
-                           int64_t window, int device, cudaStream_t stream) {
+                           int64_t window, int device, cudaStream_t stream, int8_t* xq = nullptr,
+                           int64_t ldq = 0, float* xs = nullptr) {
   using C = w8::TcCfg<D>;
   // Heads per CTA: the largest power of two <= 16 dividing the query-group size.
   const int64_t group = heads / kv_heads;
@@ -613,6 +677,9 @@ static int attention_tc_go(const uint16_t* q, int64_t q_head, int64_t q_tok, con
   a.kv_heads = static_cast<int>(kv_heads);
   a.window = static_cast<int>(window);
   a.pack = pack;
+  a.q = xq;
+  a.ldq = ldq;
+  a.s = xs;
   // Two CTAs (a cluster) per 2 * rows queries, head group and output half.
   const int64_t blocks = 2 * ((t + 2 * rows - 1) / (2 * rows)) * (heads / pack) * (D / w8::kTcDV);
   W8_CHECK_ARG(blocks < (1ll << 31), "too many query blocks");
@@ -639,6 +706,23 @@ int attention_tc(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_
                                 kv_heads, window, device, stream);
   return attention_tc_go<512>(q, q_head, q_tok, k, k_head, k_tok, v, v_head, v_tok, o, o_head, o_tok, t, heads,
                               kv_heads, window, device, stream);
+}
+
+// Whether attention_tc_quant takes a shape: head_dim 256 and every head of a token in one
+// CTA (one KV head, heads a power of two <= 16).
+bool attention_tc_quant_fits(int64_t heads, int64_t kv_heads, int64_t head_dim) {
+  return head_dim == 256 && kv_heads == 1 && heads >= 1 && heads <= 16 && (heads & (heads - 1)) == 0;
+}
+
+// Attention with k_attn_out fused (arguments checked by the caller, the shape fits): the
+// int8 rows q [T, heads * 256] (pitch ldq) and scales s [T] instead of the bf16 output.
+int attention_tc_quant(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k, int64_t k_head,
+                       int64_t k_tok, const uint16_t* v, int64_t v_head, int64_t v_tok, int64_t t, int64_t heads,
+                       int64_t kv_heads, int64_t window, int8_t* xq, int64_t ldq, float* xs, int device,
+                       cudaStream_t stream) {
+  // The output tensor map is never used on this path: it is encoded over q (valid bf16).
+  return attention_tc_go<256>(q, q_head, q_tok, k, k_head, k_tok, v, v_head, v_tok, const_cast<uint16_t*>(q), q_head,
+                              q_tok, t, heads, kv_heads, window, device, stream, xq, ldq, xs);
 }
 
 // Read (and optionally clear) the attention kernel's sticky device status.

@@ -319,6 +319,30 @@ def attention_prefill(q, k, v, window=0, out=None, schedule="tc"):
     return out
 
 
+def attention_quant(q, k, v, window=0, xq=None, xs=None):
+    """Prefill attention followed by k_attn_out (pipeline.py:139-180 then :88-92): returns
+    the per-token _quant of the attention output, (xq int8 [T, H*D], xs fp32 [T]),
+    bit-identical to attn_out_quant(attention_prefill(q, k, v, window)).  One kernel when
+    head_dim is 256 with one KV head and a power-of-two head count <= 16 (the Gemma E2B
+    sliding layers); the two-step path otherwise."""
+    for t_, name in ((q, "q"), (k, "k"), (v, "v")):
+        _need(isinstance(t_, torch.Tensor) and t_.is_cuda and t_.dtype == torch.bfloat16 and t_.dim() == 3
+              and t_.stride(2) == 1, f"{name} must be a bf16 CUDA tensor [heads, T, D] with unit stride along D")
+    H, T, D = q.shape
+    KV = k.shape[0]
+    _need(tuple(k.shape) == (KV, T, D) and tuple(v.shape) == (KV, T, D), "k and v must be [KV, T, D]")
+    xq = torch.empty((T, H * D), dtype=torch.int8, device=q.device) if xq is None else xq
+    xs = torch.empty((T,), dtype=torch.float32, device=q.device) if xs is None else xs
+    _check_matrix(xq, "xq", torch.int8)
+    _check_vector(xs, "xs", torch.float32, T)
+    if D == 256 and KV == 1 and 1 <= H <= 16 and H & (H - 1) == 0:
+        _lib.call("w8_attention_prefill_quant", q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), k.stride(0),
+                  k.stride(1), v.data_ptr(), v.stride(0), v.stride(1), T, H, KV, D, int(window), xq.data_ptr(),
+                  _ld(xq), xs.data_ptr(), _stream(q))
+        return xq, xs
+    return attn_out_quant(attention_prefill(q, k, v, window), xq, xs)
+
+
 def attn_out_quant(o, q=None, s=None):
     """k_attn_out (pipeline.py:88-92): o bf16 [H, T, D] -> _quant of its [T, H*D] rows."""
     _need(isinstance(o, torch.Tensor) and o.is_cuda and o.dtype == torch.bfloat16 and o.dim() == 3,

@@ -27,6 +27,7 @@
  *   w8_attn_out_quant_bf16  pipeline.py:88-92 (k_attn_out)
  *   w8_qkv_norm_rope_bf16   pipeline.py:72-86 (k_qkv)
  *   w8_attention_prefill_bf16 pipeline.py:139-180 (full_attention / sliding_attention)
+ *   w8_attention_prefill_quant the same followed by pipeline.py:88-92 (k_attn_out)
  */
 #ifndef W8A8_B200_H
 #define W8A8_B200_H
@@ -187,6 +188,17 @@ int w8_attention_prefill_bf16(const uint16_t* q, int64_t q_head, int64_t q_tok, 
                               int64_t v_tok, uint16_t* o, int64_t o_head, int64_t o_tok, int64_t t,
                               int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t window,
                               w8_stream_t stream);
+/* Attention followed by k_attn_out (pipeline.py:88-92) in one kernel: instead of o, the
+ * per-token _quant of its rows, xq [T, heads * head_dim] int8 (pitch ldq) and xs [T] fp32,
+ * bit-identical to w8_attention_prefill_bf16 then w8_attn_out_quant_bf16.  Takes head_dim
+ * 256, kv_heads 1 and heads a power of two <= 16 (every head of a token in one CTA: the
+ * Gemma E2B sliding layers); other shapes return W8_ERR_UNSUPPORTED.  xq 16-byte aligned,
+ * ldq % 16 == 0. */
+int w8_attention_prefill_quant(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k,
+                               int64_t k_head, int64_t k_tok, const uint16_t* v, int64_t v_head,
+                               int64_t v_tok, int64_t t, int64_t heads, int64_t kv_heads,
+                               int64_t head_dim, int64_t window, int8_t* xq, int64_t ldq, float* xs,
+                               w8_stream_t stream);
 /* The same contract on warp-level mma.sync tiles (no TMA, no TMEM): a second, independent
  * schedule, kept as a cross-check of the tcgen05 one. */
 int w8_attention_prefill_mma_bf16(const uint16_t* q, int64_t q_head, int64_t q_tok, const uint16_t* k,

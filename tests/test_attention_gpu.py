@@ -40,8 +40,11 @@ def test_golden(cuda, golden, name, schedule):
 
 # (T, H, KV, D, window): Gemma E2B sliding (D 256, W 512) and full (D 512) layers at the
 # config-1 length, ragged T, more KV heads, a window longer than the prompt.
+# Grouped-query packing: group size 8 -> 8 heads x 16 queries per CTA, 4 -> 4 x 32, 16 -> 16 x 8,
+# 3 -> one head per CTA (the largest power of two dividing 3 is 1).
 SHAPES = [(3658, 8, 1, 256, 512), (3658, 8, 1, 512, 0), (1000, 4, 2, 256, 0), (77, 2, 1, 256, 512),
-          (700, 8, 8, 512, 128), (1, 1, 1, 256, 0), (129, 2, 1, 512, 64)]
+          (700, 8, 8, 512, 128), (1, 1, 1, 256, 0), (129, 2, 1, 512, 64), (500, 8, 2, 256, 512),
+          (300, 16, 1, 256, 0), (200, 6, 2, 512, 100)]
 
 
 @pytest.mark.parametrize("schedule", SCHEDULES)
@@ -121,3 +124,20 @@ def test_large_logits(cuda):
         p = np.exp(s - s.max(axis=1, keepdims=True))
         want = (p / p.sum(axis=1, keepdims=True)) @ vn[0]
         assert max_rel(o[hh].float().cpu().numpy(), want) <= MAX_REL
+
+
+@pytest.mark.parametrize("t,h,kv,window", [(3658, 8, 1, 512), (77, 8, 1, 512), (1000, 4, 1, 0), (300, 16, 1, 64),
+                                           (500, 8, 2, 512)])
+def test_attention_quant_fused(cuda, t, h, kv, window):
+    """Attention with k_attn_out fused gives the bits of the two-step path (the fused kernel
+    for one KV head; the two-step fallback for (8, 2))."""
+    d = 256
+    gen = torch.Generator(device=cuda).manual_seed(t + h + window)
+    sc = d ** -0.25
+    q = (torch.randn((h, t, d), device=cuda, generator=gen) * sc).to(torch.bfloat16)
+    k = (torch.randn((kv, t, d), device=cuda, generator=gen) * sc).to(torch.bfloat16)
+    v = torch.randn((kv, t, d), device=cuda, generator=gen).to(torch.bfloat16)
+    xq, xs = w8.attention_quant(q, k, v, window)
+    wq, ws = w8.attn_out_quant(w8.attention_prefill(q, k, v, window))
+    assert torch.equal(xq, wq) and torch.equal(xs, ws)
+    assert w8.device_status() == 0
