@@ -357,7 +357,7 @@ def sharded_head(w8, dev, stream, world, steps, warmup, pk):
 
 
 def fused_gelu_up(w8, work, dev, stream, steps, warmup, world):
-    """SURVEY next row 1: the gate/up GEMM with the k_gelu glue (pipeline.py:102-107)
+    """Fused epilogue chain: the gate/up GEMM with the k_gelu glue (pipeline.py:102-107)
     fused into its epilogue, against the same work unfused on the GPU (int32 GEMM, then
     dequant, gelu(gate) * up and quant as separate kernels), 35 layers each."""
     name, n, k = LAYER_SHAPES[2]
@@ -413,7 +413,7 @@ def _torch_rope(x, cos, sin):
 
 
 def fused_layer(w8, dev, stream, m, steps, warmup, world, layers=35):
-    """SURVEY next row 1 across a whole decoder layer: the linear set with all of its glue
+    """The fused epilogue chain across a whole decoder layer: the linear set with all of its glue
     on the GPU (k_in, qkv + k_qkv, k_attn_out, o + k_post_attn, gate_up + k_gelu,
     down + k_post_ff; pipeline.py:66-114), attention excluded (a synthetic o of the right
     shape stands in).  Fused: dequant / gelu in the GEMM epilogues plus warp-per-row glue
@@ -557,7 +557,7 @@ def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35):
 
 
 def attention_bench(w8, dev, stream, m, steps, warmup, world):
-    """SURVEY next row 4: prefill attention of one prompt on the GPU (pipeline.py:139-180),
+    """GPU attention: prefill attention of one prompt on the GPU (pipeline.py:139-180),
     Gemma E2B layer types: sliding window 512 with head_dim 256 (28 of 35 layers) and full
     causal with head_dim 512 (7 layers), 8 query heads on 1 KV head.  TFLOP/s counts the
     useful products (keys each query may see), 4 * H * D per (query, key)."""
@@ -611,7 +611,7 @@ def sweep(w8, dev, stream, steps, warmup):
             row[name] = res
         out[str(m)] = row
         del work
-    # The real E2B shape mix (SURVEY next row 2) at M = 3658, 8 distinct weights per shape.
+    # The real E2B shape mix at M = 3658, 8 distinct weights per shape.
     e2b = {"gate_up_x2 24576x1536": (24576, 1536), "down_x2 1536x12288": (1536, 12288),
            "qkv_global 5120x1536": (5120, 1536), "o_global 1536x4096": (1536, 4096),
            "q_only 2048x1536": (2048, 1536), "ple_gate 256x1536": (256, 1536), "ple_proj 1536x256": (1536, 256)}

@@ -76,7 +76,7 @@ BIG = [(512, 12288, 1536), (3658, 2560, 1536), (3658, 1536, 2048), (3658, 12288,
        (3658, 1536, 6144), (3658, 8960, 1536), (207, 1536, 6144), (858, 2560, 1536), (1878, 12288, 1536)]
 
 
-# The real E2B shape mix (SURVEY next row 2): the double-wide MLP of KV-shared layers
+# The real E2B shape mix: the double-wide MLP of KV-shared layers
 # (gate/up N = 24576, down K = 12288), full-attention layers with head_dim 512 (qkv
 # N = (8 + 2) * 512, o K = 8 * 512), q-only qkv of KV-shared layers (N = 8 * 256), and the
 # per-layer-input gate / projection (1536 -> 256, 256 -> 1536).
