@@ -496,12 +496,14 @@ def fused_layer(w8, dev, stream, m, steps, warmup, world, layers=35):
 
 
 def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35):
-    """One prompt through every decoder layer's linear set, glue and attention on the GPU:
-    k_in, qkv GEMM + k_qkv, attention, k_attn_out, o GEMM + k_post_attn, gate/up GEMM +
-    k_gelu, down GEMM + k_post_ff.  Gemma E2B attention layout: every 5th layer full causal
-    with head_dim 512 (qkv 5120 x 1536, o 1536 x 4096), the others sliding window 512 with
-    head_dim 256; 8 query heads on 1 KV head; no KV sharing and no per-layer-input (PLE)
-    branch.  Random weights; the residual stream is carried from layer to layer."""
+    """One prompt through every decoder layer's linear set, glue and attention on the GPU,
+    the layer body of pipeline.py:262-310: k_in, qkv GEMM + k_qkv, attention, k_attn_out,
+    o GEMM + k_post_attn, gate/up GEMM + k_gelu, down GEMM + k_post_ff, PLE gate GEMM
+    (1536 -> 256) + k_ple_gate, PLE projection GEMM (256 -> 1536) + k_ple_out.  Gemma E2B
+    attention layout: every 5th layer full causal with head_dim 512 (qkv 5120 x 1536, o
+    1536 x 4096), the others sliding window 512 with head_dim 256; 8 query heads on 1 KV
+    head; no KV sharing.  Random weights and per-layer inputs; the residual stream is
+    carried from layer to layer, and k_ple_out shares its row pass with the next k_in."""
     eps, nh, kv, hid = 1e-6, 8, 1, 1536
     g = torch.Generator(device=dev).manual_seed(91)
 
@@ -522,7 +524,9 @@ def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35):
         d, win = (512, 0) if i % 5 == 4 else (256, 512)
         L.append(dict(d=d, win=win, qkv=wq((nh + 2 * kv) * d, hid), o=wq(hid, nh * d),
                       gup=w8.pack_gelu_up(*wq(12288, hid)), dn=wq(hid, 6144), w_in=nw(hid), qn=nw(d), kn=nw(d),
-                      w_post=nw(hid), w_pre=nw(hid), w_pff=nw(hid)))
+                      w_post=nw(hid), w_pre=nw(hid), w_pff=nw(hid), pg=wq(256, hid), pp=wq(hid, 256),
+                      w_ple=nw(hid), scalar=float((0.5 + torch.rand((1,), device=dev, generator=g)).to(torch.bfloat16))))
+    ple = torch.randn((m, layers, 256), device=dev, generator=g).to(torch.bfloat16)  # per-layer inputs
     h0 = torch.randn((m, hid), device=dev, generator=g).to(torch.bfloat16)
     h = torch.empty_like(h0)
 
@@ -538,19 +542,26 @@ def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35):
             _, xq, sx = w8.post_norm_quant(y, h, l["w_post"], l["w_pre"], eps, h=h)
             xq, sx = w8.gelu_up_quant(xq, sx, *l["gup"])
             y = w8.gemm_dequant(xq, l["dn"][0], sx, l["dn"][1])
-            # k_post_ff and the next layer's k_in in one row pass (no PLE branch between them)
+            _, xq, sx = w8.post_norm_quant(y, h, l["w_pff"], None, eps, h=h)  # k_post_ff
+            y = w8.gemm_dequant(xq, l["pg"][0], sx, l["pg"][1])
+            xq, sx = w8.ple_gate_quant(y, ple[:, i])
+            y = w8.gemm_dequant(xq, l["pp"][0], sx, l["pp"][1])
+            # k_ple_out and the next layer's k_in in one row pass
             nxt = L[i + 1]["w_in"] if i + 1 < len(L) else None
-            _, xq, sx = w8.post_norm_quant(y, h, l["w_pff"], nxt, eps, h=h)
+            r = w8.ple_out(y, h, l["w_ple"], l["scalar"], eps, w_next=nxt, h=h)
+            if nxt is not None:
+                _, xq, sx = r
 
     gr = capture(step, stream)
     ms = timed(lambda: gr.replay(), steps, warmup, stream, world) / steps
     del gr
     assert torch.isfinite(h.float()).all()
-    linear_ops = sum(2 * m * (l["qkv"][0].numel() + l["o"][0].numel() + l["gup"][0].numel() + l["dn"][0].numel())
-                     for l in L)
+    linear_ops = sum(2 * m * (l["qkv"][0].numel() + l["o"][0].numel() + l["gup"][0].numel() + l["dn"][0].numel()
+                              + l["pg"][0].numel() + l["pp"][0].numel()) for l in L)
     return {"workload": f"{layers} decoder layers of one {m}-token prompt on the GPU (linear set + glue + attention; "
                         "every 5th layer full attention with head_dim 512, others sliding window 512 / head_dim 256; "
-                        "no KV sharing, no PLE branch, so k_post_ff and the next layer's k_in share one row pass)",
+                        "PLE branch per layer (gate 1536->256 + k_ple_gate, projection 256->1536 + k_ple_out); "
+                        "no KV sharing)",
             "ms_per_prefill": ms, "linear_tops": linear_ops / (ms * 1e-3) / 1e12,
             "reference": "the reference keeps its NPU busy 2.38 s per 3658-token prefill (README.md:61-62), its CPU "
                          "attention on top"}

@@ -24,14 +24,15 @@ for _m in (_lib, build, kernels, gemm, lm_head):
 
 from .kernels import (  # noqa: E402,F401
     BLOCK_K, BLOCK_M, BLOCK_N, attention_prefill, attention_quant, attn_out_quant, dequant, gelu_up_quant, gemm_dequant, int8_linear,
-    lm_head_logits, mm_i8, mm_i8_nk, pack_gelu_up, post_norm_quant, qkv_norm_rope, quant_rows, rms_quant,
-    use_device)
+    lm_head_logits, mm_i8, mm_i8_nk, pack_gelu_up, ple_gate_quant, ple_out, post_norm_quant, qkv_norm_rope,
+    quant_rows, rms_quant, use_device)
 from .gemm import (  # noqa: E402,F401
     BACKENDS, B200Gemm, Int8Head, NPUGemm, Slice, add_backend_argument, apply_backend, to_b200)
 from .lm_head import ShardedInt8Head  # noqa: E402,F401
 from ._lib import W8Error, device_status  # noqa: E402,F401
 
 __all__ = ["mm_i8", "mm_i8_nk", "gemm_dequant", "gelu_up_quant", "pack_gelu_up", "rms_quant", "post_norm_quant",
+           "ple_gate_quant", "ple_out",
            "attn_out_quant", "attention_prefill", "attention_quant", "qkv_norm_rope", "quant_rows", "dequant",
            "int8_linear",
            "lm_head_logits", "use_device", "B200Gemm", "NPUGemm", "Slice", "Int8Head", "to_b200",

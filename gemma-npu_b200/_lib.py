@@ -80,6 +80,9 @@ SIGNATURES = {
     "w8_rms_quant_bf16": (_i, [_p, _i64, _p, ctypes.c_float, _p, _i64, _p, _i64, _i64, _p]),
     "w8_post_norm_quant_bf16": (_i, [_p, _i64, _p, _i64, _p, _p, ctypes.c_float, _p, _i64, _p, _i64, _p, _i64,
                                      _i64, _p]),
+    "w8_ple_gate_quant_bf16": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _i64, _p]),
+    "w8_ple_out_bf16": (_i, [_p, _i64, _p, _i64, _p, ctypes.c_float, _p, ctypes.c_float, _p, _i64, _p, _i64, _p,
+                             _i64, _i64, _p]),
     "w8_qkv_norm_rope_bf16": (_i, [_p, _i64, _p, _p, _i64, _p, _p, ctypes.c_float, _p, _i64, _i64, _i64, _i64,
                                    _i64, _i64, _i, _p]),
     "w8_attention_prefill_bf16": (_i, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64,

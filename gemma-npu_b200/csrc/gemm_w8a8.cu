@@ -230,32 +230,6 @@ __device__ __forceinline__ void dequant_pack(const GemmArgs& a, int col0, const 
   }
 }
 
-constexpr float kGeluBeta = 0.7978845608028654f;  // sqrt(2 / pi)
-constexpr float kGeluKappa = 0.044715f;
-
-__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
-
-// 1 + tanh(z) = 2 / (1 + e^(-2z)), from one ex2.approx and one rcp.approx (relative error
-// a few 2^-23).  Like 1 + tanhf(z) in fp32 it is exactly 2 for large z and exactly 0 for
-// very negative z (e^(-2z) overflows to +inf, whose reciprocal is 0).
-__device__ __forceinline__ float one_plus_tanh(float z) {
-  float e, r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(__fmul_rn(z, -2.8853900817779268f)));  // -2 log2(e)
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fadd_rn(1.f, e)));
-  return 2.f * r;
-}
-
-// bf16 of F.gelu(g, approximate="tanh") for a bf16 value g: ATen's fp32 operation order
-// 0.5 * g * (1 + tanh(sqrt(2/pi) * (g + 0.044715 * g^3))) with every product and sum
-// rounded (no FMA contraction), rounded once to bf16 at the end.  Only 1 + tanh comes
-// from the approximation above, so the result is the reference's except for a bf16
-// rounding flip about once in 10^4 values.
-__device__ __forceinline__ float gelu_tanh_bf16(float g) {
-  const float g3 = __fmul_rn(__fmul_rn(g, g), g);
-  const float inner = __fmul_rn(kGeluBeta, __fadd_rn(g, __fmul_rn(kGeluKappa, g3)));
-  return round_bf16(__fmul_rn(__fmul_rn(0.5f, g), one_plus_tanh(inner)));
-}
-
 // 32 gate accumulators (GEMM columns gcol0..) and the 32 up accumulators 128 columns to
 // their right -> 16 words of packed bf16 a = bf16(gelu(_deq(gate)) * _deq(up)); `amax`
 // accumulates max |a|.

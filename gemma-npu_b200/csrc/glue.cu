@@ -7,6 +7,9 @@
 //   k_post_attn h = bf16(res + bf16(_rms(y, w1)));  q, s = _quant(bf16(_rms(h, w2)))  (:95-99)
 //   k_post_ff   h = bf16(res + bf16(_rms(y, w1)));  q, s = _quant(h)           (:110-114)
 //   k_attn_out  q, s = _quant(o.transpose(0, 1).reshape(T, H * D))            (:88-92)
+//   k_ple_gate  q, s = _quant(bf16(bf16(gelu_tanh(y)) * ple))                  (:117-121)
+//   k_ple_out   h = bf16(bf16(h + bf16(_rms(y, w1))) * scalar)                  (:124-127)
+//               [+ the next layer's k_in: q, s = _quant(bf16(_rms(h, w2)))]
 //
 // _rms (pipeline.py:43-46) in fp32: x * pow(mean(x^2) + eps, -0.5), then * w; mean is the
 // fp32 sum / N and pow(., -0.5) a correctly rounded reciprocal square root.  The sum is a
@@ -24,21 +27,22 @@ constexpr int kGlueWarps = 8;
 constexpr int kGlueMaxVecs = 8;  // 16-byte vectors per lane: N <= 32 * 8 * 8 = 2048
 constexpr int kGlueMaxVecsAttn = 16;  // k_attn_out rows: H * D <= 4096 (head_dim 512 layers)
 
-enum GlueMode : int { kGlueIn = 0, kGluePost1 = 1, kGluePost2 = 2, kGlueAttnOut = 3 };
+enum GlueMode : int { kGlueIn = 0, kGluePost1 = 1, kGluePost2 = 2, kGlueAttnOut = 3, kGluePleGate = 4 };
 
 struct GlueArgs {
   const __nv_bfloat16* x;  // k_in: h; post: y = _deq(acc); attn_out: o [H, T, D]
   int64_t ldx;             // row (token) pitch of x in elements
   int64_t ld_head;         // attn_out: pitch between heads of o, in elements
   int head_dim;            // attn_out: D
-  const __nv_bfloat16* res;
+  const __nv_bfloat16* res;  // post: the residual stream; PLE gate: this layer's per-layer input
   int64_t ldr;
   const __nv_bfloat16* w1;
   const __nv_bfloat16* w2;
   float eps;
+  float scalar;            // post: the layer scalar applied to h (1: none)
   __nv_bfloat16* h;        // post: the new residual stream
   int64_t ldh;
-  int8_t* q;
+  int8_t* q;               // Post1: may be null (no quant of h)
   int64_t ldq;
   float* s;
   int t, n;
@@ -114,7 +118,20 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
       }
     }
   }
-  if constexpr (MODE != kGlueAttnOut) {
+  if constexpr (MODE == kGluePleGate) {
+#pragma unroll
+    for (int i = 0; i < kMax; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nv) {
+        float x[8], p[8];
+        unpack8(v[i], x);
+        unpack8(ld16(a.res + static_cast<int64_t>(row) * a.ldr + vi * 8), p);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = rbf16(__fmul_rn(gelu_tanh_bf16(x[e]), p[e]));
+        v[i] = pack8(x);
+      }
+    }
+  } else if constexpr (MODE != kGlueAttnOut) {
     uint4 res[MODE == kGlueIn ? 1 : NV];
     if constexpr (MODE != kGlueIn) {
 #pragma unroll
@@ -135,6 +152,7 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
         for (int e = 0; e < 8; ++e) {
           const float t = rbf16(__fmul_rn(__fmul_rn(x[e], r1), w[e]));
           x[e] = MODE == kGlueIn ? t : rbf16(__fadd_rn(rr[e], t));
+          if (MODE != kGlueIn && a.scalar != 1.f) x[e] = rbf16(__fmul_rn(x[e], a.scalar));
         }
         v[i] = pack8(x);
         if constexpr (MODE != kGlueIn)
@@ -157,6 +175,7 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
       }
     }
   }
+  if (MODE == kGluePost1 && a.q == nullptr) return;  // k_ple_out alone: h only
   // _quant of the row.
   float amax = 0.f;
 #pragma unroll
@@ -192,10 +211,10 @@ __global__ void __launch_bounds__(32 * kGlueWarps, NV <= 6 ? 4 : 3) glue_rows_ke
   pdl_launch_dependents();
   // The norm weights are the same for every row: staged once per CTA in shared memory,
   // before waiting for the previous kernel of the stream (they do not depend on it).
-  __shared__ uint4 w1s[MODE == kGlueAttnOut ? 1 : 32 * NV];
+  __shared__ uint4 w1s[(MODE == kGlueAttnOut || MODE == kGluePleGate) ? 1 : 32 * NV];
   __shared__ uint4 w2s[MODE == kGluePost2 ? 32 * NV : 1];
   const int nv = a.n / 8;
-  if constexpr (MODE != kGlueAttnOut) {
+  if constexpr (MODE != kGlueAttnOut && MODE != kGluePleGate) {
     for (int i = threadIdx.x; i < nv; i += blockDim.x) {
       w1s[i] = ld16(a.w1 + i * 8);
       if constexpr (MODE == kGluePost2) w2s[i] = ld16(a.w2 + i * 8);
@@ -355,10 +374,16 @@ static int glue_launch(int mode, const w8::GlueArgs& a, cudaStream_t stream) {
   const int max_n = 32 * 8 * (mode == w8::kGlueAttnOut ? w8::kGlueMaxVecsAttn : w8::kGlueMaxVecs);
   W8_CHECK_ARG(a.n > 0 && a.n % 8 == 0 && a.n <= max_n, "row length %d must be a multiple of 8 and at most %d", a.n,
                max_n);
-  W8_CHECK_ARG(a.x != nullptr && a.q != nullptr && a.s != nullptr, "null pointer");
+  const bool no_quant = mode == w8::kGluePost1 && a.q == nullptr && a.s == nullptr;
+  W8_CHECK_ARG(a.x != nullptr && (no_quant || (a.q != nullptr && a.s != nullptr)), "null pointer");
   W8_CHECK_ALIGN(aligned(a.x, 16) && a.ldx % 8 == 0, "x must be 16-byte aligned with a pitch %% 8 == 0");
-  W8_CHECK_ALIGN(aligned(a.q, 8) && a.ldq % 8 == 0 && a.ldq >= a.n, "q must be 8-byte aligned, ldq %% 8 == 0, ldq >= n");
-  if (mode != w8::kGlueAttnOut) {
+  W8_CHECK_ALIGN(no_quant || (aligned(a.q, 8) && a.ldq % 8 == 0 && a.ldq >= a.n),
+                 "q must be 8-byte aligned, ldq %% 8 == 0, ldq >= n");
+  if (mode == w8::kGluePleGate) {
+    W8_CHECK_ARG(a.res != nullptr, "null per-layer input");
+    W8_CHECK_ALIGN(aligned(a.res, 16) && a.ldr % 8 == 0, "per-layer input rows must be 16-byte aligned, pitch %% 8 == 0");
+    W8_CHECK_ARG(a.ldr >= a.n && a.ldx >= a.n, "row pitch smaller than n");
+  } else if (mode != w8::kGlueAttnOut) {
     W8_CHECK_ARG(a.w1 != nullptr, "null norm weight");
     W8_CHECK_ALIGN(aligned(a.w1, 16), "norm weights must be 16-byte aligned");
     W8_CHECK_ARG(a.ldx >= a.n, "row pitch smaller than n");
@@ -392,6 +417,9 @@ static int glue_launch(int mode, const w8::GlueArgs& a, cudaStream_t stream) {
     case w8::kGluePost2:
       return a.n <= 1536 ? glue_go(w8::glue_rows_kernel<w8::kGluePost2, 6>, a, stream)
                          : glue_go(w8::glue_rows_kernel<w8::kGluePost2, w8::kGlueMaxVecs>, a, stream);
+    case w8::kGluePleGate:
+      return a.n <= 1536 ? glue_go(w8::glue_rows_kernel<w8::kGluePleGate, 6>, a, stream)
+                         : glue_go(w8::glue_rows_kernel<w8::kGluePleGate, w8::kGlueMaxVecs>, a, stream);
     default:
       return a.n <= 32 * 8 * w8::kGlueMaxVecs
                  ? glue_go(w8::glue_rows_kernel<w8::kGlueAttnOut, w8::kGlueMaxVecs>, a, stream)
@@ -403,6 +431,7 @@ static w8::GlueArgs glue_args(int64_t t, int64_t n) {
   w8::GlueArgs a = {};
   a.t = static_cast<int>(t);
   a.n = static_cast<int>(n);
+  a.scalar = 1.f;
   return a;
 }
 
@@ -441,6 +470,45 @@ extern "C" int w8_post_norm_quant_bf16(const uint16_t* y, int64_t ldy, const uin
   a.ldq = ldq;
   a.s = s;
   return w8host::glue_launch(w2 != nullptr ? w8::kGluePost2 : w8::kGluePost1, a,
+                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int w8_ple_gate_quant_bf16(const uint16_t* y, int64_t ldy, const uint16_t* ple, int64_t ldp, int8_t* q,
+                                      int64_t ldq, float* s, int64_t t, int64_t n, w8_stream_t stream) {
+  W8_CHECK_ARG(t >= 0 && n >= 0 && t < (1ll << 31) && n < (1ll << 31), "bad size");
+  w8::GlueArgs a = w8host::glue_args(t, n);
+  a.x = reinterpret_cast<const __nv_bfloat16*>(y);
+  a.ldx = ldy;
+  a.res = reinterpret_cast<const __nv_bfloat16*>(ple);
+  a.ldr = ldp;
+  a.q = q;
+  a.ldq = ldq;
+  a.s = s;
+  return w8host::glue_launch(w8::kGluePleGate, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int w8_ple_out_bf16(const uint16_t* y, int64_t ldy, const uint16_t* res, int64_t ldr,
+                               const uint16_t* w_post, float scalar, const uint16_t* w_next, float eps, uint16_t* h,
+                               int64_t ldh, int8_t* q, int64_t ldq, float* s, int64_t t, int64_t n,
+                               w8_stream_t stream) {
+  W8_CHECK_ARG(t >= 0 && n >= 0 && t < (1ll << 31) && n < (1ll << 31), "bad size");
+  W8_CHECK_ARG(w_next != nullptr || (q == nullptr && s == nullptr),
+               "q / s are written only with the next layer's norm weight");
+  w8::GlueArgs a = w8host::glue_args(t, n);
+  a.x = reinterpret_cast<const __nv_bfloat16*>(y);
+  a.ldx = ldy;
+  a.res = reinterpret_cast<const __nv_bfloat16*>(res);
+  a.ldr = ldr;
+  a.w1 = reinterpret_cast<const __nv_bfloat16*>(w_post);
+  a.w2 = reinterpret_cast<const __nv_bfloat16*>(w_next);
+  a.eps = eps;
+  a.scalar = scalar;
+  a.h = reinterpret_cast<__nv_bfloat16*>(h);
+  a.ldh = ldh;
+  a.q = q;
+  a.ldq = ldq;
+  a.s = s;
+  return w8host::glue_launch(w_next != nullptr ? w8::kGluePost2 : w8::kGluePost1, a,
                              reinterpret_cast<cudaStream_t>(stream));
 }
 

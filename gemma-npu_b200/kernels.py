@@ -268,6 +268,52 @@ def post_norm_quant(y, res, w1, w2, eps, h=None, q=None, s=None):
     return h, q, s
 
 
+def ple_gate_quant(y, ple, q=None, s=None):
+    """k_ple_gate (pipeline.py:117-121) on y = the PLE gate GEMM's dequantised bf16 output
+    [T, n] and this layer's per-layer input `ple` [T, n] (bf16, any row pitch, e.g. a
+    [:, layer] slice of the [T, layers, n] per-layer inputs):
+    q, s = _quant(bf16(bf16(gelu_tanh(y)) * ple)).  Returns (q, s)."""
+    _bf16_rows(y, "y")
+    T, N = y.shape
+    _bf16_rows(ple, "ple", N)
+    _need(ple.shape[0] == T, "ple must have the rows of y")
+    q = torch.empty((T, N), dtype=torch.int8, device=y.device) if q is None else q
+    s = torch.empty((T,), dtype=torch.float32, device=y.device) if s is None else s
+    _check_matrix(q, "q", torch.int8)
+    _check_vector(s, "s", torch.float32, T)
+    _lib.call("w8_ple_gate_quant_bf16", y.data_ptr(), _ld(y), ple.data_ptr(), _ld(ple), q.data_ptr(), _ld(q),
+              s.data_ptr(), T, N, _stream(y))
+    return q, s
+
+
+def ple_out(y, res, w_post, scalar, eps, w_next=None, h=None, q=None, s=None):
+    """k_ple_out (pipeline.py:124-127) on y = the PLE projection GEMM's dequantised bf16
+    output: h = bf16(bf16(res + bf16(_rms(y, w_post))) * scalar), `scalar` the layer's bf16
+    layer_scalar (a 1-element tensor or a float; pass a float inside a CUDA graph capture,
+    where reading a device tensor is not allowed).  Returns h; with `w_next` (the next
+    layer's input norm weight) the next layer's k_in runs in the same pass and
+    (h, q, s) is returned, q, s = _quant(bf16(_rms(h, w_next))).  `h` may be `res`."""
+    _bf16_rows(y, "y")
+    T, N = y.shape
+    _bf16_rows(res, "res", N)
+    _need(res.shape[0] == T, "res must have the rows of y")
+    _bf16_vec(w_post, "w_post", N)
+    h = torch.empty((T, N), dtype=torch.bfloat16, device=y.device) if h is None else h
+    _bf16_rows(h, "h", N)
+    qp = sp = None
+    if w_next is not None:
+        _bf16_vec(w_next, "w_next", N)
+        q = torch.empty((T, N), dtype=torch.int8, device=y.device) if q is None else q
+        s = torch.empty((T,), dtype=torch.float32, device=y.device) if s is None else s
+        _check_matrix(q, "q", torch.int8)
+        _check_vector(s, "s", torch.float32, T)
+        qp, sp = q.data_ptr(), s.data_ptr()
+    _lib.call("w8_ple_out_bf16", y.data_ptr(), _ld(y), res.data_ptr(), _ld(res), w_post.data_ptr(),
+              float(scalar), None if w_next is None else w_next.data_ptr(), float(eps), h.data_ptr(), _ld(h), qp,
+              _ld(q) if q is not None else 0, sp, T, N, _stream(y))
+    return h if w_next is None else (h, q, s)
+
+
 def qkv_norm_rope(y, cos, sin, qw, kw, eps, heads, kv_heads, head_dim, shared=False, out=None):
     """k_qkv (pipeline.py:72-86) on y = the qkv GEMM's dequantised bf16 output [T, (H+2KV)*D]
     (or [T, H*D] when shared): returns (q [H, T, D], k [KV, T, D], v [KV, T, D]) bf16, slices of

@@ -25,6 +25,8 @@
  *   w8_rms_quant_bf16       pipeline.py:66-69 (k_in)
  *   w8_post_norm_quant_bf16 pipeline.py:95-99 (k_post_attn), :110-114 (k_post_ff)
  *   w8_attn_out_quant_bf16  pipeline.py:88-92 (k_attn_out)
+ *   w8_ple_gate_quant_bf16  pipeline.py:117-121 (k_ple_gate)
+ *   w8_ple_out_bf16         pipeline.py:124-127 (k_ple_out) [+ :66-69, the next layer's k_in]
  *   w8_qkv_norm_rope_bf16   pipeline.py:72-86 (k_qkv)
  *   w8_attention_prefill_bf16 pipeline.py:139-180 (full_attention / sliding_attention)
  *   w8_attention_prefill_quant the same followed by pipeline.py:88-92 (k_attn_out)
@@ -153,6 +155,24 @@ int w8_post_norm_quant_bf16(const uint16_t* y, int64_t ldy, const uint16_t* res,
                             const uint16_t* w1, const uint16_t* w2, float eps, uint16_t* h,
                             int64_t ldh, int8_t* q, int64_t ldq, float* s, int64_t t, int64_t n,
                             w8_stream_t stream);
+
+/* k_ple_gate (pipeline.py:117-121) after the PLE gate GEMM with the dequant fused
+ * (y = _deq(acc), bf16 [T, n]) and this layer's per-layer input ple (bf16 [T, n], row pitch
+ * ldp): q, s = _quant(bf16(bf16(gelu_tanh(y)) * ple)), q [T, n] int8, s [T] fp32.
+ * n % 8 == 0, n <= 2048.  gelu's 1 + tanh comes from exp2 / reciprocal approximations
+ * (relative error a few 2^-23): a bf16 value may move by one step, an int8 code by one. */
+int w8_ple_gate_quant_bf16(const uint16_t* y, int64_t ldy, const uint16_t* ple, int64_t ldp, int8_t* q,
+                           int64_t ldq, float* s, int64_t t, int64_t n, w8_stream_t stream);
+
+/* k_ple_out (pipeline.py:124-127) after the PLE projection GEMM with the dequant fused
+ * (y = _deq(acc), bf16 [T, n]): h = bf16(bf16(res + bf16(_rms(y, w_post))) * scalar), scalar
+ * the layer's bf16 layer_scalar as a float.  With w_next != NULL the next layer's k_in
+ * (pipeline.py:66-69) follows in the same row pass: q, s = _quant(bf16(_rms(h, w_next)));
+ * with w_next == NULL, q and s must be NULL.  h may alias res.  Same tolerance as
+ * w8_post_norm_quant_bf16. */
+int w8_ple_out_bf16(const uint16_t* y, int64_t ldy, const uint16_t* res, int64_t ldr, const uint16_t* w_post,
+                    float scalar, const uint16_t* w_next, float eps, uint16_t* h, int64_t ldh, int8_t* q,
+                    int64_t ldq, float* s, int64_t t, int64_t n, w8_stream_t stream);
 
 /* k_attn_out (pipeline.py:88-92): the attention output o [H, T, D] (bf16; element
  * (h, t, d) at o[h * ld_head + t * ld_tok + d]) quantised per token over its H * D

@@ -148,6 +148,20 @@ def k_post(y, res, w1, w2, eps):
     return h, q, s
 
 
+def k_ple_gate(y, ple):
+    """k_ple_gate (pipeline.py:117-121) after the dequant, y = _deq(acc) as bf16 values:
+    g = bf16(bf16(gelu_tanh(y)) * ple); returns _quant(g)."""
+    g = bf16_round(gelu_tanh_bf16(y) * np.asarray(ple, np.float32))
+    return quant_rows(g)
+
+
+def k_ple_out(y, h, w, scalar, eps):
+    """k_ple_out (pipeline.py:124-127) after the dequant: bf16(bf16(h + bf16(_rms(y, w))) * scalar),
+    `scalar` the bf16 layer scalar as a float."""
+    hh = bf16_round(np.asarray(h, np.float32) + bf16_round(rms(y, w, eps)))
+    return bf16_round(hh * np.float32(scalar))
+
+
 def k_attn_out(o):
     """k_attn_out (pipeline.py:88-92): o [H, T, D] -> _quant of the [T, H*D] rows."""
     o = np.asarray(o, np.float32)

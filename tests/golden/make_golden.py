@@ -15,6 +15,8 @@ repository) and records, on seeded inputs:
   gelu_up   pipeline.k_gelu (pipeline.py:102-107): dequant, gelu_tanh(gate) * up, int8 quant
   k_in, k_post_attn, k_post_ff, k_attn_out, k_qkv(_shared)
             the RMSNorm / residual / RoPE glue of pipeline.py:66-99, 110-114 (eager bodies)
+  k_ple_gate, k_ple_out(_one)
+            the per-layer-input glue of pipeline.py:117-127 (eager bodies)
   attn_sliding, attn_full
             pipeline.sliding_attention / full_attention (pipeline.py:139-180), q_start = 0
 
@@ -180,6 +182,26 @@ def main(ref_dir):
         aq, ak = (aq.float() * scale).to(torch.bfloat16), (ak.float() * scale).to(torch.bfloat16)
         ao = pipeline.sliding_attention(aq, ak, av, 0, win) if win else pipeline.full_attention(aq, ak, av, 0)
         out[name] = dict(q=bf16_bits(aq), k=bf16_bits(ak), v=bf16_bits(av), window=np.int32(win), o=bf16_bits(ao))
+
+    # ---- the per-layer-input glue (pipeline.py:117-127, k_ple_gate / k_ple_out), eager bodies:
+    # the PLE gate GEMM output [T, 256] with this layer's per-layer input, and the projection
+    # output [T, hidden] added into the residual stream and scaled by the layer scalar
+    pn = 256
+    acc, sxa, swa = gemm_out(nt, pn, k=nn)
+    ple = torch.randn(nt, pn).to(torch.bfloat16)
+    ple[0] = 0                                            # gated-off row: the 1e-8 scale floor
+    q_, s_ = eager(pipeline.k_ple_gate)(acc, sxa, swa, ple)
+    out["k_ple_gate"] = dict(acc=acc.numpy(), sx=sxa.numpy(), sw=swa.numpy(), ple=bf16_bits(ple), q=q_.numpy(),
+                             s=s_.numpy())
+    acc, sxa, swa = gemm_out(nt, nn, k=pn)
+    res = torch.randn(nt, nn).to(torch.bfloat16)
+    w1 = norm_w(nn)
+    for tag, val in (("", 0.3), ("_one", 1.0)):
+        scalar = torch.tensor([val]).to(torch.bfloat16)
+        h_ = eager(pipeline.k_ple_out)(acc, sxa, swa, res, w1, scalar, eps)
+        out[f"k_ple_out{tag}"] = dict(acc=acc.numpy(), sx=sxa.numpy(), sw=swa.numpy(), res=bf16_bits(res),
+                                      w1=bf16_bits(w1), scalar=bf16_bits(scalar), eps=np.float32(eps),
+                                      h=bf16_bits(h_))
 
     for name, arrays in out.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)

@@ -168,3 +168,74 @@ def test_qkv_gemm_then_norm_rope_matches_oracle(cuda, t, nh, kv, d, shared):
                            1e-6, nh, kv, d, shared)
     for mine, theirs in ((q, qr), (kk, kr), (v, vr)):
         close_bf16(bits(mine[:, rows]), ref.f32_to_bf16_bits(theirs), per_vector=True)
+
+
+# ---- the per-layer-input (PLE) branch: k_ple_gate / k_ple_out (pipeline.py:117-127).
+# gelu's 1 + tanh comes from exp2 / reciprocal approximations (relative error a few
+# 2^-23), so a gated value may move by one bf16 step and an int8 code by one.
+
+def test_golden_k_ple_gate(cuda, golden):
+    g = golden("k_ple_gate")
+    acc = torch.from_numpy(g["acc"]).to(cuda)
+    y = w8.dequant(acc, torch.from_numpy(g["sx"]).to(cuda), torch.from_numpy(g["sw"]).to(cuda))
+    q, s = w8.ple_gate_quant(y, bf16(g["ple"], cuda))
+    close_q(q.cpu().numpy(), g["q"])
+    np.testing.assert_allclose(s.cpu().numpy(), g["s"], rtol=2.0 ** -7)
+    assert s[0].item() == np.float32(1e-8) / np.float32(127)  # the gated-off row: the scale floor
+
+
+@pytest.mark.parametrize("name", ["k_ple_out", "k_ple_out_one"])
+def test_golden_k_ple_out(cuda, golden, name):
+    g = golden(name)
+    acc = torch.from_numpy(g["acc"]).to(cuda)
+    y = w8.dequant(acc, torch.from_numpy(g["sx"]).to(cuda), torch.from_numpy(g["sw"]).to(cuda))
+    scalar = bf16(g["scalar"], cuda)
+    h = w8.ple_out(y, bf16(g["res"], cuda), bf16(g["w1"], cuda), scalar, float(g["eps"]))
+    close_bf16(bits(h), g["h"], res=ref.bf16_bits_to_f32(g["res"]) * float(scalar.float().item()))
+
+
+@pytest.mark.parametrize("t", [3658, 300])
+def test_ple_branch_matches_oracle(cuda, t):
+    """The whole PLE branch of a layer on the GPU: gate GEMM (1536 -> 256, dequant fused),
+    k_ple_gate with a [:, layer] slice of the [T, layers, 256] per-layer inputs, projection
+    GEMM (256 -> 1536), k_ple_out in place on the residual stream fused with the next
+    layer's k_in.  Each stage is checked against the oracle on the GPU's own inputs."""
+    hid, pn, layers, layer = 1536, 256, 35, 17
+    gen = torch.Generator(device=cuda).manual_seed(t)
+    x, sx = w8.quant_rows(torch.randn((t, hid), device=cuda, generator=gen, dtype=torch.bfloat16))
+    wg, swg = w8.quant_rows(torch.randn((pn, hid), device=cuda, generator=gen, dtype=torch.bfloat16) * 0.02)
+    wp, swp = w8.quant_rows(torch.randn((hid, pn), device=cuda, generator=gen, dtype=torch.bfloat16) * 0.02)
+    ple_all = torch.randn((t, layers, pn), device=cuda, generator=gen).to(torch.bfloat16)
+    ple = ple_all[:, layer]
+    res = torch.randn((t, hid), device=cuda, generator=gen).to(torch.bfloat16)
+    w_post = (1 + 0.1 * torch.randn((hid,), device=cuda, generator=gen)).to(torch.bfloat16)
+    w_next = (1 + 0.1 * torch.randn((hid,), device=cuda, generator=gen)).to(torch.bfloat16)
+    scalar = torch.tensor([0.4], device=cuda).to(torch.bfloat16)
+
+    yg = w8.gemm_dequant(x, wg, sx, swg)
+    q1, s1 = w8.ple_gate_quant(yg, ple)
+    yp = w8.gemm_dequant(q1, wp, s1, swp)
+    res0 = res.clone()
+    h, q2, s2 = w8.ple_out(yp, res, w_post, scalar, 1e-6, w_next=w_next, h=res)
+    assert h.data_ptr() == res.data_ptr()
+
+    rows = _rows(t, 7)
+    yr = ref.bf16_bits_to_f32(ref.dequant(ref.int_mm(x[rows].cpu().numpy(), wg.t().cpu().numpy()),
+                                          sx[rows].cpu().numpy(), swg.cpu().numpy()))
+    np.testing.assert_array_equal(bits(yg[rows]), ref.f32_to_bf16_bits(yr))
+    qr1, sr1 = ref.k_ple_gate(yr, ple[rows].float().cpu().numpy())
+    close_q(q1[rows].cpu().numpy(), qr1)
+    np.testing.assert_allclose(s1[rows].cpu().numpy(), sr1, rtol=2.0 ** -7)
+
+    yr2 = ref.bf16_bits_to_f32(ref.dequant(ref.int_mm(q1[rows].cpu().numpy(), wp.t().cpu().numpy()),
+                                           s1[rows].cpu().numpy(), swp.cpu().numpy()))
+    sc = float(scalar.float().item())
+    hr = ref.k_ple_out(yr2, res0[rows].float().cpu().numpy(), w_post.float().cpu().numpy(), sc, 1e-6)
+    close_bf16(bits(h[rows]), ref.f32_to_bf16_bits(hr), res=res0[rows].float().cpu().numpy() * sc)
+    qr2, sr2 = ref.k_in(h[rows].float().cpu().numpy(), w_next.float().cpu().numpy(), 1e-6)
+    close_q(q2[rows].cpu().numpy(), qr2)
+    np.testing.assert_allclose(s2[rows].cpu().numpy(), sr2, rtol=2.0 ** -7)
+
+    # Without the next layer's weight: h only, the same values.
+    h2 = w8.ple_out(yp, res0, w_post, scalar, 1e-6)
+    assert torch.equal(h2, h)

@@ -144,6 +144,26 @@ def test_k_post_attn_and_ff(golden):
         np.testing.assert_allclose(s, g["s"], rtol=2.0 ** -7)
 
 
+def test_k_ple_gate_bit_exact(golden):
+    """k_ple_gate (pipeline.py:117-121): dequant, bf16(gelu_tanh(y)) * ple, int8 quant."""
+    g = golden("k_ple_gate")
+    y = ref.bf16_bits_to_f32(ref.dequant(g["acc"], g["sx"], g["sw"]))
+    q, s = ref.k_ple_gate(y, ref.bf16_bits_to_f32(g["ple"]))
+    np.testing.assert_array_equal(q, g["q"])
+    np.testing.assert_array_equal(s, g["s"])
+
+
+def test_k_ple_out(golden):
+    """k_ple_out (pipeline.py:124-127), with a layer scalar of 0.3 and of exactly 1."""
+    for name in ("k_ple_out", "k_ple_out_one"):
+        g = golden(name)
+        y = ref.bf16_bits_to_f32(ref.dequant(g["acc"], g["sx"], g["sw"]))
+        scalar = float(ref.bf16_bits_to_f32(g["scalar"])[0])
+        h = ref.k_ple_out(y, ref.bf16_bits_to_f32(g["res"]), ref.bf16_bits_to_f32(g["w1"]), scalar,
+                          float(g["eps"]))
+        _close_bf16(ref.f32_to_bf16_bits(h), g["h"])
+
+
 def test_k_attn_out_bit_exact(golden):
     g = golden("k_attn_out")
     q, s = ref.k_attn_out(ref.bf16_bits_to_f32(g["o"]))
