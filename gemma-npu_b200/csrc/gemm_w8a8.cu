@@ -1032,10 +1032,14 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   // needs K to be a multiple of 128.  Otherwise one CTA per 128 x 256 tile.
   const bool pair = m > w8::kBM && k % w8::kBK == 0;
   const int rows_per_tile = pair ? 2 * w8::kBM : w8::kBM;
-  // Tile width: on CTA pairs over a K-major B, 192 columns when that fills the last wave
-  // enough to pay for narrower tiles (measured: a 192-wide tile costs ~1.28x per column
-  // of a 256-wide one), e.g. N = 2560 (qkv) and N = 1536 (o) at M = 3658.  Shapes that
-  // stream-K will balance keep 256.
+  // Tile width on CTA pairs over a K-major B: the narrowest of 64, 128, 192 and 256
+  // columns that needs no more waves of workers than any other.  A narrower tile costs
+  // more per column (a 192-wide tile ~1.28x of a 256-wide one, a 64-wide one ~3x) but
+  // finishes sooner, so it pays only where it adds no wave: N = 2560 / 1536 at M = 3658
+  // take 192, while GEMMs with one wave of tiles or less (the 1536 -> 256 PLE gate, short
+  // prompts) take 64 or 128 and spread over more SMs (measured, bf16 out: PLE gate at
+  // M = 3658 11.2 -> 8.6 us, qkv at M = 207 10.1 -> 8.5 us, o at M = 858 11.4 -> 10.7 us).
+  // Shapes that stream-K will balance keep 256.
   int bn = w8::kBN;
   if (pair && b_layout == W8_B_NK && epi != w8::kEpiGeluUp &&
       !(epi == w8::kEpiI32 && workspace != nullptr && k >= 24 * w8::kBK)) {
@@ -1044,7 +1048,15 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
     if (st != W8_OK) return st;
     const int64_t m_tiles = (m + rows_per_tile - 1) / rows_per_tile;
     auto waves = [&](int64_t w) { return (m_tiles * ((n + w - 1) / w) + cap - 1) / cap; };
-    if (waves(192) * 192 * 128 < waves(256) * 256 * 100) bn = 192;
+    const int widths[4] = {256, 192, 128, 64};
+    int64_t best = waves(256);
+    for (int w : widths) {
+      const int64_t v = waves(w);
+      if (v <= best) {
+        best = v;
+        bn = w;
+      }
+    }
   }
   const uint32_t b_box_n = pair ? bn / 2 : w8::kBN;  // B columns one CTA stages per K-block
   CUtensorMap ta, tb, tc;
@@ -1099,13 +1111,23 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
     return pair ? launch_pair<false, w8::kEpiGeluUp, 256>(device, ta, tb, tc, args, flag_words, stream)
                 : launch_single<false, w8::kEpiGeluUp>(device, ta, tb, tc, args, flag_words, stream);
   if (pair) {
-    if (i32)
-      return mn ? launch_pair<true, w8::kEpiI32, 256>(device, ta, tb, tc, args, flag_words, stream)
-                : bn == 192 ? launch_pair<false, w8::kEpiI32, 192>(device, ta, tb, tc, args, flag_words, stream)
-                            : launch_pair<false, w8::kEpiI32, 256>(device, ta, tb, tc, args, flag_words, stream);
-    return mn ? launch_pair<true, w8::kEpiBf16, 256>(device, ta, tb, tc, args, flag_words, stream)
-              : bn == 192 ? launch_pair<false, w8::kEpiBf16, 192>(device, ta, tb, tc, args, flag_words, stream)
-                          : launch_pair<false, w8::kEpiBf16, 256>(device, ta, tb, tc, args, flag_words, stream);
+    if (mn)
+      return i32 ? launch_pair<true, w8::kEpiI32, 256>(device, ta, tb, tc, args, flag_words, stream)
+                 : launch_pair<true, w8::kEpiBf16, 256>(device, ta, tb, tc, args, flag_words, stream);
+    if (i32) {
+      switch (bn) {
+        case 64: return launch_pair<false, w8::kEpiI32, 64>(device, ta, tb, tc, args, flag_words, stream);
+        case 128: return launch_pair<false, w8::kEpiI32, 128>(device, ta, tb, tc, args, flag_words, stream);
+        case 192: return launch_pair<false, w8::kEpiI32, 192>(device, ta, tb, tc, args, flag_words, stream);
+        default: return launch_pair<false, w8::kEpiI32, 256>(device, ta, tb, tc, args, flag_words, stream);
+      }
+    }
+    switch (bn) {
+      case 64: return launch_pair<false, w8::kEpiBf16, 64>(device, ta, tb, tc, args, flag_words, stream);
+      case 128: return launch_pair<false, w8::kEpiBf16, 128>(device, ta, tb, tc, args, flag_words, stream);
+      case 192: return launch_pair<false, w8::kEpiBf16, 192>(device, ta, tb, tc, args, flag_words, stream);
+      default: return launch_pair<false, w8::kEpiBf16, 256>(device, ta, tb, tc, args, flag_words, stream);
+    }
   }
   if (i32)
     return mn ? launch_single<true, w8::kEpiI32>(device, ta, tb, tc, args, flag_words, stream)
