@@ -103,21 +103,25 @@ __global__ void __launch_bounds__(kGemvThreads)
 
   const int stride = gridDim.x * kTeams * R;
   const int first = (blockIdx.x * kTeams + team) * R;
-  uint4 wv[R][J];
-  auto load_w = [&](int n0) {
+  // One row per team per step (short matrices): the next step's weights are loaded while
+  // this step computes, so a CTA with several steps waits for one DRAM round trip, not
+  // one per step.  With R > 1 the doubled registers would cost residency instead.
+  constexpr bool kPrefetch = R == 1;
+  uint4 wv[R][J], wn[R][J];
+  auto load_w = [&](uint4 (&dst)[R][J], int n0) {
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
       for (int c = 0; c < J; ++c) {
         const int k0 = ((sl * J + c) * 32 + lane) * 16;
         const int row = n0 + r;
-        wv[r][c] = (row < n && k0 < k) ? ldg_stream(w + static_cast<int64_t>(row) * ldw + k0)
-                                       : make_uint4(0u, 0u, 0u, 0u);
+        dst[r][c] = (row < n && k0 < k) ? ldg_stream(w + static_cast<int64_t>(row) * ldw + k0)
+                                        : make_uint4(0u, 0u, 0u, 0u);
       }
   };
   // The weights do not depend on the previous kernel: start streaming them before
   // waiting for it (only the activation row does).
-  load_w(first);
+  load_w(wv, first);
   pdl_wait();
 
   for (int t = 0; t < t_count; ++t) {
@@ -160,7 +164,19 @@ __global__ void __launch_bounds__(kGemvThreads)
     }
 
     for (int n0 = first; n0 < n; n0 += stride) {
-      if (t > 0 || n0 != first) load_w(n0);
+      bool fetched = false;
+      if constexpr (kPrefetch) {
+        // wv holds row n0 (loaded by the previous step, or before the wait); fetch the
+        // row of the next step (the next activation row starts again at `first`).
+        int nx = n0 + stride;
+        if (nx >= n && t + 1 < t_count) nx = first;
+        if (nx < n) {
+          load_w(wn, nx);
+          fetched = true;
+        }
+      } else {
+        if (t > 0 || n0 != first) load_w(wv, n0);
+      }
       float acc[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
@@ -201,6 +217,14 @@ __global__ void __launch_bounds__(kGemvThreads)
           if (LOGITS && best != nullptr) mine = max(mine, argmax_key(f, n0 + lane));
         }
         asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");
+      }
+      if constexpr (kPrefetch) {
+        if (fetched) {
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int c = 0; c < J; ++c) wv[r][c] = wn[r][c];
+        }
       }
     }
   }

@@ -116,6 +116,26 @@ def test_extreme_values_no_overflow(cuda):
     assert int(c[1, 0]) == k * 127 * 127 and int(c[1, 1]) == -k * 127 * 128
 
 
+# The tile width follows the wave count: 64 or 128 columns for GEMMs with one wave of
+# tiles or less (short prompts, the 1536 -> 256 PLE gate), 192 for qkv / o at M = 3658,
+# 256 otherwise; ragged last n-tiles (N = 200, 264) included.
+@pytest.mark.parametrize("m,n,k", [(300, 384, 1536), (257, 200, 128), (513, 264, 640), (207, 2560, 1536),
+                                   (858, 1536, 2048), (3658, 256, 1536), (1878, 1536, 2048), (3658, 2560, 1536)])
+def test_dequant_every_tile_width_bit_exact(cuda, m, n, k):
+    gen = torch.Generator(device=cuda).manual_seed(m + 7 * n + k)
+    a = torch.randint(-128, 128, (m, k), dtype=torch.int8, device=cuda, generator=gen)
+    w = torch.randint(-128, 128, (n, k), dtype=torch.int8, device=cuda, generator=gen)
+    sx = torch.rand((m,), device=cuda, generator=gen) * 1e-2
+    sw = torch.rand((n,), device=cuda, generator=gen) * 1e-3
+    y = w8.gemm_dequant(a, w, sx, sw)
+    c = torch.empty((m, n), dtype=torch.int32, device=cuda)
+    w8.mm_i8_nk(a, w, c)
+    assert torch.equal(c, torch._int_mm(a, w.t().contiguous()))
+    rows = sorted({0, m - 1} | set(torch.randperm(m, generator=torch.Generator().manual_seed(1))[:20].tolist()))
+    want = ref.dequant(c[rows].cpu().numpy(), sx[rows].cpu().numpy(), sw.cpu().numpy())
+    np.testing.assert_array_equal(y[rows].cpu().view(torch.int16).numpy().view(np.uint16), want)
+
+
 @pytest.mark.parametrize("n", [300, 301, 37])
 def test_any_output_pitch(cuda, n):
     # contiguous C with N % 4 != 0: row starts are not 16-byte aligned -> element stores
