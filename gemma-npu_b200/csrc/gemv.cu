@@ -312,9 +312,11 @@ static int gemv_dispatch(const uint16_t* xh, int64_t ldx, const int8_t* w, int64
   if (st2 != W8_OK) return st2;
   // Smallest (S, J) whose slice covers K: x stays within 64 fp32 registers per lane.
   // R rows per team per step: the large R keeps more weight bytes in flight per warp;
-  // a matrix too short to give two CTAs per SM at that R takes one row per team.
+  // a matrix too short to give one CTA per SM at that R takes one row per team (measured
+  // in a dependent chain: down 1536 x 6144 5.2 -> 4.2 us and 8960 x 1536 5.5 -> 4.4 us with
+  // R = 4 at one or more CTAs per SM, against R = 1 at two).
 #define W8_GEMV(J, S, R)                                                                      \
-  return n < 2 * sms * (w8::kGemvWarps / (S)) * (R)                                            \
+  return n < sms * (w8::kGemvWarps / (S)) * (R)                                                \
              ? launch_gemv<J, S, 1, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream, best) \
              : launch_gemv<J, S, R, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream, best)
   if (k <= 512) W8_GEMV(1, 1, 4);
