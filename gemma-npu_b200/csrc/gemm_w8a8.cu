@@ -83,22 +83,7 @@ struct GemmArgs {
   uint32_t* flags;   // stream-K: one zero-initialised counter per tile
   int bn;            // output columns per tile: 256, or 192 on CTA pairs when it balances waves
   float* row_absmax; // kEpiGeluUp: per-row max |output| (fp32 bits, atomicMax), zero on entry
-  int raster_n;      // tile order: 1 = the n-tiles of one m-tile are consecutive, 0 = m-tiles
 };
-
-// Output tile -> (m-tile, n-tile).  Consecutive tiles run on neighbouring workers at the
-// same time, so the order decides which operand a wave shares: with the n-tiles of one
-// m-tile consecutive, a wave reads few A rows and much of B (better when B is the smaller
-// operand, N < M: qkv, o, down at M = 3658), and the other way round for wide N.
-__device__ __forceinline__ void tile_coords(const GemmArgs& a, int tile, int& mb, int& nb) {
-  if (a.raster_n) {
-    mb = tile / a.n_tiles;
-    nb = tile - mb * a.n_tiles;
-  } else {
-    nb = tile / a.m_tiles;
-    mb = tile - nb * a.m_tiles;
-  }
-}
 
 constexpr int kEpiBufBytes = 32 * 128;  // one 32-row x 128-byte store box
 constexpr int kEpiBufs = 2;             // per epilogue warp: fill one while TMA drains the other
@@ -490,8 +475,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
       uint32_t phase = 0;
       bool ok = true;
       while (ok && sched.next(args, sg)) {
-        int mb, nb;
-        tile_coords(args, sg.tile, mb, nb);
+        const int mb = sg.tile % args.m_tiles;
+        const int nb = sg.tile / args.m_tiles;
         const int a_row = mb * 2 * kBM + static_cast<int>(rank) * kBM;
         const int b_col = nb * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
@@ -595,8 +580,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
       const bool ok = mbar_wait_bounded(tfull_bar(acc), acc_phase, abort_flag, &g_gemm_status);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      int mb, nb;
-      tile_coords(args, sg.tile, mb, nb);
+      const int mb = sg.tile % args.m_tiles;
+      const int nb = sg.tile / args.m_tiles;
       const int row0 = mb * 2 * kBM + static_cast<int>(rank) * kBM + quarter * 32;
       float sxr = 0.f;
       if constexpr (EPI != kEpiI32) sxr = row0 + lane < args.m ? __ldg(args.sx + row0 + lane) : 0.f;
@@ -679,8 +664,8 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
       uint32_t phase = 0, issued_mask = 0, last_phase = 0;
       bool ok = true;
       while (ok && sched.next(args, sg)) {
-        int mb, nb;
-        tile_coords(args, sg.tile, mb, nb);
+        const int mb = sg.tile % args.m_tiles;
+        const int nb = sg.tile / args.m_tiles;
         for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, &g_gemm_status)) {
             ok = false;
@@ -775,8 +760,8 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
       const bool ok = mbar_wait_bounded(tfull_bar(acc), acc_phase, abort_flag, &g_gemm_status);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      int mb, nb;
-      tile_coords(args, sg.tile, mb, nb);
+      const int mb = sg.tile % args.m_tiles;
+      const int nb = sg.tile / args.m_tiles;
       const int row0 = mb * kBM + quarter * 32;
       float sxr = 0.f;
       if constexpr (EPI != kEpiI32) sxr = row0 + lane < args.m ? __ldg(args.sx + row0 + lane) : 0.f;
@@ -1074,7 +1059,7 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
     st = encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, n, k, ldb, 128, stage_k);
   if (st != W8_OK) return st;
 
-  w8::GemmArgs args = {};
+  w8::GemmArgs args;
   args.m = static_cast<int>(m);
   args.n = static_cast<int>(n);
   args.k = static_cast<int>(k);
@@ -1091,7 +1076,6 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   args.stream_k = 0;
   args.flags = static_cast<uint32_t*>(workspace);
   args.row_absmax = row_absmax;
-  args.raster_n = n < m ? 1 : 0;
   const int64_t flag_words = workspace_bytes / 4;
   // Output through TMA when the tensor map can address it (16-byte base and pitch);
   // one box is 32 rows x 128 bytes.  Otherwise the epilogue stores directly.
