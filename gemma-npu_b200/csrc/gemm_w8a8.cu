@@ -89,16 +89,22 @@ constexpr int kEpiBufBytes = 32 * 128;  // one 32-row x 128-byte store box
 constexpr int kEpiBufs = 2;             // per epilogue warp: fill one while TMA drains the other
 
 // Epilogue warps of a CTA: one per TMEM lane quarter, each with two staging boxes.  The
-// gate/up glue, whose per-element math outweighs its stores, takes two warps per quarter
-// (each finishes one of the tile's two output boxes) with one staging box each: the
-// same shared memory, twice the issue slots.
+// gate/up glue, whose per-element math outweighs its stores, takes four warps per quarter
+// (each finishes 32 of the tile's 128 output columns, one 32-row x 64-byte box) with one
+// staging box each: the same shared memory, four times the warps to hide the latency of
+// the math (with two warps per quarter it waited on its own dependences, not on a unit).
+constexpr int kGeluWarpsPerQuarter = 4;
+constexpr int kGeluBufBytes = 32 * 64;
 template <int EPI>
-constexpr int epi_warps() { return EPI == kEpiGeluUp ? 2 * kEpiWarps : kEpiWarps; }
+constexpr int epi_warps() { return EPI == kEpiGeluUp ? kGeluWarpsPerQuarter * kEpiWarps : kEpiWarps; }
 template <int EPI>
-constexpr int epi_bufs() { return EPI == kEpiGeluUp ? kEpiBufs / 2 : kEpiBufs; }
+constexpr int epi_bufs() { return EPI == kEpiGeluUp ? 1 : kEpiBufs; }
+template <int EPI>
+constexpr int epi_buf_bytes() { return EPI == kEpiGeluUp ? kGeluBufBytes : kEpiBufBytes; }
 template <int EPI>
 constexpr int threads_for() { return 64 + 32 * epi_warps<EPI>(); }
-static_assert(2 * kEpiWarps * (kEpiBufs / 2) == kEpiWarps * kEpiBufs, "staging layout differs");
+static_assert(kGeluWarpsPerQuarter * kEpiWarps * kGeluBufBytes == kEpiWarps * kEpiBufs * kEpiBufBytes,
+              "staging layout differs");
 
 // Shared-memory plan of one CTA: the operand ring, the epilogue staging boxes, barriers.
 template <int STAGES, int A_BYTES, int B_BYTES>
@@ -230,31 +236,34 @@ __device__ __forceinline__ void dequant_pack(const GemmArgs& a, int col0, const 
   }
 }
 
-// 32 gate accumulators (GEMM columns gcol0..) and the 32 up accumulators 128 columns to
-// their right -> 16 words of packed bf16 a = bf16(gelu(_deq(gate)) * _deq(up)); `amax`
-// accumulates max |a|.
-__device__ __forceinline__ void gelu_up_pack(const GemmArgs& a, int gcol0, const uint32_t (&rg)[32],
-                                             const uint32_t (&ru)[32], float sxr, uint32_t* out,
-                                             float& amax) {
-  float wg[32], wu[32];
+// The weight scales of 16 gate columns (GEMM columns gcol0..) and of the 16 up columns
+// 128 columns to their right.
+__device__ __forceinline__ void gelu_up_scales16(const GemmArgs& a, int gcol0, float (&wg)[16], float (&wu)[16]) {
   if (a.vec_sw) {
     const float4* g4 = reinterpret_cast<const float4*>(a.sw + gcol0);
     const float4* u4 = reinterpret_cast<const float4*>(a.sw + gcol0 + 128);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < 4; ++j) {
       const float4 t = __ldg(g4 + j), v = __ldg(u4 + j);
       wg[4 * j] = t.x, wg[4 * j + 1] = t.y, wg[4 * j + 2] = t.z, wg[4 * j + 3] = t.w;
       wu[4 * j] = v.x, wu[4 * j + 1] = v.y, wu[4 * j + 2] = v.z, wu[4 * j + 3] = v.w;
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < 16; ++j) {
       wg[j] = __ldg(a.sw + gcol0 + j);
       wu[j] = __ldg(a.sw + gcol0 + 128 + j);
     }
   }
+}
+
+// 16 gate and 16 up accumulators with their scales -> 8 words of packed bf16
+// a = bf16(gelu(_deq(gate)) * _deq(up)); `amax` accumulates max |a|.
+__device__ __forceinline__ void gelu_up_pack16(const uint32_t (&rg)[16], const uint32_t (&ru)[16],
+                                               const float (&wg)[16], const float (&wu)[16], float sxr,
+                                               uint32_t* out, float& amax) {
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
+  for (int j = 0; j < 8; ++j) {
     float av[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -293,6 +302,22 @@ __device__ __forceinline__ void put_box(const CUtensorMap* tm_c, const uint32_t 
   }
 }
 
+// Stage one 32-row x 64-byte box (32 bf16 columns, row = lane, no swizzle) in this warp's
+// buffer and store it with TMA at column x, row row0.
+__device__ __forceinline__ void put_box64(const CUtensorMap* tm_c, const uint32_t (&v)[16], uint32_t buf,
+                                          int lane, int x, int row0) {
+  if (lane == 0) bulk_wait_group_read<0>();  // the previous box stored from buf is read
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) st_shared_v4(buf + lane * 64 + j * 16, v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tm_c, buf, x, row0);
+    bulk_commit_group();
+  }
+}
+
 // Drain one 32-row slice of a finished accumulator (called by one whole epilogue warp).
 // `taddr` addresses the warp's TMEM lanes at the accumulator's first column; rows
 // row0.. and columns col_base.. of the output.  `release` hands the accumulator back to
@@ -306,28 +331,30 @@ __device__ __forceinline__ void epilogue_rows(const GemmArgs& args, const CUtens
   const int n_cols = min(args.bn, args.n - col_base);  // columns of this tile inside N
   const int row = row0 + lane;
   if constexpr (EPI == kEpiGeluUp) {
-    // 256 accumulator columns = 128 gate + 128 up -> output columns col_base / 2 ..+128,
-    // two 64-column bf16 boxes (the output must be TMA-addressable); this warp finishes
-    // box `part`, the warp of the same lane quarter in the other half the other box.
+    // 256 accumulator columns = 128 gate + 128 up -> output columns col_base / 2 ..+128;
+    // this warp (`part` of the four of its lane quarter) finishes output columns
+    // 32 part .. 32 part + 31 of its 32 rows, 16 at a time.
     float amax = 0.f;
     {
-      const int b = part;
-      uint32_t v[32];
+      uint32_t v[16];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int c = b * 64 + h * 32;
-        uint32_t rg[32], ru[32];
-        tmem_ld_32x32b_x32(taddr + c, rg);
-        tmem_ld_32x32b_x32(taddr + 128 + c, ru);
+        const int c = part * 32 + h * 16;
+        uint32_t rg[16], ru[16];
+        tmem_ld_32x32b_x16(taddr + c, rg);
+        tmem_ld_32x32b_x16(taddr + 128 + c, ru);
         tmem_wait_ld();
+        float wg[16], wu[16];
+        gelu_up_scales16(args, col_base + c, wg, wu);
         if (h == 1) {  // this warp's columns are in registers: hand TMEM back
           tc_fence_before();
           __syncwarp();
           if (lane == 0) release();
         }
-        gelu_up_pack(args, col_base + c, rg, ru, sxr, v + h * 16, amax);
+        gelu_up_pack16(rg, ru, wg, wu, sxr, v + h * 8, amax);
       }
-      put_box<epi_bufs<EPI>()>(tm_c, v, stage_base, sbuf, lane, col_base / 2 + b * 64, row0, false);
+      (void)sbuf;
+      put_box64(tm_c, v, stage_base, lane, col_base / 2 + part * 32, row0);
     }
     if (row < args.m) atomicMax(reinterpret_cast<int*>(args.row_absmax) + row, __float_as_int(amax));
     return;
@@ -567,7 +594,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
     // ---------------- epilogue (both CTAs): this CTA's 128 rows of every 256 x 256 tile
     const int quarter = warp & 3;     // TMEM lane quarter this warp may access
     const int part = (warp - 2) / 4;  // which share of the tile's columns (gate/up glue)
-    const uint32_t stage_base = base + L::kEpiOff + (warp - 2) * epi_bufs<EPI>() * kEpiBufBytes;
+    const uint32_t stage_base = base + L::kEpiOff + (warp - 2) * epi_bufs<EPI>() * epi_buf_bytes<EPI>();
     const uint32_t tempty_leader0 = mapa_shared(tempty_bar(0), 0);
     Schedule sched(args, worker, workers);
     Segment sg;
@@ -748,7 +775,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
     // ---------------- epilogue
     const int quarter = warp & 3;
     const int part = (warp - 2) / 4;
-    const uint32_t stage_base = base + L::kEpiOff + (warp - 2) * epi_bufs<EPI>() * kEpiBufBytes;
+    const uint32_t stage_base = base + L::kEpiOff + (warp - 2) * epi_bufs<EPI>() * epi_buf_bytes<EPI>();
     Schedule sched(args, blockIdx.x, gridDim.x);
     Segment sg;
     uint32_t sbuf = 0;
@@ -807,9 +834,11 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D tensor [outer, inner] with row pitch `pitch` bytes, 128-byte swizzled boxes.
+// 2-D tensor [outer, inner] with row pitch `pitch` bytes, 128-byte swizzled boxes (or
+// `swizzle`).
 static int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* ptr, int64_t inner,
-                     int64_t outer, int64_t pitch, uint32_t box_inner, uint32_t box_outer) {
+                     int64_t outer, int64_t pitch, uint32_t box_inner, uint32_t box_outer,
+                     CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) {
     set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -820,7 +849,7 @@ static int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* pt
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = enc(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed with CUresult %d (inner %lld, outer %lld, pitch %lld)",
@@ -1083,8 +1112,13 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   args.tma_out = 0;
   if (args.vec_out) {
     const bool i32 = epi == w8::kEpiI32;
-    st = encode_2d(&tc, i32 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, n_out, m,
-                   ldo * out_elem, i32 ? 32 : 64, 32);
+    // The gate/up glue stores 32-row x 32-column bf16 boxes (one per epilogue warp,
+    // unswizzled 64-byte rows).
+    st = epi == w8::kEpiGeluUp
+             ? encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, n_out, m, ldo * out_elem, 32, 32,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)
+             : encode_2d(&tc, i32 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, n_out,
+                         m, ldo * out_elem, i32 ? 32 : 64, 32);
     if (st != W8_OK) return st;
     args.tma_out = 1;
   }
