@@ -257,24 +257,73 @@ __device__ __forceinline__ void gelu_up_scales16(const GemmArgs& a, int gcol0, f
   }
 }
 
+// Two fp32 values in one 64-bit register pair, for sm_100's packed f32x2 instructions:
+// each lane of a packed mul / add is one IEEE fp32 operation rounded to nearest, so a
+// pair of outputs takes one instruction per step and the same bits as two.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// Both values rounded to bf16 (nearest even); returns them as fp32 and sets `bits` to the
+// packed bf16 pair.
+__device__ __forceinline__ uint64_t f2_round_bf16(uint64_t v, uint32_t& bits) {
+  float lo, hi;
+  f2_unpack(v, lo, hi);
+  __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  bits = *reinterpret_cast<uint32_t*>(&p);
+  return f2_pack(__uint_as_float(bits << 16), __uint_as_float(bits & 0xFFFF0000u));
+}
+
 // 16 gate and 16 up accumulators with their scales -> 8 words of packed bf16
-// a = bf16(gelu(_deq(gate)) * _deq(up)); `amax` accumulates max |a|.
+// a = bf16(gelu(_deq(gate)) * _deq(up)); `amax` accumulates max |a|.  Two columns at a
+// time on packed f32x2 instructions, in gelu_tanh_bf16's operation order.
 __device__ __forceinline__ void gelu_up_pack16(const uint32_t (&rg)[16], const uint32_t (&ru)[16],
                                                const float (&wg)[16], const float (&wu)[16], float sxr,
                                                uint32_t* out, float& amax) {
+  const uint64_t sx2 = f2_pack(sxr, sxr);
+  const uint64_t kappa2 = f2_pack(kGeluKappa, kGeluKappa), beta2 = f2_pack(kGeluBeta, kGeluBeta);
+  const uint64_t m2l2e2 = f2_pack(-2.8853900817779268f, -2.8853900817779268f);  // -2 log2(e)
+  const uint64_t one2 = f2_pack(1.f, 1.f), two2 = f2_pack(2.f, 2.f), half2 = f2_pack(0.5f, 0.5f);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    float av[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int c = 2 * j + e;
-      const float g = round_bf16(__fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(rg[c])), sxr), wg[c]));
-      const float u = round_bf16(__fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(ru[c])), sxr), wu[c]));
-      av[e] = round_bf16(__fmul_rn(gelu_tanh_bf16(g), u));
-      amax = fmaxf(amax, fabsf(av[e]));
-    }
-    __nv_bfloat162 p = __floats2bfloat162_rn(av[0], av[1]);
-    out[j] = *reinterpret_cast<uint32_t*>(&p);
+    const int c = 2 * j;
+    uint32_t bits;
+    const uint64_t gi = f2_pack(__int2float_rn(static_cast<int>(rg[c])), __int2float_rn(static_cast<int>(rg[c + 1])));
+    const uint64_t ui = f2_pack(__int2float_rn(static_cast<int>(ru[c])), __int2float_rn(static_cast<int>(ru[c + 1])));
+    const uint64_t g = f2_round_bf16(f2_mul(f2_mul(gi, sx2), f2_pack(wg[c], wg[c + 1])), bits);
+    const uint64_t u = f2_round_bf16(f2_mul(f2_mul(ui, sx2), f2_pack(wu[c], wu[c + 1])), bits);
+    // gelu_tanh_bf16 on both: 1 + tanh(z) = 2 / (1 + e^(-2z)).
+    const uint64_t g3 = f2_mul(f2_mul(g, g), g);
+    const uint64_t inner = f2_mul(beta2, f2_add(g, f2_mul(kappa2, g3)));
+    float a0, a1;
+    f2_unpack(f2_mul(inner, m2l2e2), a0, a1);
+    float e0, e1;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(a0));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(a1));
+    float d0, d1, r0, r1;
+    f2_unpack(f2_add(one2, f2_pack(e0, e1)), d0, d1);
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d0));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d1));
+    const uint64_t gel = f2_round_bf16(f2_mul(f2_mul(half2, g), f2_mul(two2, f2_pack(r0, r1))), bits);
+    const uint64_t av = f2_round_bf16(f2_mul(gel, u), bits);
+    float v0, v1;
+    f2_unpack(av, v0, v1);
+    amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
+    out[j] = bits;
   }
 }
 
