@@ -208,55 +208,6 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0
   }
 }
 
-// 32 int32 accumulators of columns col0.. -> 16 words of packed bf16 pairs,
-// bf16((float(acc) * sx[row]) * sw[col]) with _deq's operation order.
-__device__ __forceinline__ void dequant_pack(const GemmArgs& a, int col0, const uint32_t (&r)[32],
-                                             float sxr, uint32_t* out) {
-  float w[32];
-  if (a.vec_sw && col0 + 32 <= a.n) {
-    const float4* sw4 = reinterpret_cast<const float4*>(a.sw + col0);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 t = __ldg(sw4 + j);
-      w[4 * j] = t.x;
-      w[4 * j + 1] = t.y;
-      w[4 * j + 2] = t.z;
-      w[4 * j + 3] = t.w;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) w[j] = col0 + j < a.n ? __ldg(a.sw + col0 + j) : 0.f;
-  }
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const float v0 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[2 * j])), sxr), w[2 * j]);
-    const float v1 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[2 * j + 1])), sxr), w[2 * j + 1]);
-    __nv_bfloat162 p = __floats2bfloat162_rn(v0, v1);
-    out[j] = *reinterpret_cast<uint32_t*>(&p);
-  }
-}
-
-// The weight scales of 16 gate columns (GEMM columns gcol0..) and of the 16 up columns
-// 128 columns to their right.
-__device__ __forceinline__ void gelu_up_scales16(const GemmArgs& a, int gcol0, float (&wg)[16], float (&wu)[16]) {
-  if (a.vec_sw) {
-    const float4* g4 = reinterpret_cast<const float4*>(a.sw + gcol0);
-    const float4* u4 = reinterpret_cast<const float4*>(a.sw + gcol0 + 128);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float4 t = __ldg(g4 + j), v = __ldg(u4 + j);
-      wg[4 * j] = t.x, wg[4 * j + 1] = t.y, wg[4 * j + 2] = t.z, wg[4 * j + 3] = t.w;
-      wu[4 * j] = v.x, wu[4 * j + 1] = v.y, wu[4 * j + 2] = v.z, wu[4 * j + 3] = v.w;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      wg[j] = __ldg(a.sw + gcol0 + j);
-      wu[j] = __ldg(a.sw + gcol0 + 128 + j);
-    }
-  }
-}
-
 // Two fp32 values in one 64-bit register pair, for sm_100's packed f32x2 instructions:
 // each lane of a packed mul / add is one IEEE fp32 operation rounded to nearest, so a
 // pair of outputs takes one instruction per step and the same bits as two.
@@ -286,6 +237,57 @@ __device__ __forceinline__ uint64_t f2_round_bf16(uint64_t v, uint32_t& bits) {
   __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
   bits = *reinterpret_cast<uint32_t*>(&p);
   return f2_pack(__uint_as_float(bits << 16), __uint_as_float(bits & 0xFFFF0000u));
+}
+
+// 32 int32 accumulators of columns col0.. -> 16 words of packed bf16 pairs,
+// bf16((float(acc) * sx[row]) * sw[col]) with _deq's operation order.
+__device__ __forceinline__ void dequant_pack(const GemmArgs& a, int col0, const uint32_t (&r)[32],
+                                             float sxr, uint32_t* out) {
+  float w[32];
+  if (a.vec_sw && col0 + 32 <= a.n) {
+    const float4* sw4 = reinterpret_cast<const float4*>(a.sw + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 t = __ldg(sw4 + j);
+      w[4 * j] = t.x;
+      w[4 * j + 1] = t.y;
+      w[4 * j + 2] = t.z;
+      w[4 * j + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) w[j] = col0 + j < a.n ? __ldg(a.sw + col0 + j) : 0.f;
+  }
+  const uint64_t sx2 = f2_pack(sxr, sxr);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {  // two columns per packed f32x2 multiply
+    const uint64_t a = f2_pack(__int2float_rn(static_cast<int>(r[2 * j])), __int2float_rn(static_cast<int>(r[2 * j + 1])));
+    float v0, v1;
+    f2_unpack(f2_mul(f2_mul(a, sx2), f2_pack(w[2 * j], w[2 * j + 1])), v0, v1);
+    __nv_bfloat162 p = __floats2bfloat162_rn(v0, v1);
+    out[j] = *reinterpret_cast<uint32_t*>(&p);
+  }
+}
+
+// The weight scales of 16 gate columns (GEMM columns gcol0..) and of the 16 up columns
+// 128 columns to their right.
+__device__ __forceinline__ void gelu_up_scales16(const GemmArgs& a, int gcol0, float (&wg)[16], float (&wu)[16]) {
+  if (a.vec_sw) {
+    const float4* g4 = reinterpret_cast<const float4*>(a.sw + gcol0);
+    const float4* u4 = reinterpret_cast<const float4*>(a.sw + gcol0 + 128);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 t = __ldg(g4 + j), v = __ldg(u4 + j);
+      wg[4 * j] = t.x, wg[4 * j + 1] = t.y, wg[4 * j + 2] = t.z, wg[4 * j + 3] = t.w;
+      wu[4 * j] = v.x, wu[4 * j + 1] = v.y, wu[4 * j + 2] = v.z, wu[4 * j + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      wg[j] = __ldg(a.sw + gcol0 + j);
+      wu[j] = __ldg(a.sw + gcol0 + 128 + j);
+    }
+  }
 }
 
 // 16 gate and 16 up accumulators with their scales -> 8 words of packed bf16
