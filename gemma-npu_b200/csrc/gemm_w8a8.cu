@@ -208,37 +208,6 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, int row, int col0
   }
 }
 
-// Two fp32 values in one 64-bit register pair, for sm_100's packed f32x2 instructions:
-// each lane of a packed mul / add is one IEEE fp32 operation rounded to nearest, so a
-// pair of outputs takes one instruction per step and the same bits as two.
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-// Both values rounded to bf16 (nearest even); returns them as fp32 and sets `bits` to the
-// packed bf16 pair.
-__device__ __forceinline__ uint64_t f2_round_bf16(uint64_t v, uint32_t& bits) {
-  float lo, hi;
-  f2_unpack(v, lo, hi);
-  __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
-  bits = *reinterpret_cast<uint32_t*>(&p);
-  return f2_pack(__uint_as_float(bits << 16), __uint_as_float(bits & 0xFFFF0000u));
-}
-
 // 32 int32 accumulators of columns col0.. -> 16 words of packed bf16 pairs,
 // bf16((float(acc) * sx[row]) * sw[col]) with _deq's operation order.
 __device__ __forceinline__ void dequant_pack(const GemmArgs& a, int col0, const uint32_t (&r)[32],

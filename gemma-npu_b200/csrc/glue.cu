@@ -139,38 +139,47 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
         if (lane + 32 * i < nv) res[i] = ld16(a.res + static_cast<int64_t>(row) * a.ldr + (lane + 32 * i) * 8);
     }
     const float r1 = rms_factor<NV>(v, nv, lane, a.n, a.eps);
+    const uint64_t r1_2 = f2_pack(r1, r1), sc2 = f2_pack(a.scalar, a.scalar);
 #pragma unroll
     for (int i = 0; i < kMax; ++i) {
       const int vi = lane + 32 * i;
       if (vi < nv) {
-        float x[8], w[8];
-        unpack8(v[i], x);
-        unpack8(w1s[vi], w);
-        float rr[8];
-        if constexpr (MODE != kGlueIn) unpack8(res[i], rr);
+        // Two elements per packed f32x2 step, in the scalar operation order.
+        uint32_t xw[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        const uint4 wv = w1s[vi];
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t rw[4] = {0u, 0u, 0u, 0u};
+        if constexpr (MODE != kGlueIn) rw[0] = res[i].x, rw[1] = res[i].y, rw[2] = res[i].z, rw[3] = res[i].w;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float t = rbf16(__fmul_rn(__fmul_rn(x[e], r1), w[e]));
-          x[e] = MODE == kGlueIn ? t : rbf16(__fadd_rn(rr[e], t));
-          if (MODE != kGlueIn && a.scalar != 1.f) x[e] = rbf16(__fmul_rn(x[e], a.scalar));
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t t = bf16x2_from_f2(f2_mul(f2_mul(f2_from_bf16x2(xw[j]), r1_2), f2_from_bf16x2(ww[j])));
+          if constexpr (MODE == kGlueIn) {
+            xw[j] = t;
+          } else {
+            uint32_t h = bf16x2_from_f2(f2_add(f2_from_bf16x2(rw[j]), f2_from_bf16x2(t)));
+            if (a.scalar != 1.f) h = bf16x2_from_f2(f2_mul(f2_from_bf16x2(h), sc2));
+            xw[j] = h;
+          }
         }
-        v[i] = pack8(x);
+        v[i] = make_uint4(xw[0], xw[1], xw[2], xw[3]);
         if constexpr (MODE != kGlueIn)
           *reinterpret_cast<uint4*>(a.h + static_cast<int64_t>(row) * a.ldh + vi * 8) = v[i];
       }
     }
     if constexpr (MODE == kGluePost2) {
       const float r2 = rms_factor<NV>(v, nv, lane, a.n, a.eps);
+      const uint64_t r2_2 = f2_pack(r2, r2);
 #pragma unroll
       for (int i = 0; i < kMax; ++i) {
         const int vi = lane + 32 * i;
         if (vi < nv) {
-          float x[8], w[8];
-          unpack8(v[i], x);
-          unpack8(w2s[vi], w);
+          uint32_t xw[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+          const uint4 wv = w2s[vi];
+          const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-          for (int e = 0; e < 8; ++e) x[e] = rbf16(__fmul_rn(__fmul_rn(x[e], r2), w[e]));
-          v[i] = pack8(x);
+          for (int j = 0; j < 4; ++j)
+            xw[j] = bf16x2_from_f2(f2_mul(f2_mul(f2_from_bf16x2(xw[j]), r2_2), f2_from_bf16x2(ww[j])));
+          v[i] = make_uint4(xw[0], xw[1], xw[2], xw[3]);
         }
       }
     }
@@ -190,15 +199,23 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
   const float sc = __fdiv_rn(fmaxf(amax, 1e-8f), 127.f);
   const float rc = __frcp_rn(sc);
   if (lane == 0) a.s[row] = sc;
+  const uint64_t rc2 = f2_pack(rc, rc), nsc2 = f2_pack(-sc, -sc);
 #pragma unroll
   for (int i = 0; i < kMax; ++i) {
     const int vi = lane + 32 * i;
     if (vi < nv) {
-      float x[8];
-      unpack8(v[i], x);
+      const uint32_t xw[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
       int8_t out[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) out[e] = quant_one(x[e], sc, rc);
+      for (int j = 0; j < 4; ++j) {
+        // div_rn_by on a pair: t = x * r, then t + r * (x - s * t), each step rounded once.
+        const uint64_t x2 = f2_from_bf16x2(xw[j]);
+        const uint64_t t2 = f2_mul(x2, rc2);
+        float q0, q1;
+        f2_unpack(f2_fma(f2_fma(nsc2, t2, x2), rc2, t2), q0, q1);
+        out[2 * j] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(q0), -127.f), 127.f)));
+        out[2 * j + 1] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(q1), -127.f), 127.f)));
+      }
       store_q<8>(a.q + static_cast<int64_t>(row) * a.ldq + vi * 8, out);
     }
   }
