@@ -15,6 +15,8 @@
 // registers between the absmax pass and the quantise pass), a grid-stride 16-byte
 // vectorised loop for dequant.
 #include "common.cuh"
+#include <type_traits>
+
 #include "rowquant.cuh"
 
 namespace w8 {
@@ -66,16 +68,24 @@ __global__ void __launch_bounds__(kQuantThreads)
     const int vi = threadIdx.x + i * kQuantThreads;
     if (vi < nvec) {
       int8_t out[VEC];
+      if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
+        quant8_bf16(*reinterpret_cast<const uint4*>(held[i].v), sc, rc, out);
+      } else {
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) out[e] = quant_one(to_f32(held[i].v[e]), sc, rc);
+        for (int e = 0; e < VEC; ++e) out[e] = quant_one(to_f32(held[i].v[e]), sc, rc);
+      }
       store_q<VEC>(qr + static_cast<int64_t>(vi) * VEC, out);
     }
   }
   for (int vi = threadIdx.x + kQuantMaxVecs * kQuantThreads; vi < nvec; vi += kQuantThreads) {
     const Vec<T, VEC> v = load_vec<T, VEC>(xr + static_cast<int64_t>(vi) * VEC);
     int8_t out[VEC];
+    if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
+      quant8_bf16(*reinterpret_cast<const uint4*>(v.v), sc, rc, out);
+    } else {
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) out[e] = quant_one(to_f32(v.v[e]), sc, rc);
+      for (int e = 0; e < VEC; ++e) out[e] = quant_one(to_f32(v.v[e]), sc, rc);
+    }
     store_q<VEC>(qr + static_cast<int64_t>(vi) * VEC, out);
   }
 }
@@ -143,8 +153,7 @@ __global__ void __launch_bounds__(kQuantThreads)
     const int vi = threadIdx.x + i * kQuantThreads;
     if (vi < nvec) {
       int8_t out[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) out[e] = quant_one(__bfloat162float(held[i].v[e]), sc, rc);
+      quant8_bf16(*reinterpret_cast<const uint4*>(held[i].v), sc, rc, out);
       store_q<8>(qr + vi * 8, out);
     }
   }
@@ -152,8 +161,7 @@ __global__ void __launch_bounds__(kQuantThreads)
   for (int vi = threadIdx.x + kQuantMaxVecs * kQuantThreads; vi < nvec; vi += kQuantThreads) {
     const Vec<__nv_bfloat16, 8> v = load_vec<__nv_bfloat16, 8>(yr + vi * 8);
     int8_t out[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) out[e] = quant_one(__bfloat162float(v.v[e]), sc, rc);
+    quant8_bf16(*reinterpret_cast<const uint4*>(v.v), sc, rc, out);
     store_q<8>(qr + vi * 8, out);
   }
 }

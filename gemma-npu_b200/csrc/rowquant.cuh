@@ -34,6 +34,22 @@ __device__ __forceinline__ int8_t quant_one(float v, float s, float r) {
   return static_cast<int8_t>(static_cast<int>(q));
 }
 
+// quant_one on the eight bf16 values of a 16-byte vector, two at a time: the division
+// steps on packed f32x2 instructions (the same IEEE operations, so the same codes).
+__device__ __forceinline__ void quant8_bf16(const uint4& v, float s, float r, int8_t (&out)[8]) {
+  const uint64_t r2 = f2_pack(r, r), ns2 = f2_pack(-s, -s);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint64_t x2 = f2_from_bf16x2(w[j]);
+    const uint64_t t2 = f2_mul(x2, r2);
+    float q0, q1;
+    f2_unpack(f2_fma(f2_fma(ns2, t2, x2), r2, t2), q0, q1);
+    out[2 * j] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(q0), -127.f), 127.f)));
+    out[2 * j + 1] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(q1), -127.f), 127.f)));
+  }
+}
+
 // VEC elements of T per 16-byte vector (VEC == 1: unaligned scalar path).
 template <typename T, int VEC>
 struct alignas(VEC * sizeof(T) >= 16 ? 16 : alignof(T)) Vec {
