@@ -297,15 +297,20 @@ __global__ void __launch_bounds__(32 * kGlueWarps) qkv_rows_kernel(const QkvArgs
   for (int j = 0; j < 2; ++j)
     if (j < slots && active) {
       const int c = (lane + 32 * j) * 8;
-      float f[8], g[8];
-      unpack8(v[j], f);
-      if (w != nullptr) unpack8(ld16(w + c), g);
+      // Two elements per packed f32x2 step (the same IEEE operations as one at a time).
+      const uint64_t r2 = f2_pack(r, r);
+      uint32_t xw[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+      if (w != nullptr) {
+        const uint4 gv = ld16(w + c);
+        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float t = __fmul_rn(f[e], r);
-        f[e] = rbf16(w != nullptr ? __fmul_rn(t, g[e]) : t);
+        for (int q = 0; q < 4; ++q)
+          xw[q] = bf16x2_from_f2(f2_mul(f2_mul(f2_from_bf16x2(xw[q]), r2), f2_from_bf16x2(gw[q])));
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) xw[q] = bf16x2_from_f2(f2_mul(f2_from_bf16x2(xw[q]), r2));
       }
-      v[j] = pack8(f);
+      v[j] = make_uint4(xw[0], xw[1], xw[2], xw[3]);
     }
   if (!is_v) {
     // rotate_half partner of vector vi is vi + nv/2 (first half) or vi - nv/2.
@@ -328,17 +333,22 @@ __global__ void __launch_bounds__(32 * kGlueWarps) qkv_rows_kernel(const QkvArgs
         const int vi = lane + 32 * j;
         const int c = vi * 8;
         const bool first = vi < nv / 2;
-        float x[8], px[8], cs[8], sn[8];
-        unpack8(v[j], x);
-        unpack8(p[j], px);
-        unpack8(ld16(cr + c), cs);
-        unpack8(ld16(sr + c), sn);
+        // bf16(bf16(x * cos) + bf16(rotate_half(x) * sin)), two elements per packed step;
+        // the first half's partner is negated by its sign bits (exact, as -x).
+        const uint4 cv = ld16(cr + c), sv = ld16(sr + c);
+        const uint32_t xw[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+        const uint32_t pw[4] = {p[j].x, p[j].y, p[j].z, p[j].w};
+        const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
+        const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+        const uint32_t flip = first ? 0x80008000u : 0u;
+        uint32_t ow[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float rot = first ? -px[e] : px[e];
-          x[e] = rbf16(__fadd_rn(rbf16(__fmul_rn(x[e], cs[e])), rbf16(__fmul_rn(rot, sn[e]))));
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t xc = bf16x2_from_f2(f2_mul(f2_from_bf16x2(xw[q]), f2_from_bf16x2(cw[q])));
+          const uint32_t rs = bf16x2_from_f2(f2_mul(f2_from_bf16x2(pw[q] ^ flip), f2_from_bf16x2(sw[q])));
+          ow[q] = bf16x2_from_f2(f2_add(f2_from_bf16x2(xc), f2_from_bf16x2(rs)));
         }
-        v[j] = pack8(x);
+        v[j] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
       }
   }
   __nv_bfloat16* orow = a.out + static_cast<int64_t>(head) * a.ld_head + static_cast<int64_t>(tok) * a.ld_tok;
