@@ -186,38 +186,19 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
   }
   if (MODE == kGluePost1 && a.q == nullptr) return;  // k_ple_out alone: h only
   // _quant of the row.
-  float amax = 0.f;
+  uint32_t m2 = 0u;  // two bf16 lanes of max |x|
 #pragma unroll
   for (int i = 0; i < kMax; ++i)
-    if (lane + 32 * i < nv) {
-      float x[8];
-      unpack8(v[i], x);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(x[e]));
-    }
-  amax = warp_max(amax);
+    if (lane + 32 * i < nv) m2 = bf16x2_absmax8(v[i], m2);
+  const float amax = warp_max(bf16x2_max_lanes(m2));
   const float sc = __fdiv_rn(fmaxf(amax, 1e-8f), 127.f);
   const float rc = __frcp_rn(sc);
   if (lane == 0) a.s[row] = sc;
-  const uint64_t rc2 = f2_pack(rc, rc), nsc2 = f2_pack(-sc, -sc);
 #pragma unroll
   for (int i = 0; i < kMax; ++i) {
     const int vi = lane + 32 * i;
-    if (vi < nv) {
-      const uint32_t xw[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-      int8_t out[8];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        // div_rn_by on a pair: t = x * r, then t + r * (x - s * t), each step rounded once.
-        const uint64_t x2 = f2_from_bf16x2(xw[j]);
-        const uint64_t t2 = f2_mul(x2, rc2);
-        float q0, q1;
-        f2_unpack(f2_fma(f2_fma(nsc2, t2, x2), rc2, t2), q0, q1);
-        out[2 * j] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(q0), -127.f), 127.f)));
-        out[2 * j + 1] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(q1), -127.f), 127.f)));
-      }
-      store_q<8>(a.q + static_cast<int64_t>(row) * a.ldq + vi * 8, out);
-    }
+    if (vi < nv)
+      *reinterpret_cast<uint2*>(a.q + static_cast<int64_t>(row) * a.ldq + vi * 8) = quant8_bf16_codes(v[i], sc, rc);
   }
 }
 

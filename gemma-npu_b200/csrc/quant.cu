@@ -35,23 +35,34 @@ __global__ void __launch_bounds__(kQuantThreads)
   int8_t* qr = q + static_cast<int64_t>(row) * ldq;
   const int nvec = k / VEC;
 
+  constexpr bool kBf16x8 = std::is_same<T, __nv_bfloat16>::value && VEC == 8;
   Vec<T, VEC> held[kQuantMaxVecs];
   float amax = 0.f;
+  uint32_t m2 = 0u;  // bf16 rows: two bf16 lanes of max |x|
 #pragma unroll
   for (int i = 0; i < kQuantMaxVecs; ++i) {
     const int vi = threadIdx.x + i * kQuantThreads;
     if (vi < nvec) {
       held[i] = load_vec<T, VEC>(xr + static_cast<int64_t>(vi) * VEC);
+      if constexpr (kBf16x8) {
+        m2 = bf16x2_absmax8(*reinterpret_cast<const uint4*>(held[i].v), m2);
+      } else {
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) amax = fmaxf(amax, fabsf(to_f32(held[i].v[e])));
+        for (int e = 0; e < VEC; ++e) amax = fmaxf(amax, fabsf(to_f32(held[i].v[e])));
+      }
     }
   }
   // Rows longer than the register window: stream the rest (read again in pass 2).
   for (int vi = threadIdx.x + kQuantMaxVecs * kQuantThreads; vi < nvec; vi += kQuantThreads) {
     const Vec<T, VEC> v = load_vec<T, VEC>(xr + static_cast<int64_t>(vi) * VEC);
+    if constexpr (kBf16x8) {
+      m2 = bf16x2_absmax8(*reinterpret_cast<const uint4*>(v.v), m2);
+    } else {
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) amax = fmaxf(amax, fabsf(to_f32(v.v[e])));
+      for (int e = 0; e < VEC; ++e) amax = fmaxf(amax, fabsf(to_f32(v.v[e])));
+    }
   }
+  if constexpr (kBf16x8) amax = bf16x2_max_lanes(m2);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
@@ -67,26 +78,28 @@ __global__ void __launch_bounds__(kQuantThreads)
   for (int i = 0; i < kQuantMaxVecs; ++i) {
     const int vi = threadIdx.x + i * kQuantThreads;
     if (vi < nvec) {
-      int8_t out[VEC];
-      if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
-        quant8_bf16(*reinterpret_cast<const uint4*>(held[i].v), sc, rc, out);
+      if constexpr (kBf16x8) {
+        *reinterpret_cast<uint2*>(qr + static_cast<int64_t>(vi) * VEC) =
+            quant8_bf16_codes(*reinterpret_cast<const uint4*>(held[i].v), sc, rc);
       } else {
+        int8_t out[VEC];
 #pragma unroll
         for (int e = 0; e < VEC; ++e) out[e] = quant_one(to_f32(held[i].v[e]), sc, rc);
+        store_q<VEC>(qr + static_cast<int64_t>(vi) * VEC, out);
       }
-      store_q<VEC>(qr + static_cast<int64_t>(vi) * VEC, out);
     }
   }
   for (int vi = threadIdx.x + kQuantMaxVecs * kQuantThreads; vi < nvec; vi += kQuantThreads) {
     const Vec<T, VEC> v = load_vec<T, VEC>(xr + static_cast<int64_t>(vi) * VEC);
-    int8_t out[VEC];
-    if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
-      quant8_bf16(*reinterpret_cast<const uint4*>(v.v), sc, rc, out);
+    if constexpr (kBf16x8) {
+      *reinterpret_cast<uint2*>(qr + static_cast<int64_t>(vi) * VEC) =
+          quant8_bf16_codes(*reinterpret_cast<const uint4*>(v.v), sc, rc);
     } else {
+      int8_t out[VEC];
 #pragma unroll
       for (int e = 0; e < VEC; ++e) out[e] = quant_one(to_f32(v.v[e]), sc, rc);
+      store_q<VEC>(qr + static_cast<int64_t>(vi) * VEC, out);
     }
-    store_q<VEC>(qr + static_cast<int64_t>(vi) * VEC, out);
   }
 }
 
@@ -152,17 +165,13 @@ __global__ void __launch_bounds__(kQuantThreads)
   for (int i = 0; i < kQuantMaxVecs; ++i) {
     const int vi = threadIdx.x + i * kQuantThreads;
     if (vi < nvec) {
-      int8_t out[8];
-      quant8_bf16(*reinterpret_cast<const uint4*>(held[i].v), sc, rc, out);
-      store_q<8>(qr + vi * 8, out);
+      *reinterpret_cast<uint2*>(qr + vi * 8) = quant8_bf16_codes(*reinterpret_cast<const uint4*>(held[i].v), sc, rc);
     }
   }
   // Rows longer than the register window: the rest streams through.
   for (int vi = threadIdx.x + kQuantMaxVecs * kQuantThreads; vi < nvec; vi += kQuantThreads) {
     const Vec<__nv_bfloat16, 8> v = load_vec<__nv_bfloat16, 8>(yr + vi * 8);
-    int8_t out[8];
-    quant8_bf16(*reinterpret_cast<const uint4*>(v.v), sc, rc, out);
-    store_q<8>(qr + vi * 8, out);
+    *reinterpret_cast<uint2*>(qr + vi * 8) = quant8_bf16_codes(*reinterpret_cast<const uint4*>(v.v), sc, rc);
   }
 }
 

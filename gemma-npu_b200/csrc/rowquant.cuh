@@ -34,20 +34,41 @@ __device__ __forceinline__ int8_t quant_one(float v, float s, float r) {
   return static_cast<int8_t>(static_cast<int>(q));
 }
 
-// quant_one on the eight bf16 values of a 16-byte vector, two at a time: the division
-// steps on packed f32x2 instructions (the same IEEE operations, so the same codes).
-__device__ __forceinline__ void quant8_bf16(const uint4& v, float s, float r, int8_t (&out)[8]) {
+// quant_one of the eight bf16 values of a 16-byte vector, packed little-endian in two
+// words.  The division steps run two values at a time on packed f32x2 instructions (the
+// same IEEE operations), and rint(q) is taken from RN(q + 1.5 * 2^23): |x| <= absmax and
+// s = RN(max(absmax, 1e-8) / 127) bound |q| by 127 plus one ulp, so the sum lies in
+// [2^23, 2^24), where the fp32 grid is the integers; its rounding is rint's (nearest, ties
+// to even), the clamp to +-127 never binds, and the low byte of its bits is the code in
+// two's complement.  Byte permutes gather the four low bytes of a word.
+__device__ __forceinline__ uint2 quant8_bf16_codes(const uint4& v, float s, float r) {
   const uint64_t r2 = f2_pack(r, r), ns2 = f2_pack(-s, -s);
+  const uint64_t magic2 = f2_pack(12582912.f, 12582912.f);
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t b[8];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint64_t x2 = f2_from_bf16x2(w[j]);
     const uint64_t t2 = f2_mul(x2, r2);
-    float q0, q1;
-    f2_unpack(f2_fma(f2_fma(ns2, t2, x2), r2, t2), q0, q1);
-    out[2 * j] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(q0), -127.f), 127.f)));
-    out[2 * j + 1] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(q1), -127.f), 127.f)));
+    float lo, hi;
+    f2_unpack(f2_add(f2_fma(f2_fma(ns2, t2, x2), r2, t2), magic2), lo, hi);
+    b[2 * j] = __float_as_uint(lo);
+    b[2 * j + 1] = __float_as_uint(hi);
   }
+  return make_uint2(__byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410),
+                    __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410));
+}
+
+// max |x| over eight packed bf16 values folded into `m2` (two bf16 lanes, sign bits
+// cleared); fmaxf(lo, hi) of the result is the fp32 absmax.  The bf16 max is exact.
+__device__ __forceinline__ uint32_t bf16x2_absmax8(const uint4& v, uint32_t m2) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) asm("max.bf16x2 %0, %0, %1;" : "+r"(m2) : "r"(w[j] & 0x7FFF7FFFu));
+  return m2;
+}
+__device__ __forceinline__ float bf16x2_max_lanes(uint32_t m2) {
+  return fmaxf(__uint_as_float(m2 << 16), __uint_as_float(m2 & 0xFFFF0000u));
 }
 
 // VEC elements of T per 16-byte vector (VEC == 1: unaligned scalar path).
