@@ -378,6 +378,22 @@ __device__ __forceinline__ uint32_t bf16x2_from_f2(uint64_t v) {
   return *reinterpret_cast<uint32_t*>(&p);
 }
 
+// Packed bf16 pair arithmetic, each lane rounded once to bf16 (nearest even).  On bf16
+// operands this is exactly what eager torch computes for bf16 tensors, the fp32 result
+// rounded to bf16: fp32 holds the product of two bf16 exactly, and for a sum its 24 bits
+// (>= 2 * 8 + 2) make the double rounding innocuous (S. A. Figueroa, "When is double
+// rounding innocuous?", ACM SIGNUM Newsletter 30(3), 1995).
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 // ---------------------------------------------------------------- gelu (tanh form)
 constexpr float kGeluBeta = 0.7978845608028654f;  // sqrt(2 / pi)
 constexpr float kGeluKappa = 0.044715f;

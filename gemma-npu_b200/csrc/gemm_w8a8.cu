@@ -260,11 +260,12 @@ __device__ __forceinline__ void gelu_up_scales16(const GemmArgs& a, int gcol0, f
 }
 
 // 16 gate and 16 up accumulators with their scales -> 8 words of packed bf16
-// a = bf16(gelu(_deq(gate)) * _deq(up)); `amax` accumulates max |a|.  Two columns at a
-// time on packed f32x2 instructions, in gelu_tanh_bf16's operation order.
+// a = bf16(gelu(_deq(gate)) * _deq(up)); `amax2` accumulates max |a| in two bf16 lanes.
+// Two columns at a time on packed f32x2 instructions, in gelu_tanh_bf16's operation
+// order; the product of the two bf16 factors is one packed bf16 multiply.
 __device__ __forceinline__ void gelu_up_pack16(const uint32_t (&rg)[16], const uint32_t (&ru)[16],
                                                const float (&wg)[16], const float (&wu)[16], float sxr,
-                                               uint32_t* out, float& amax) {
+                                               uint32_t* out, uint32_t& amax2) {
   const uint64_t sx2 = f2_pack(sxr, sxr);
   const uint64_t kappa2 = f2_pack(kGeluKappa, kGeluKappa), beta2 = f2_pack(kGeluBeta, kGeluBeta);
   const uint64_t m2l2e2 = f2_pack(-2.8853900817779268f, -2.8853900817779268f);  // -2 log2(e)
@@ -276,7 +277,7 @@ __device__ __forceinline__ void gelu_up_pack16(const uint32_t (&rg)[16], const u
     const uint64_t gi = f2_pack(__int2float_rn(static_cast<int>(rg[c])), __int2float_rn(static_cast<int>(rg[c + 1])));
     const uint64_t ui = f2_pack(__int2float_rn(static_cast<int>(ru[c])), __int2float_rn(static_cast<int>(ru[c + 1])));
     const uint64_t g = f2_round_bf16(f2_mul(f2_mul(gi, sx2), f2_pack(wg[c], wg[c + 1])), bits);
-    const uint64_t u = f2_round_bf16(f2_mul(f2_mul(ui, sx2), f2_pack(wu[c], wu[c + 1])), bits);
+    const uint32_t ub = bf16x2_from_f2(f2_mul(f2_mul(ui, sx2), f2_pack(wu[c], wu[c + 1])));
     // gelu_tanh_bf16 on both: 1 + tanh(z) = 2 / (1 + e^(-2z)).
     const uint64_t g3 = f2_mul(f2_mul(g, g), g);
     const uint64_t inner = f2_mul(beta2, f2_add(g, f2_mul(kappa2, g3)));
@@ -289,12 +290,9 @@ __device__ __forceinline__ void gelu_up_pack16(const uint32_t (&rg)[16], const u
     f2_unpack(f2_add(one2, f2_pack(e0, e1)), d0, d1);
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d0));
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d1));
-    const uint64_t gel = f2_round_bf16(f2_mul(f2_mul(half2, g), f2_mul(two2, f2_pack(r0, r1))), bits);
-    const uint64_t av = f2_round_bf16(f2_mul(gel, u), bits);
-    float v0, v1;
-    f2_unpack(av, v0, v1);
-    amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
-    out[j] = bits;
+    const uint32_t gb = bf16x2_from_f2(f2_mul(f2_mul(half2, g), f2_mul(two2, f2_pack(r0, r1))));
+    out[j] = bf16x2_mul(gb, ub);
+    asm("max.bf16x2 %0, %0, %1;" : "+r"(amax2) : "r"(out[j] & 0x7FFF7FFFu));
   }
 }
 
@@ -354,7 +352,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmArgs& args, const CUtens
     // 256 accumulator columns = 128 gate + 128 up -> output columns col_base / 2 ..+128;
     // this warp (`part` of the four of its lane quarter) finishes output columns
     // 32 part .. 32 part + 31 of its 32 rows, 16 at a time.
-    float amax = 0.f;
+    uint32_t amax2 = 0u;  // max |a| in two bf16 lanes
     {
       uint32_t v[16];
 #pragma unroll
@@ -371,11 +369,12 @@ __device__ __forceinline__ void epilogue_rows(const GemmArgs& args, const CUtens
           __syncwarp();
           if (lane == 0) release();
         }
-        gelu_up_pack16(rg, ru, wg, wu, sxr, v + h * 8, amax);
+        gelu_up_pack16(rg, ru, wg, wu, sxr, v + h * 8, amax2);
       }
       (void)sbuf;
       put_box64(tm_c, v, stage_base, lane, col_base / 2 + part * 32, row0);
     }
+    const float amax = fmaxf(__uint_as_float(amax2 << 16), __uint_as_float(amax2 & 0xFFFF0000u));
     if (row < args.m) atomicMax(reinterpret_cast<int*>(args.row_absmax) + row, __float_as_int(amax));
     return;
   }

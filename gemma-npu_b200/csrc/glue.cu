@@ -90,8 +90,10 @@ __device__ __forceinline__ float rms_factor(const uint4 (&v)[NV], int nv, int la
     if (lane + 32 * i < nv) {
       float f[8];
       unpack8(v[i], f);
+      // fma(x, x, ss) = ss + x * x, one rounding fewer: the square of a bf16 is exact in
+      // fp32 (below 2^-63 it can round, but then eps decides the factor anyway).
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(f[e], f[e]));
+      for (int e = 0; e < 8; ++e) ss = __fmaf_rn(f[e], f[e], ss);
     }
   const float ms = __fdiv_rn(warp_sum(ss), static_cast<float>(n));
   return __frsqrt_rn(__fadd_rn(ms, eps));
@@ -156,7 +158,7 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
           if constexpr (MODE == kGlueIn) {
             xw[j] = t;
           } else {
-            uint32_t h = bf16x2_from_f2(f2_add(f2_from_bf16x2(rw[j]), f2_from_bf16x2(t)));
+            uint32_t h = bf16x2_add(rw[j], t);  // bf16(res + t)
             if (a.scalar != 1.f) h = bf16x2_from_f2(f2_mul(f2_from_bf16x2(h), sc2));
             xw[j] = h;
           }
@@ -270,7 +272,7 @@ __global__ void __launch_bounds__(32 * kGlueWarps) qkv_rows_kernel(const QkvArgs
       float f[8];
       unpack8(v[j], f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(f[e], f[e]));
+      for (int e = 0; e < 8; ++e) ss = __fmaf_rn(f[e], f[e], ss);  // = ss + x * x, as in rms_factor
     }
   const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(ss), static_cast<float>(a.d)), a.eps));
   // bf16(_rms(x, w)) of this lane's vectors.
@@ -314,8 +316,9 @@ __global__ void __launch_bounds__(32 * kGlueWarps) qkv_rows_kernel(const QkvArgs
         const int vi = lane + 32 * j;
         const int c = vi * 8;
         const bool first = vi < nv / 2;
-        // bf16(bf16(x * cos) + bf16(rotate_half(x) * sin)), two elements per packed step;
-        // the first half's partner is negated by its sign bits (exact, as -x).
+        // bf16(bf16(x * cos) + bf16(rotate_half(x) * sin)) on packed bf16 pairs (each step
+        // rounded once, as eager torch's bf16 ops); the first half's partner is negated by
+        // its sign bits (exact, as -x).
         const uint4 cv = ld16(cr + c), sv = ld16(sr + c);
         const uint32_t xw[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
         const uint32_t pw[4] = {p[j].x, p[j].y, p[j].z, p[j].w};
@@ -324,11 +327,8 @@ __global__ void __launch_bounds__(32 * kGlueWarps) qkv_rows_kernel(const QkvArgs
         const uint32_t flip = first ? 0x80008000u : 0u;
         uint32_t ow[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t xc = bf16x2_from_f2(f2_mul(f2_from_bf16x2(xw[q]), f2_from_bf16x2(cw[q])));
-          const uint32_t rs = bf16x2_from_f2(f2_mul(f2_from_bf16x2(pw[q] ^ flip), f2_from_bf16x2(sw[q])));
-          ow[q] = bf16x2_from_f2(f2_add(f2_from_bf16x2(xc), f2_from_bf16x2(rs)));
-        }
+        for (int q = 0; q < 4; ++q)
+          ow[q] = bf16x2_add(bf16x2_mul(xw[q], cw[q]), bf16x2_mul(pw[q] ^ flip, sw[q]));
         v[j] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
       }
   }
