@@ -474,7 +474,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       // memory, then the int8 codes with _quant's scale and rounding.
       const float inv = lt > 0.f ? 1.f / lt : 0.f;
       uint32_t pw[64];  // this thread's 128 bf16 output values, packed pairs
-      float am = 0.f;
+      uint32_t am2 = 0u;  // max |.| in two bf16 lanes
       if (good) {
         tc_fence_after();
 #pragma unroll
@@ -486,11 +486,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           for (int e = 0; e < 16; ++e) {
             const float v0 = __uint_as_float(ov[2 * e]) * inv, v1 = __uint_as_float(ov[2 * e + 1]) * inv;
             pw[16 * c + e] = pack_bf16x2(v0, v1);
-            const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&pw[16 * c + e]);
-            am = fmaxf(am, fmaxf(fabsf(__low2float(h2)), fabsf(__high2float(h2))));
           }
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            am2 = bf16x2_absmax8(make_uint4(pw[16 * c + 4 * e], pw[16 * c + 4 * e + 1], pw[16 * c + 4 * e + 2],
+                                            pw[16 * c + 4 * e + 3]),
+                                 am2);
         }
       }
+      const float am = bf16x2_max_lanes(am2);
       const int qi = r % qb_rows, slot = (r / qb_rows) * 2 + hv;  // token, (head, half)
       softmax_sync();  // every row sum above is read before xch is reused
       xch[qi * 2 * pk + slot] = am;
@@ -504,19 +508,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         int8_t* dst = a.q + static_cast<int64_t>(qpos) * a.ldq + head * kTcDV + 128 * hv;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {  // 16 values -> 16 bytes
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            int8_t b4[4];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&pw[8 * j + 2 * e + u]);
-              b4[2 * u] = quant_one(__low2float(h2), sc, rc);
-              b4[2 * u + 1] = quant_one(__high2float(h2), sc, rc);
-            }
-            w[e] = pack4(b4);
-          }
-          *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(w[0], w[1], w[2], w[3]);
+          const uint2 lo = quant8_bf16_codes(make_uint4(pw[8 * j], pw[8 * j + 1], pw[8 * j + 2], pw[8 * j + 3]), sc, rc);
+          const uint2 hi =
+              quant8_bf16_codes(make_uint4(pw[8 * j + 4], pw[8 * j + 5], pw[8 * j + 6], pw[8 * j + 7]), sc, rc);
+          *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(lo.x, lo.y, hi.x, hi.y);
         }
         if (slot == 0) a.s[qpos] = sc;
       }
