@@ -421,6 +421,22 @@ __device__ __forceinline__ float gelu_tanh_bf16(float g) {
   return round_bf16(__fmul_rn(__fmul_rn(0.5f, g), one_plus_tanh(inner)));
 }
 
+// gelu_tanh_bf16 of a packed bf16 pair, returned packed: the same operations in the same
+// order, two values per packed f32x2 step (each lane one IEEE fp32 operation).
+__device__ __forceinline__ uint32_t gelu_tanh_bf16x2(uint32_t gbits) {
+  const uint64_t g = f2_from_bf16x2(gbits);
+  const uint64_t g3 = f2_mul(f2_mul(g, g), g);
+  const uint64_t inner = f2_mul(f2_pack(kGeluBeta, kGeluBeta), f2_add(g, f2_mul(f2_pack(kGeluKappa, kGeluKappa), g3)));
+  float a0, a1, e0, e1, d0, d1, r0, r1;
+  f2_unpack(f2_mul(inner, f2_pack(-2.8853900817779268f, -2.8853900817779268f)), a0, a1);  // -2 log2(e)
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(a0));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(a1));
+  f2_unpack(f2_add(f2_pack(1.f, 1.f), f2_pack(e0, e1)), d0, d1);
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d0));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(d1));
+  return bf16x2_from_f2(f2_mul(f2_mul(f2_pack(0.5f, 0.5f), g), f2_mul(f2_pack(2.f, 2.f), f2_pack(r0, r1))));
+}
+
 }  // namespace w8
 
 // ---------------------------------------------------------------- host helpers

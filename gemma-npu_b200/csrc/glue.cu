@@ -125,12 +125,10 @@ __device__ __forceinline__ void glue_row(const GlueArgs& a, int row, int lane, i
     for (int i = 0; i < kMax; ++i) {
       const int vi = lane + 32 * i;
       if (vi < nv) {
-        float x[8], p[8];
-        unpack8(v[i], x);
-        unpack8(ld16(a.res + static_cast<int64_t>(row) * a.ldr + vi * 8), p);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = rbf16(__fmul_rn(gelu_tanh_bf16(x[e]), p[e]));
-        v[i] = pack8(x);
+        // bf16(gelu_tanh(x) * ple): the product of two bf16 values is one packed bf16 multiply.
+        const uint4 p = ld16(a.res + static_cast<int64_t>(row) * a.ldr + vi * 8);
+        v[i] = make_uint4(bf16x2_mul(gelu_tanh_bf16x2(v[i].x), p.x), bf16x2_mul(gelu_tanh_bf16x2(v[i].y), p.y),
+                          bf16x2_mul(gelu_tanh_bf16x2(v[i].z), p.z), bf16x2_mul(gelu_tanh_bf16x2(v[i].w), p.w));
       }
     }
   } else if constexpr (MODE != kGlueAttnOut) {
