@@ -72,6 +72,8 @@ SIGNATURES = {
     "w8_last_error": (ctypes.c_char_p, []),
     "w8_device_status": (_i, [_i]),
     "w8_abi_version": (_i, []),
+    "w8_gemm_last_schedule": (_i, [ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    "w8_inject_stream_k_stall": (_i, [_i, ctypes.c_uint64]),
     "w8_mm_i8": (_i, [_p, _i64, _p, _i64, _i, _p, _i64, _i64, _i64, _i64, _p]),
     "w8_mm_i8_ws": (_i, [_p, _i64, _p, _i64, _i, _p, _i64, _i64, _i64, _i64, _p, _i64, _p]),
     "w8_mm_i8_workspace_bytes": (_i64, [_i64, _i64, _i64]),
@@ -135,6 +137,13 @@ def check(status, fn):
 def call(name, *args):
     """Call a status-returning entry point and raise on failure."""
     check(getattr(lib(), name)(*args), name)
+
+
+def last_schedule():
+    """Schedule of the last GEMM this thread launched: dict(pair, stream_k, workers, tile_n)."""
+    sk, workers, tile_n = _i(), _i(), _i()
+    pair = lib().w8_gemm_last_schedule(ctypes.byref(sk), ctypes.byref(workers), ctypes.byref(tile_n))
+    return {"pair": bool(pair), "stream_k": bool(sk.value), "workers": workers.value, "tile_n": tile_n.value}
 
 
 def device_status(clear=True):

@@ -84,7 +84,7 @@ extern "C" const char* w8_status_string(int status) {
 
 extern "C" const char* w8_last_error(void) { return w8host::g_last_error; }
 
-extern "C" int w8_abi_version(void) { return (1 << 16) | 0; }
+extern "C" int w8_abi_version(void) { return (1 << 16) | 1; }
 
 extern "C" int w8_device_status(int clear) {
   int dev = 0;

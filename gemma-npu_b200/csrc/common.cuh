@@ -129,8 +129,10 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// Bounded spin until *p >= target (gpu-scope acquire); false (and a status) on timeout.
-__device__ __forceinline__ bool wait_counter_bounded(const uint32_t* p, uint32_t target, int* status) {
+// Bounded spin until *p >= target (gpu-scope acquire); false (and a status) after
+// `limit_ns` nanoseconds.
+__device__ __forceinline__ bool wait_counter_bounded(const uint32_t* p, uint32_t target, int* status,
+                                                     unsigned long long limit_ns = kWaitTimeoutNs) {
 #pragma unroll 1
   for (int i = 0; i < 64; ++i)
     if (ld_acquire_gpu(p) >= target) return true;
@@ -139,7 +141,7 @@ __device__ __forceinline__ bool wait_counter_bounded(const uint32_t* p, uint32_t
   while (true) {
     if (ld_acquire_gpu(p) >= target) return true;
     __nanosleep(64);
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
+    if (globaltimer() - t0 > limit_ns) {
       atomicExch(status, W8_ERR_DEVICE_TIMEOUT);
       return false;
     }

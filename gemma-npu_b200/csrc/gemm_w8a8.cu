@@ -56,6 +56,13 @@ namespace w8 {
 // Sticky device-side error word of the GEMM kernels (bounded-wait timeouts).
 __device__ int g_gemm_status = 0;
 
+// Fault injection for the tests of the bounded stream-K wait (w8_inject_stream_k_stall):
+// while g_sk_drop_signal is set, the owner of a split tile's last K-block stores its
+// partial sum but never signals, so the other contributors' wait runs out after
+// g_sk_wait_limit_ns (0: the default kWaitTimeoutNs).  Both are zero unless a test sets them.
+__device__ int g_sk_drop_signal = 0;
+__device__ unsigned long long g_sk_wait_limit_ns = 0;
+
 constexpr int kBM = 128;      // rows per CTA = TMEM lanes
 constexpr int kBN = 256;      // columns per tile = accumulator columns
 constexpr int kBK = 128;      // K elements (= bytes) per stage: one 128-byte swizzle row
@@ -434,7 +441,8 @@ __device__ __forceinline__ void epilogue_segment(const GemmArgs& args, const CUt
   if (split && !tail) {
     bool ok = true;
     if (lane == 0) {
-      ok = wait_counter_bounded(flag, static_cast<uint32_t>(warps_per_contrib), &g_gemm_status);
+      const unsigned long long limit = g_sk_wait_limit_ns ? g_sk_wait_limit_ns : kWaitTimeoutNs;
+      ok = wait_counter_bounded(flag, static_cast<uint32_t>(warps_per_contrib), &g_gemm_status, limit);
       fence_proxy_async_global();
     }
     __syncwarp();
@@ -446,7 +454,8 @@ __device__ __forceinline__ void epilogue_segment(const GemmArgs& args, const CUt
     bulk_wait_group<0>();  // this warp's boxes have landed in C
     __threadfence();
     const uint32_t total = static_cast<uint32_t>(warps_per_contrib * s.contributors);
-    if (atomicAdd(flag, 1u) == total - 1) atomicExch(flag, 0u);  // last one: reset for the next launch
+    if (!(tail && g_sk_drop_signal))
+      if (atomicAdd(flag, 1u) == total - 1) atomicExch(flag, 0u);  // last one: reset for the next launch
   }
   __syncwarp();
 }
@@ -969,6 +978,12 @@ static int launch_pdl(Kernel kern, int grid, int threads, int smem, cudaStream_t
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, args));
 }
 
+// Schedule of the last GEMM launched from this thread (w8_gemm_last_schedule).
+struct LastSchedule {
+  int stream_k, workers, tile_n, pair;
+};
+static thread_local LastSchedule g_last_schedule = {0, 0, 0, 0};
+
 // Stream-K pays off when whole tiles would leave the last wave of workers mostly idle
 // and each tile is long enough (K) that splitting it costs little next to its MMAs.
 static bool want_stream_k(int64_t tiles, int workers, int k) {
@@ -993,6 +1008,7 @@ static int launch_pair(int device, const CUtensorMap& ta, const CUtensorMap& tb,
     workers = static_cast<int>(units < cap ? units : cap);
     args.stream_k = 1;
   }
+  g_last_schedule = {args.stream_k, workers, BN, 1};
   return launch_pdl(kern, 2 * workers, w8::threads_for<EPI>(), w8::PairSmem::kAlloc, stream, ta, tb, tc, args);
 }
 
@@ -1015,13 +1031,15 @@ static int launch_single(int device, const CUtensorMap& ta, const CUtensorMap& t
     workers = static_cast<int>(units < sms ? units : sms);
     args.stream_k = 1;
   }
+  g_last_schedule = {args.stream_k, workers, w8::kBN, 0};
   return launch_pdl(kern, workers, w8::threads_for<EPI>(), w8::SingleSmem::kAlloc, stream, ta, tb, tc, args);
 }
 
 static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,
                        void* out, int64_t ldo, int out_elem, const float* sx, const float* sw,
                        int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
-                       cudaStream_t stream, int epi, float* row_absmax = nullptr) {
+                       cudaStream_t stream, int epi, float* row_absmax = nullptr,
+                       int64_t clear_words = 0) {
   // Output columns: the GEMM's N, or N / 2 for the gate/up glue (gelu(gate) * up).
   const int64_t n_out = epi == w8::kEpiGeluUp ? n / 2 : n;
   W8_CHECK_ARG(m >= 0 && n >= 0 && k >= 0, "negative size (m=%lld n=%lld k=%lld)", (long long)m,
@@ -1142,6 +1160,11 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
     args.tma_out = 1;
   }
 
+  // Counters the caller asked to have cleared (the allocation-free entry point's shared
+  // scratch) are cleared only now, after every argument check: a rejected call leaves
+  // them as they were.
+  if (clear_words > 0) W8_CUDA_TRY(cudaMemsetAsync(workspace, 0, static_cast<size_t>(clear_words) * 4, stream));
+
   const bool mn = b_layout == W8_B_KN;
   const bool i32 = epi == w8::kEpiI32;
   if (epi == w8::kEpiGeluUp)
@@ -1201,8 +1224,13 @@ static __device__ __align__(256) uint32_t g_noalloc_counters[kNoAllocMaxTiles];
 namespace w8host {
 // Device address of g_noalloc_counters, looked up once per device with that device current.
 static int noalloc_counters(int device, uint32_t** out) {
+  constexpr int kMaxDevices = 64;
   static std::mutex mu;
-  static uint32_t* ptr[64] = {};
+  static uint32_t* ptr[kMaxDevices] = {};
+  if (device < 0 || device >= kMaxDevices) {
+    set_error("w8_mm_i8_noalloc: device ordinal %d out of range", device);
+    return W8_ERR_UNSUPPORTED;
+  }
   std::lock_guard<std::mutex> lock(mu);
   if (ptr[device] == nullptr) {
     void* p = nullptr;
@@ -1233,11 +1261,30 @@ extern "C" int w8_mm_i8_noalloc(const int8_t* a, int64_t lda, const int8_t* b, i
   uint32_t* counters = nullptr;
   st = w8host::noalloc_counters(device, &counters);
   if (st != W8_OK) return st;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // The array keeps whatever the last call left: start this call's counters at zero.
-  W8_CUDA_TRY(cudaMemsetAsync(counters, 0, static_cast<size_t>(tiles) * 4, s));
+  // The array keeps whatever the last call left: gemm_common clears this call's counters,
+  // after its argument checks and just before the launch.
   return w8host::gemm_common(a, lda, b, ldb, b_layout, c, ldc, 4, nullptr, nullptr, m, n, k, counters,
-                             tiles * 4, s, w8::kEpiI32);
+                             tiles * 4, reinterpret_cast<cudaStream_t>(stream), w8::kEpiI32, nullptr, tiles);
+}
+
+extern "C" int w8_gemm_last_schedule(int* stream_k, int* workers, int* tile_n) {
+  const w8host::LastSchedule& s = w8host::g_last_schedule;
+  if (stream_k != nullptr) *stream_k = s.stream_k;
+  if (workers != nullptr) *workers = s.workers;
+  if (tile_n != nullptr) *tile_n = s.tile_n;
+  return s.pair;
+}
+
+extern "C" int w8_inject_stream_k_stall(int drop_signal, uint64_t wait_limit_ns) {
+  int device = 0;
+  int st = w8host::require_sm100(&device);
+  if (st != W8_OK) return st;
+  const int drop = drop_signal ? 1 : 0;
+  const unsigned long long limit = wait_limit_ns;
+  W8_CUDA_TRY(cudaDeviceSynchronize());  // no GEMM of this device is in flight while the hook changes
+  W8_CUDA_TRY(cudaMemcpyToSymbol(w8::g_sk_drop_signal, &drop, sizeof(int)));
+  W8_CUDA_TRY(cudaMemcpyToSymbol(w8::g_sk_wait_limit_ns, &limit, sizeof(limit)));
+  return W8_OK;
 }
 
 extern "C" int64_t w8_mm_i8_workspace_bytes(int64_t m, int64_t n, int64_t k) {

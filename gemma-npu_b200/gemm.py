@@ -25,6 +25,18 @@ What changes on B200:
   * the dequant of `matmul` is fused into the GEMM epilogue.
 Launches are stream-ordered on torch's current stream, so a returned view is
 ready for any later work on that stream.
+
+Where results live.  By default the slots are in HBM and `launch_slot` returns a CUDA
+int32 view: the caller's glue must then run on the GPU too (the `kernels` row kernels),
+because the reference's `k_*` glue is torch.compile'd for the CPU (pipeline.py:66-127)
+and handed CUDA tensors Inductor would generate GPU code of its own.  With
+`host_io=True` (to_b200(model, host_io=True)) the slots the caller reads and writes are
+pinned host memory, like the reference's host-visible NPU buffers: `stage` returns host
+rows, `launch_slot` copies them to HBM, runs the GEMM there, copies the int32 result
+back and returns it once it has landed, and `.sw` is a host fp32 tensor.  The
+reference's unchanged Prefill / Worker (pipeline.py:196-242) and its CPU glue then run
+as they are, with every GEMM on the GPU.  `matmul` and `Int8Head` follow the input:
+host rows in, host rows out.
 """
 import os
 import time
@@ -48,6 +60,19 @@ BACKENDS = ("b200", "npu", "cpu-int8", "cpu")
 
 def _round_up(v, m):
     return -(-v // m) * m
+
+
+def partition_rows(total, world, rank):
+    """Rows [r0, r1) of `total` that `rank` of `world` owns: an even split of concatenated
+    prompt rows, for running independent prompts' linears data-parallel over GPUs.
+
+    Every W8A8 linear is row-independent (per-token quant, per-row dequant), so the rows of
+    several prompts can be concatenated and cut anywhere; shares differ by at most one row.
+    The reference cuts one prompt into 512-row micro-batches instead (pipeline.py:328).
+    """
+    if world < 1 or not 0 <= rank < world or total < 0:
+        raise ValueError(f"bad partition: total={total} world={world} rank={rank}")
+    return total * rank // world, total * (rank + 1) // world
 
 
 def int8_linear(x2d, wq, sw):
@@ -76,8 +101,9 @@ class B200Gemm:
     a_flat = None  # int8 activations, MAX_ROWS x max K
     c_flat = None  # int32 results, MAX_ROWS x max N
     slots = []     # per pipelined micro-batch: (int8 activations, int32 results), SLOT_ROWS each
+    host_slots = []  # host_io: the same pairs in pinned host memory (what stage/launch_slot expose)
 
-    def __init__(self, linears, on_cpu=False, device=None):
+    def __init__(self, linears, on_cpu=False, device=None, host_io=False):
         ws = [l.weight.detach() for l in linears]
         dt = torch.bfloat16 if all(w.dtype == torch.bfloat16 for w in ws) else torch.float32
         w = torch.cat([x.to(dt) for x in ws])
@@ -88,8 +114,12 @@ class B200Gemm:
         self.n_pad = _round_up(self.N, 16)
         self.device = torch.device(device) if device is not None else torch.device(
             "cuda", torch.cuda.current_device())
-        self.w, self.sw = quantize_weight(w, self.device)  # int8 [N, K], fp32 [N]
-        self.sw_cpu = self.sw.to(torch.bfloat16)            # bf16 scales of the decode GEMV
+        self.w, self.sw_dev = quantize_weight(w, self.device)  # int8 [N, K], fp32 [N] in HBM
+        self.sw_gemv = self.sw_dev.to(torch.bfloat16)           # bf16 scales of the decode GEMV
+        self.host_io = bool(host_io)
+        # The scales where the caller's glue reads them (pipeline.py:262-308 passes G[..].sw).
+        self.sw = self.sw_dev.cpu() if self.host_io else self.sw_dev
+        self.sw_cpu = self.sw_gemv.cpu() if self.host_io else self.sw_gemv
         self.on_cpu = False                                   # everything runs on the GPU
         self.w_kn = None                                      # no separate [K, N] copy
         self.dtype = linears[0].weight.dtype
@@ -102,27 +132,46 @@ class B200Gemm:
         return self.w
 
     @classmethod
-    def allocate(cls, max_k, max_n, device=None):
-        """Resident staging buffers: one flat pair plus one (A, C) pair per micro-batch slot."""
+    def allocate(cls, max_k, max_n, device=None, host_io=False):
+        """Resident staging buffers: one flat pair plus one (A, C) pair per micro-batch slot
+        (with host_io, also a pinned host pair per slot)."""
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         max_n = _round_up(max_n, 16)
         cls.a_flat = torch.empty(MAX_ROWS * max_k, dtype=torch.int8, device=dev)
         cls.c_flat = torch.empty(MAX_ROWS * max_n, dtype=torch.int32, device=dev)
         cls.slots = [(torch.empty(SLOT_ROWS * max_k, dtype=torch.int8, device=dev),
                       torch.empty(SLOT_ROWS * max_n, dtype=torch.int32, device=dev)) for _ in range(N_SLOTS)]
+        cls.host_slots = [(torch.empty(SLOT_ROWS * max_k, dtype=torch.int8).pin_memory(),
+                           torch.empty(SLOT_ROWS * max_n, dtype=torch.int32).pin_memory())
+                          for _ in range(N_SLOTS)] if host_io else []
 
     def stage(self, slot, T):
-        """The slot's int8 activation rows [T, K], to be filled before launch_slot."""
+        """The slot's int8 activation rows [T, K], to be filled before launch_slot (host rows
+        with host_io)."""
         assert T <= SLOT_ROWS, f"micro-batch of {T} rows > {SLOT_ROWS}"
-        return self.slots[slot][0][: T * self.K].view(T, self.K)
+        slots = self.host_slots if self.host_io else self.slots
+        return slots[slot][0][: T * self.K].view(T, self.K)
 
     def launch_slot(self, T, slot):
-        """One GEMM over the slot's T staged rows; int32 [T, N], a view of the slot's results."""
+        """One GEMM over the slot's T staged rows; int32 [T, N], a view of the slot's results.
+
+        With host_io the staged host rows are copied to HBM first and the view is of the
+        pinned host results, complete when this returns (the reference's launch is
+        synchronous from its worker's view, pipeline.py:206-209)."""
         t = time.perf_counter()
         a_flat, c_flat = self.slots[slot]
         a = a_flat[: T * self.K].view(T, self.K)
         c = c_flat[: T * self.n_pad].view(T, self.n_pad)[:, : self.N]
-        kernels.mm_i8_nk(a, self.w, c)
+        if self.host_io:
+            ha, hc = self.host_slots[slot]
+            a.copy_(ha[: T * self.K].view(T, self.K), non_blocking=True)
+            kernels.mm_i8_nk(a, self.w, c)
+            out = hc[: T * self.n_pad].view(T, self.n_pad)
+            out.copy_(c_flat[: T * self.n_pad].view(T, self.n_pad), non_blocking=True)
+            torch.cuda.current_stream(self.device).synchronize()
+            c = out[:, : self.N]
+        else:
+            kernels.mm_i8_nk(a, self.w, c)
         dt = time.perf_counter() - t
         TIMES["launches"] += 1
         TIMES["gpu"] += dt
@@ -138,18 +187,23 @@ class B200Gemm:
         per-token quant, then one GEMM with the dequant fused into its epilogue.
         """
         T = x2d.shape[0]
+        on_host = not x2d.is_cuda  # host rows in, host rows out; the work runs in HBM
+        if on_host:
+            x2d = x2d.to(self.device, non_blocking=True)
         if T < GEMV_ROWS:
-            return int8_linear(x2d, self.w, self.sw_cpu).to(self.dtype)
+            y = int8_linear(x2d, self.w, self.sw_gemv).to(self.dtype)
+            return y.cpu() if on_host else y
         t = time.perf_counter()
         xq, sx = kernels.quant_rows(x2d.contiguous())
         t1 = time.perf_counter()
         TIMES["quant"] += t1 - t
-        y = kernels.gemm_dequant(xq, self.w, sx, self.sw)
+        y = kernels.gemm_dequant(xq, self.w, sx, self.sw_dev)
         TIMES["launches"] += 1
         TIMES["gpu"] += time.perf_counter() - t1
         st = BY_SHAPE.setdefault((self.N, self.K), [0, 0.0])
         st[0] += 1
-        return y if self.dtype == torch.bfloat16 else y.to(self.dtype)
+        y = y if self.dtype == torch.bfloat16 else y.to(self.dtype)
+        return y.cpu() if on_host else y
 
 
 # Kept for callers that import the reference's class name.
@@ -171,7 +225,10 @@ class Int8Head(torch.nn.Module):
 
     def forward(self, x):
         shape = x.shape[:-1]
-        return int8_linear(x.reshape(-1, x.shape[-1]), self.wq, self.sw).reshape(*shape, -1)
+        on_host = not x.is_cuda  # host rows in, host logits out; the GEMV runs in HBM
+        xd = x.to(self.wq.device, non_blocking=True) if on_host else x
+        y = int8_linear(xd.reshape(-1, x.shape[-1]), self.wq, self.sw).reshape(*shape, -1)
+        return y.cpu() if on_host else y
 
     def logits(self, h, cap=None, out=None):
         """fp32 logits of one hidden row with the final softcap fused (pipeline.py:335-338)."""
@@ -222,24 +279,25 @@ def layer_groups(lm):
     return groups, per_layer
 
 
-def to_b200(model, device=None):
+def to_b200(model, device=None, host_io=False):
     """Swap the text decoder's linears for resident W8A8 GEMMs on a B200 (to_npu, gemma_npu.py:207-241).
 
     Every group, the PLE gate/projection included, becomes a B200Gemm; the tied LM
     head gets a separate int8 copy (Int8Head).  Returns the list of groups and sets
-    model.layer_gemms like the reference.
+    model.layer_gemms like the reference.  host_io=True keeps the slots the caller reads
+    and writes in pinned host memory, for the reference's unchanged CPU pipeline.
     """
     lm = model.model.language_model
     groups, per_layer = layer_groups(lm)
     gemms = []
     for parent, names, linears in groups:
-        g = B200Gemm(linears, device=device)
+        g = B200Gemm(linears, device=device, host_io=host_io)
         g.name = "+".join(names)
         gemms.append(g)
         for i, (name, l) in enumerate(zip(names, linears)):
             setattr(parent, name, Slice(g, i, l.in_features, l.out_features))
     model.layer_gemms = [dict(zip(keys, gemms[6 * i: 6 * i + 6])) for i, keys in enumerate(per_layer)]
-    B200Gemm.allocate(max(g.K for g in gemms), max(g.n_pad for g in gemms), device=device)
+    B200Gemm.allocate(max(g.K for g in gemms), max(g.n_pad for g in gemms), device=device, host_io=host_io)
     model.lm_head = Int8Head(model.lm_head, device=device)
     return gemms
 
@@ -262,7 +320,7 @@ def add_backend_argument(parser):
     return parser
 
 
-def apply_backend(model, backend, device=None):
+def apply_backend(model, backend, device=None, host_io=False):
     """What load(backend) does to the model (gemma_npu.py:254) for the b200 backend.
 
     Returns the groups.  The npu / cpu-int8 / cpu backends are the reference's own
@@ -270,4 +328,4 @@ def apply_backend(model, backend, device=None):
     """
     if backend != "b200":
         raise ValueError(f"backend {backend!r} is served by the reference pipeline, not by this library")
-    return to_b200(model, device=device)
+    return to_b200(model, device=device, host_io=host_io)

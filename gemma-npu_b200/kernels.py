@@ -4,7 +4,7 @@ B200 counterpart of the reference's kernel module `npu_kernels.py` plus the
 quant/dequant glue of `pipeline.py` / `gemma_npu.py`:
 
     mm_i8(a, b, c) -> c          npu_kernels.py:59-64   (int8 [M,K] @ int8 [K,N] -> int32)
-    use_device()                 npu_kernels.py:25-26   (use_npu: per-thread device selection)
+    use_device() / use_npu()     npu_kernels.py:25-26   (per-thread device selection)
     quant_rows(x) -> (q, s)      pipeline.py:49-52, gemma_npu.py:37-42
     dequant(acc, sx, sw)         pipeline.py:55-57, gemma_npu.py:45-47
     int8_linear(x, wq, sw)       gemma_npu.py:155-156   (torch._weight_int8pack_mm)
@@ -43,6 +43,10 @@ def use_device(device=None):
     if device is None:
         device = torch.cuda.current_device()
     torch.cuda.set_device(device)
+
+
+# The reference's name for the same per-thread selection (npu_kernels.py:25-26).
+use_npu = use_device
 
 
 def _stream(t):

@@ -64,6 +64,22 @@ const char* w8_last_error(void);
 int w8_device_status(int clear);
 /* ABI version: (major << 16) | minor. */
 int w8_abi_version(void);
+/* Schedule of the last GEMM launched from the calling thread: *stream_k = 1 when its
+ * tiles were split over workers (stream-K), *workers = CTA pairs or CTAs launched,
+ * *tile_n = output columns per tile; returns 1 for the CTA-pair kernel, 0 for the
+ * single-CTA kernel (0 everywhere before the first launch).  A diagnostic of this
+ * library with no reference counterpart (the reference's grid is always (M/512, N/512),
+ * npu_kernels.py:63). */
+int w8_gemm_last_schedule(int* stream_k, int* workers, int* tile_n);
+/* Fault injection for tests of the bounded device-side wait, with no reference
+ * counterpart: while drop_signal != 0, the owner of a stream-K tile split between
+ * workers stores its partial sum but never signals the other contributors, whose
+ * counter wait then gives up after wait_limit_ns (0 = the default 2 s) and records
+ * W8_ERR_DEVICE_TIMEOUT for w8_device_status().  The kernel still ends and the context
+ * stays usable; the counters of that call are left non-zero (use a fresh workspace
+ * afterwards).  Synchronises the current device.  Production code never calls it;
+ * w8_inject_stream_k_stall(0, 0) restores normal operation. */
+int w8_inject_stream_k_stall(int drop_signal, uint64_t wait_limit_ns);
 
 /* ---- prefill GEMMs (tcgen05 kind::i8, int32 accumulators in TMEM) ----- */
 
@@ -102,7 +118,7 @@ int64_t w8_mm_i8_workspace_bytes(int64_t m, int64_t n, int64_t k);
  * W8_ERR_INVALID_ARG.  The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress, with that device current), so make that first call before any
  * stream capture.  Each call clears the counters it uses (an asynchronous memset on
- * `stream`) and allocates nothing.  All calls share the one array: calls that can
+ * `stream`, queued after the argument checks pass) and allocates nothing.  All calls share the one array: calls that can
  * overlap on the GPU (other streams, other threads) race and must be serialised by the
  * caller.  Same constraints and result bits as w8_mm_i8. */
 int w8_mm_i8_noalloc(const int8_t* a, int64_t lda, const int8_t* b, int64_t ldb, int b_layout,

@@ -1,6 +1,8 @@
 """Multi-rank host logic on CPU ranks (gloo, world size 2): the column-sharded LM head's
-shard ranges and logit all-gather reassemble the single-rank result, and a rank that
-fails before the collective ends the others' wait with an error instead of a hang."""
+shard ranges and logit all-gather reassemble the single-rank result, the row partition of
+config 4's concatenated prompts gives every row to exactly one rank with the same product,
+and a rank that fails before the collective ends the others' wait with an error instead of
+a hang."""
 import os
 import socket
 
@@ -101,3 +103,44 @@ def test_dead_rank_ends_the_collective_with_an_error():
     got = dict(q.get(timeout=5) for _ in range(2))
     assert got[1] == "raised"
     assert got[0].startswith("error:")
+
+
+def _rows_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        _import_pkg()
+        from gemma_npu_b200.gemm import partition_rows
+
+        lengths = [300, 17, 129, 64]  # prompts of uneven length, rows concatenated
+        total = sum(lengths)
+        rng = np.random.default_rng(1)
+        a = rng.integers(-127, 128, size=(total, 32), dtype=np.int8)
+        b = rng.integers(-127, 128, size=(32, 48), dtype=np.int8)
+        r0, r1 = partition_rows(total, world, rank)
+        # This rank's rows through the linear (the GPU GEMM's job on a B200: the oracle here).
+        mine = ref.int_mm(a[r0:r1], b)
+        sizes = [None] * world
+        dist.all_gather_object(sizes, (r0, r1))  # test-side reassembly only
+        parts = [None] * world
+        dist.all_gather_object(parts, mine)
+        covered = sorted(r for lo, hi in sizes for r in range(lo, hi)) == list(range(total))
+        balanced = max(hi - lo for lo, hi in sizes) - min(hi - lo for lo, hi in sizes) <= 1
+        same = np.array_equal(np.concatenate(parts), ref.int_mm(a, b))
+        q.put((rank, covered and balanced and same))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_partition_covers_rows_once_and_matches_one_rank():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rows_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    res = sorted(q.get(timeout=10) for _ in range(2))
+    assert all(ok for _, ok in res), res
+    assert all(p.exitcode == 0 for p in procs)
