@@ -311,6 +311,9 @@ def build_decode(w8, work, dev):
         h, hq, hsc, logits = head
         w8.lm_head_logits(h, hq, hsc, SOFTCAP, out=logits, argmax=True)  # + the greedy token
 
+    best = torch.zeros((1,), dtype=torch.int64, device=dev)
+    fused = w8.GemvChain([(x[0], wq, s, y[0]) for x, wq, s, y in chain] + [head + (SOFTCAP, best)])
+
     side = [torch.cuda.Stream(device=dev) for _ in range(4)]
     layer_bytes = sum(wq.numel() + 2 * wq.shape[0] + 2 * x.numel() + 2 * y.numel() for x, wq, _, y in chain)
 
@@ -332,7 +335,7 @@ def build_decode(w8, work, dev):
         for ev in joins:
             cur.wait_event(ev)
 
-    return step, nbytes, len(chain) + 1, head, (step_independent, layer_bytes, len(chain))
+    return step, nbytes, len(chain) + 1, head, (step_independent, layer_bytes, len(chain)), fused
 
 
 def prompt_lengths(count=8, seed=0, lo=200, hi=3700):
@@ -594,15 +597,19 @@ def fused_layer(w8, dev, stream, m, steps, warmup, world, layers=35):
             "unfused": "int32 GEMMs + dequant / quant kernels + the reference's glue as torch ops on the same GPU"}
 
 
-def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35):
+def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35, kv_shared=0):
     """One prompt through every decoder layer's linear set, glue and attention on the GPU,
-    the layer body of pipeline.py:262-310: k_in, qkv GEMM + k_qkv, attention, k_attn_out,
-    o GEMM + k_post_attn, gate/up GEMM + k_gelu, down GEMM + k_post_ff, PLE gate GEMM
-    (1536 -> 256) + k_ple_gate, PLE projection GEMM (256 -> 1536) + k_ple_out.  Gemma E2B
-    attention layout: every 5th layer full causal with head_dim 512 (qkv 5120 x 1536, o
-    1536 x 4096), the others sliding window 512 with head_dim 256; 8 query heads on 1 KV
-    head; no KV sharing.  Random weights and per-layer inputs; the residual stream is
-    carried from layer to layer, and k_ple_out shares its row pass with the next k_in."""
+    the layer body of pipeline.py:262-310: k_in, qkv GEMM + k_qkv (one kernel for head_dim
+    256), attention, k_attn_out, o GEMM + k_post_attn, gate/up GEMM + k_gelu, down GEMM +
+    k_post_ff, PLE gate GEMM (1536 -> 256) + k_ple_gate, PLE projection GEMM (256 -> 1536) +
+    k_ple_out.  Gemma E2B attention layout: every 5th layer full causal with head_dim 512
+    (qkv 5120 x 1536, o 1536 x 4096), the others sliding window 512 with head_dim 256; 8
+    query heads on 1 KV head.  The last `kv_shared` layers are KV-shared as the reference
+    groups them (gemma_npu.py:214-216, pipeline.py:258-281): a q-only qkv GEMM, the keys and
+    values of the last unshared layer of the same attention type, and a double-wide MLP
+    (gate/up 24576 x 1536, down 1536 x 12288).  Random weights and per-layer inputs; the
+    residual stream is carried from layer to layer, and k_ple_out shares its row pass with
+    the next k_in."""
     eps, nh, kv, hid = 1e-6, 8, 1, 1536
     g = torch.Generator(device=dev).manual_seed(91)
 
@@ -619,23 +626,38 @@ def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35):
 
     tables = {256: rope(256, 1e4), 512: rope(512, 1e6)}
     L = []
+    first_shared = layers - kv_shared
     for i in range(layers):
         d, win = (512, 0) if i % 5 == 4 else (256, 512)
-        L.append(dict(d=d, win=win, qkv=wq((nh + 2 * kv) * d, hid), o=wq(hid, nh * d),
-                      gup=w8.pack_gelu_up(*wq(12288, hid)), dn=wq(hid, 6144), w_in=nw(hid), qn=nw(d), kn=nw(d),
+        shared = i >= first_shared
+        inter = 12288 if shared else 6144  # the double-wide MLP of KV-shared layers
+        L.append(dict(d=d, win=win, shared=shared, qkv=wq((nh if shared else nh + 2 * kv) * d, hid), o=wq(hid, nh * d),
+                      gup=w8.pack_gelu_up(*wq(2 * inter, hid)), dn=wq(hid, inter), w_in=nw(hid), qn=nw(d), kn=nw(d),
                       w_post=nw(hid), w_pre=nw(hid), w_pff=nw(hid), pg=wq(256, hid), pp=wq(hid, 256),
                       w_ple=nw(hid), scalar=float((0.5 + torch.rand((1,), device=dev, generator=g)).to(torch.bfloat16))))
     ple = torch.randn((m, layers, 256), device=dev, generator=g).to(torch.bfloat16)  # per-layer inputs
     h0 = torch.randn((m, hid), device=dev, generator=g).to(torch.bfloat16)
     h = torch.empty_like(h0)
 
+    # keys / values of the last unshared layer of each attention type, for the shared layers
+    kv_store = {d: torch.empty((2 * kv, m, d), dtype=torch.bfloat16, device=dev) for d in tables}
+
     def step():
         h.copy_(h0)
         xq, sx = w8.rms_quant(h, L[0]["w_in"], eps)
         for i, l in enumerate(L):
             d = l["d"]
-            y = w8.gemm_dequant(xq, l["qkv"][0], sx, l["qkv"][1])
-            q, k, v = w8.qkv_norm_rope(y, *tables[d], l["qn"], l["kn"], eps, nh, kv, d)
+            if l["shared"]:
+                q, _, _ = w8.gemm_qkv_norm_rope(xq, l["qkv"][0], sx, l["qkv"][1], *tables[d], l["qn"], None, eps, nh,
+                                                kv, d, shared=True)
+                k, v = kv_store[d][:kv], kv_store[d][kv:]
+            else:
+                q, k, v = w8.gemm_qkv_norm_rope(xq, l["qkv"][0], sx, l["qkv"][1], *tables[d], l["qn"], l["kn"], eps,
+                                                nh, kv, d)
+                if i < first_shared and any(x["d"] == d for x in L[first_shared:]) and \
+                        all(x["d"] != d for x in L[i + 1: first_shared]):
+                    kv_store[d][:kv].copy_(k)  # the last unshared layer of this type stores its K / V
+                    kv_store[d][kv:].copy_(v)
             xq, sx = w8.attention_quant(q, k, v, l["win"])  # attention + k_attn_out
             y = w8.gemm_dequant(xq, l["o"][0], sx, l["o"][1])
             _, xq, sx = w8.post_norm_quant(y, h, l["w_post"], l["w_pre"], eps, h=h)
@@ -660,7 +682,8 @@ def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35):
     return {"workload": f"{layers} decoder layers of one {m}-token prompt on the GPU (linear set + glue + attention; "
                         "every 5th layer full attention with head_dim 512, others sliding window 512 / head_dim 256; "
                         "PLE branch per layer (gate 1536->256 + k_ple_gate, projection 256->1536 + k_ple_out); "
-                        "no KV sharing)",
+                        + (f"the last {kv_shared} layers KV-shared: q-only qkv, shared K/V, double-wide MLP)"
+                           if kv_shared else "no KV sharing)"),
             "ms_per_prefill": ms, "linear_tops": linear_ops / (ms * 1e-3) / 1e12,
             "reference": "the reference keeps its NPU busy 2.38 s per 3658-token prefill (README.md:61-62), its CPU "
                          "attention on top"}
@@ -742,6 +765,42 @@ def sweep(w8, dev, stream, steps, warmup):
         del gr
         mix[name] = {"us_per_gemm": ms * 1e3 / len(ws), "tops": 2 * m * n * k * len(ws) / (ms * 1e-3) / 1e12}
     out["e2b_mix_m3658"] = mix
+    return out
+
+
+def gemm_table(w8, dev, stream, steps, warmup):
+    """Each config-1 shape at M = 3658 with this library's GEMM (w8_mm_i8_ws) and with
+    cuBLASLt (torch._int_mm, the library GEMM the kernel replaces), int32 out, both over
+    the same 4 rotating (activation, weight, output) sets so that every launch streams from
+    HBM; the results are compared bit for bit.  us per GEMM and TOPS per side."""
+    m = M_TOKENS
+    g = torch.Generator(device=dev).manual_seed(17)
+    out = {}
+    for name, n, k in LAYER_SHAPES + [PLE_SHAPE]:
+        sets = [(torch.randint(-128, 128, (m, k), dtype=torch.int8, device=dev, generator=g),
+                 torch.randint(-128, 128, (n, k), dtype=torch.int8, device=dev, generator=g),
+                 torch.empty((m, n), dtype=torch.int32, device=dev)) for _ in range(4)]
+        refs = [torch.empty((m, n), dtype=torch.int32, device=dev) for _ in range(4)]
+
+        def ours():
+            for a, w, c in sets:
+                w8.mm_i8_nk(a, w, c)
+
+        def cublas():
+            for (a, w, _), r in zip(sets, refs):
+                torch._int_mm(a, w.t(), out=r)
+
+        res = {}
+        for label, fn in (("b200", ours), ("cublaslt", cublas)):
+            gr = capture(fn, stream)
+            ms = timed(lambda: gr.replay(), steps, warmup, stream, 1) / steps
+            del gr
+            us = ms * 1e3 / len(sets)
+            res[label] = {"us": us, "tops": 2 * m * n * k / (us * 1e-6) / 1e12}
+        res["bit_exact"] = all(torch.equal(c, r) for (_, _, c), r in zip(sets, refs))
+        res["ratio_b200_over_cublaslt"] = res["cublaslt"]["us"] / res["b200"]["us"]
+        out[f"{name} {m}x{n}x{k}"] = res
+        del sets, refs
     return out
 
 
@@ -844,6 +903,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-step-s", type=float, default=4.0, help="CPU seconds per reference-arm step")
     ap.add_argument("--sweep", action="store_true", help="config 3: per-shape M sweep, padded vs unpadded (own JSON line)")
+    ap.add_argument("--gemm-table", action="store_true",
+                    help="each config-1 shape against cuBLASLt (torch._int_mm), bit-exact check (own JSON line)")
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 prompts / sharded LM head objects")
     ap.add_argument("--no-fused", action="store_true", help="skip the fused gate/up glue object")
     ap.add_argument("--no-attention", action="store_true", help="skip the prefill attention object")
@@ -875,6 +936,13 @@ def main():
             att = attention_bench(w8, dev, stream, args.m, args.steps, args.warmup, world)
             if rank == 0:
                 print(json.dumps({"attention": att}), flush=True)
+            return
+        if args.gemm_table:
+            table = gemm_table(w8, dev, stream, args.steps, args.warmup)
+            if rank == 0:
+                print(json.dumps({"metric": "W8A8 GEMM us per launch vs cuBLASLt, config-1 shapes @M=3658",
+                                  "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                                  "dtype": "int8", "data": "synthetic", "table": table}), flush=True)
             return
         if args.sweep:
             table = sweep(w8, dev, stream, args.steps, args.warmup)
@@ -947,7 +1015,16 @@ def main():
                                  "path": "gemma_npu_b200.mm_i8_nk per GEMM: pinned int8 activations H2D, int32 results "
                                          "D2H (pipeline.py's Prefill.gemm data flow); same three-stream pipeline"}
         if not args.no_decode and args.only is None:
-            step, nbytes, launches, head, (istep, ibytes, ilaunches) = build_decode(w8, work, dev)
+            step, nbytes, launches, head, (istep, ibytes, ilaunches), fused = build_decode(w8, work, dev)
+            # The decode step as one persistent kernel (w8_gemv_chain): the headline.  One
+            # launch per token, so it is timed as back-to-back launches on the stream.
+            with torch.cuda.stream(stream):
+                fused()
+            stream.synchronize()
+            cms = timed(fused, args.decode_steps, args.warmup, stream, world)
+            cper = cms / args.decode_steps
+            cgbs = nbytes / (cper * 1e-3) / 1e9
+            # The same chain as one kernel per GEMV in a graph (programmatic dependent launch).
             dgraph = capture(step, stream)
             dms = timed(lambda: dgraph.replay(), args.decode_steps, args.warmup, stream, world)
             per = dms / args.decode_steps
@@ -965,21 +1042,25 @@ def main():
             igbs = ibytes / (ims * 1e-3) / 1e9
             line["decode_gemv"] = {
                 "metric": "int8 GEMV GB/s, decode chain (config 2: 140 layer GEMVs + LM head 262144x1536, "
-                          "softcap and greedy argmax fused, one CUDA graph)",
-                "value": world * gbs, "unit": "GB/s", "ms_per_token": per, "bytes_per_token": nbytes,
-                "launches_per_token": launches,
-                "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                             "frac": gbs / pk["hbm_gbs"], "traffic": None,
+                          "softcap and greedy argmax fused, each GEMV ordered after the previous one)",
+                "value": world * cgbs, "unit": "GB/s", "ms_per_token": cper, "bytes_per_token": nbytes,
+                "launches_per_token": 1,
+                "path": "w8_gemv_chain: one persistent kernel, one CTA per SM; each SM streams its rows of every "
+                        "GEMV through shared memory, each GEMV's activation read waits on a grid-wide counter",
+                "roofline": {"bound": "hbm", "achieved": cgbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                             "frac": cgbs / pk["hbm_gbs"], "traffic": None,
                              "peak_note": f"{pk['source']} HBM copy bandwidth"},
+                "per_gemv_kernels": {"ms_per_token": per, "gbs": gbs, "frac": gbs / pk["hbm_gbs"],
+                                     "launches_per_token": launches,
+                                     "note": "the same chain as one int8_gemv_kernel per GEMV, captured in one "
+                                             "graph with programmatic dependent launch"},
                 "lm_head": {"us": hms * 1e3, "bytes": head_bytes, "gbs": head_gbs,
                             "frac": head_gbs / pk["hbm_gbs"],
-                            "note": "the 262144x1536 head GEMV alone (402.7 MB int8): the chain's per-layer "
-                                    "GEMVs (3.1-18.9 MB) are bound by launch and DRAM latency, not bandwidth"},
+                            "note": "the 262144x1536 head GEMV alone (402.7 MB int8)"},
                 "layer_gemvs_independent": {"us": ims * 1e3, "bytes": ibytes, "gbs": igbs,
                                             "frac": igbs / pk["hbm_gbs"], "launches": ilaunches,
                                             "note": "the chain's 140 layer GEMVs with no dependence between them, "
-                                                    "round-robin on 4 streams inside one graph so that they overlap: "
-                                                    "the kernel's streaming rate without the dependent-launch floor"}}
+                                                    "one kernel each, round-robin on 4 streams inside one graph"}}
         if not args.no_fused and args.only is None:
             line["fused_gelu_up"] = fused_gelu_up(w8, work, dev, stream, 10, 3, world)
             line["fused_layer"] = fused_layer(w8, dev, stream, args.m, 5, 3, world)
@@ -987,6 +1068,9 @@ def main():
         if not args.no_attention and args.only is None:
             line["attention"] = attention_bench(w8, dev, stream, args.m, 10, 3, world)
             line["prefill_gpu"] = prefill_gpu(w8, dev, stream, args.m, 3, 3, world)
+            # Gemma E2B's count of KV-shared layers comes from its config.json, absent here:
+            # 20 of 35 is an assumption that exercises the shared-layer path at scale.
+            line["prefill_gpu_kv_shared"] = prefill_gpu(w8, dev, stream, args.m, 3, 3, world, kv_shared=20)
         if not args.no_config4 and args.only is None:
             line["config4"] = {"prompts_dp": prompts_dp(w8, dev, stream, world, rank, 3, 3),
                                "lm_head_sharded": sharded_head(w8, dev, stream, world, 50, 5, pk)}

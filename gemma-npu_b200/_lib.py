@@ -94,6 +94,8 @@ SIGNATURES = {
     "w8_attn_out_quant_bf16": (_i, [_p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _p]),
     "w8_attention_prefill_quant": (_i, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                                         _i64, _p, _i64, _p, _p]),
+    "w8_gemm_qkv_norm_rope": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _i, _p, _p, _i64, _p, _p, _f, _p,
+                                   _i64, _i64, _i64, _p]),
     "w8_gemm_gelu_up_quant": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _p, _p]),
     "w8_quant_rows_bf16": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _p]),
     "w8_quant_rows_f32": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _p]),
@@ -102,6 +104,16 @@ SIGNATURES = {
     "w8_lm_head_f32": (_i, [_p, _p, _p, _f, _p, _i64, _i64, _p]),
     "w8_lm_head_argmax_f32": (_i, [_p, _p, _p, _f, _p, _i64, _i64, _p, _p]),
 }
+
+class W8GemvStep(ctypes.Structure):
+    """w8_gemv_step (w8a8_b200.h): one GEMV of a decode chain."""
+    _fields_ = [("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("s", ctypes.c_void_p), ("y", ctypes.c_void_p),
+                ("best", ctypes.c_void_p), ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("cap", ctypes.c_float),
+                ("logits", ctypes.c_int)]
+
+
+SIGNATURES["w8_gemv_chain"] = (_i, [ctypes.POINTER(W8GemvStep), _i, _p, _i64, _p])
+SIGNATURES["w8_gemv_chain_workspace_bytes"] = (_i64, [_i])
 
 _lock = threading.Lock()
 _lib = None

@@ -111,6 +111,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, uint32_t src,
                "r"(src), "r"(x), "r"(y)
                : "memory");
 }
+// 3-D tiled bulk tensor store (innermost coordinate x, then y, then z), clipped at the
+// tensor bounds; the same alignment rule on x as the 2-D store.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, uint32_t src, int32_t x, int32_t y, int32_t z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
 // Same box, added element-wise into global memory (s32 add for an INT32 tensor map);
 // performed at L2, so concurrent adds from other CTAs combine exactly.
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, uint32_t src, int32_t x,
@@ -118,6 +126,13 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, uint32_t
   asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(m)),
                "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+// 1-D bulk copy global -> shared memory (no tensor map), completion counted on `bar` in
+// bytes.  Both addresses 16-byte aligned, `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_load_1d(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
                : "memory");
 }
 // Order this thread's earlier generic-proxy global accesses before its later async-proxy ones.

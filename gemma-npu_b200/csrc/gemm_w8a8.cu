@@ -74,7 +74,10 @@ constexpr uint32_t kTmemCols = 2 * kBN;  // two accumulators of 256 int32 column
 // k_gelu (pipeline.py:102-107) up to its quant: bf16(gelu_tanh(gate) * up) of the
 // dequantised halves of each 256-column tile (packed weights: tile t holds gate rows
 // 128t.. and up rows I + 128t..), 128 bf16 outputs per tile row, plus the row absmax.
-enum EpiKind : int { kEpiI32 = 0, kEpiBf16 = 1, kEpiGeluUp = 2 };
+// kEpiQkv: the qkv glue k_qkv (pipeline.py:72-86) for head_dim 256, one head per
+// 256-column tile: dequant, the head's RMSNorm (q_norm / k_norm weight, none for v) and,
+// for q and k heads, RoPE, stored head-major [heads, T, 256] as bf16.
+enum EpiKind : int { kEpiI32 = 0, kEpiBf16 = 1, kEpiGeluUp = 2, kEpiQkv = 3 };
 
 struct GemmArgs {
   int m, n, k;
@@ -90,6 +93,14 @@ struct GemmArgs {
   uint32_t* flags;   // stream-K: one zero-initialised counter per tile
   int bn;            // output columns per tile: 256, or 192 on CTA pairs when it balances waves
   float* row_absmax; // kEpiGeluUp: per-row max |output| (fp32 bits, atomicMax), zero on entry
+  // kEpiQkv: heads [0, q_heads) are q, [q_heads, q_heads + k_heads) k, the rest v.
+  const __nv_bfloat16* cos;  // [T, >= 256] row pitch ldcs
+  const __nv_bfloat16* sin;
+  int64_t ldcs;
+  const __nv_bfloat16* qw;   // q_norm weight [256]
+  const __nv_bfloat16* kw;   // k_norm weight [256]
+  float eps;
+  int q_heads, k_heads;
 };
 
 constexpr int kEpiBufBytes = 32 * 128;  // one 32-row x 128-byte store box
@@ -102,15 +113,27 @@ constexpr int kEpiBufs = 2;             // per epilogue warp: fill one while TMA
 // the math (with two warps per quarter it waited on its own dependences, not on a unit).
 constexpr int kGeluWarpsPerQuarter = 4;
 constexpr int kGeluBufBytes = 32 * 64;
+// The qkv glue: two warps per lane quarter (each finishes half of the head's RoPE column
+// pairs), each with two 32-row x 64-byte staging boxes.
+constexpr int kQkvWarpsPerQuarter = 2;
+constexpr int kQkvBufs = 2;
+constexpr int kQkvBufBytes = 32 * 64;
 template <int EPI>
-constexpr int epi_warps() { return EPI == kEpiGeluUp ? kGeluWarpsPerQuarter * kEpiWarps : kEpiWarps; }
+constexpr int epi_warps() {
+  return EPI == kEpiGeluUp ? kGeluWarpsPerQuarter * kEpiWarps
+                           : (EPI == kEpiQkv ? kQkvWarpsPerQuarter * kEpiWarps : kEpiWarps);
+}
 template <int EPI>
-constexpr int epi_bufs() { return EPI == kEpiGeluUp ? 1 : kEpiBufs; }
+constexpr int epi_bufs() { return EPI == kEpiGeluUp ? 1 : (EPI == kEpiQkv ? kQkvBufs : kEpiBufs); }
 template <int EPI>
-constexpr int epi_buf_bytes() { return EPI == kEpiGeluUp ? kGeluBufBytes : kEpiBufBytes; }
+constexpr int epi_buf_bytes() {
+  return EPI == kEpiGeluUp ? kGeluBufBytes : (EPI == kEpiQkv ? kQkvBufBytes : kEpiBufBytes);
+}
 template <int EPI>
 constexpr int threads_for() { return 64 + 32 * epi_warps<EPI>(); }
 static_assert(kGeluWarpsPerQuarter * kEpiWarps * kGeluBufBytes == kEpiWarps * kEpiBufs * kEpiBufBytes,
+              "staging layout differs");
+static_assert(kQkvWarpsPerQuarter * kEpiWarps * kQkvBufs * kQkvBufBytes == kEpiWarps * kEpiBufs * kEpiBufBytes,
               "staging layout differs");
 
 // Shared-memory plan of one CTA: the operand ring, the epilogue staging boxes, barriers.
@@ -343,6 +366,132 @@ __device__ __forceinline__ void put_box64(const CUtensorMap* tm_c, const uint32_
   }
 }
 
+// Stage one 32-row x 64-byte box (32 bf16 columns, row = lane, no swizzle) in one of this
+// warp's two buffers and store it with TMA into a 3-D [heads, T, D] output at (x, row0, z).
+__device__ __forceinline__ void put_box64_3d(const CUtensorMap* tm_c, const uint32_t (&v)[16], uint32_t stage_base,
+                                             uint32_t& sbuf, int lane, int x, int row0, int z) {
+  const uint32_t buf = stage_base + (sbuf & 1u) * kQkvBufBytes;
+  ++sbuf;
+  if (lane == 0) bulk_wait_group_read<1>();  // the box last stored from buf is read
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) st_shared_v4(buf + lane * 64 + j * 16, v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_3d(tm_c, buf, x, row0, z);
+    bulk_commit_group();
+  }
+}
+
+// 16 words of bf16 pairs (32 consecutive columns of one row) from global memory, or zeros
+// for a row past M.
+__device__ __forceinline__ void load_row32_bf16(const __nv_bfloat16* p, bool valid, uint32_t (&out)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 v = valid ? __ldg(reinterpret_cast<const uint4*>(p) + j) : make_uint4(0u, 0u, 0u, 0u);
+    out[4 * j] = v.x, out[4 * j + 1] = v.y, out[4 * j + 2] = v.z, out[4 * j + 3] = v.w;
+  }
+}
+
+// k_qkv for one head (256 columns) of this thread's row (pipeline.py:72-86), the operation
+// order of the row kernel w8_qkv_norm_rope_bf16, so the output bits are the same:
+//   pass 1: y = _deq(acc) (bf16); 32 partial sums of y^2 over 8 consecutive columns,
+//           combined in the row kernel's lane-then-xor-tree order; r = rsqrt(sum/256 + eps)
+//   pass 2: x = bf16(y * r * w) (v heads: bf16(y * r)); q / k heads:
+//           out = bf16(bf16(x * cos) + bf16(rotate_half(x) * sin)) on packed bf16 pairs.
+// `part` (0 or 1) picks the RoPE column pairs (c, c + 128) this warp finishes:
+// c in [64 part, 64 part + 64).
+template <typename Release>
+__device__ __forceinline__ void qkv_epilogue_rows(const GemmArgs& args, const CUtensorMap* tm_c, uint32_t taddr,
+                                                  int row0, int col_base, float sxr, uint32_t stage_base,
+                                                  uint32_t& sbuf, int lane, int part, Release release) {
+  const int head = col_base >> 8;
+  const int row = row0 + lane;
+  const bool valid = row < args.m;
+  // ---- pass 1: the row's sum of squares of the dequantised bf16 values
+  float ps[32];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint32_t r[32], y[16];
+    tmem_ld_32x32b_x32(taddr + c * 32, r);
+    tmem_wait_ld();
+    dequant_pack(args, col_base + c * 32, r, sxr, y);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      float acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float lo = __uint_as_float(y[4 * g + e] << 16), hi = __uint_as_float(y[4 * g + e] & 0xFFFF0000u);
+        acc = __fmaf_rn(lo, lo, acc);
+        acc = __fmaf_rn(hi, hi, acc);
+      }
+      ps[4 * c + g] = acc;
+    }
+  }
+  // A warp's xor-butterfly sum, as lane 0 of the row kernel forms it (v + shfl_xor(v, o)
+  // for o = 16, 8, 4, 2, 1; addition is commutative, so every lane holds these bits).
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < o; ++i) ps[i] = __fadd_rn(ps[i], ps[i + o]);
+  const float rn = __frsqrt_rn(__fadd_rn(__fdiv_rn(ps[0], 256.f), args.eps));
+  const uint64_t r2 = f2_pack(rn, rn);
+  const bool is_q = head < args.q_heads;
+  const bool is_k = !is_q && head < args.q_heads + args.k_heads;
+  const __nv_bfloat16* wnorm = is_q ? args.qw : (is_k ? args.kw : nullptr);
+  const __nv_bfloat16* crow = args.cos + static_cast<int64_t>(row) * args.ldcs;
+  const __nv_bfloat16* srow = args.sin + static_cast<int64_t>(row) * args.ldcs;
+  // ---- pass 2: this warp's column pairs (c, c + 128), 32 columns at a time
+#pragma unroll 1
+  for (int cc = 0; cc < 2; ++cc) {
+    const int c0 = part * 64 + cc * 32;  // first half: columns c0..c0+31; second: c0+128..
+    uint32_t ra[32], rb[32], xa[16], xb[16];
+    tmem_ld_32x32b_x32(taddr + c0, ra);
+    tmem_ld_32x32b_x32(taddr + 128 + c0, rb);
+    tmem_wait_ld();
+    if (cc == 1) {  // this warp's columns are in registers: hand TMEM back
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) release();
+    }
+    dequant_pack(args, col_base + c0, ra, sxr, xa);
+    dequant_pack(args, col_base + 128 + c0, rb, sxr, xb);
+    if (wnorm != nullptr) {
+      uint32_t wa[16], wb[16];
+      load_row32_bf16(wnorm + c0, true, wa);
+      load_row32_bf16(wnorm + 128 + c0, true, wb);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        xa[q] = bf16x2_from_f2(f2_mul(f2_mul(f2_from_bf16x2(xa[q]), r2), f2_from_bf16x2(wa[q])));
+        xb[q] = bf16x2_from_f2(f2_mul(f2_mul(f2_from_bf16x2(xb[q]), r2), f2_from_bf16x2(wb[q])));
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        xa[q] = bf16x2_from_f2(f2_mul(f2_from_bf16x2(xa[q]), r2));
+        xb[q] = bf16x2_from_f2(f2_mul(f2_from_bf16x2(xb[q]), r2));
+      }
+    }
+    if (wnorm != nullptr) {  // q and k heads: RoPE with rotate_half's partner c <-> c + 128
+      uint32_t ca[16], cb[16], sa[16], sb[16];
+      load_row32_bf16(crow + c0, valid, ca);
+      load_row32_bf16(crow + 128 + c0, valid, cb);
+      load_row32_bf16(srow + c0, valid, sa);
+      load_row32_bf16(srow + 128 + c0, valid, sb);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const uint32_t oa = bf16x2_add(bf16x2_mul(xa[q], ca[q]), bf16x2_mul(xb[q] ^ 0x80008000u, sa[q]));
+        const uint32_t ob = bf16x2_add(bf16x2_mul(xb[q], cb[q]), bf16x2_mul(xa[q], sb[q]));
+        xa[q] = oa;
+        xb[q] = ob;
+      }
+    }
+    put_box64_3d(tm_c, xa, stage_base, sbuf, lane, c0, row0, head);
+    put_box64_3d(tm_c, xb, stage_base, sbuf, lane, 128 + c0, row0, head);
+  }
+}
+
 // Drain one 32-row slice of a finished accumulator (called by one whole epilogue warp).
 // `taddr` addresses the warp's TMEM lanes at the accumulator's first column; rows
 // row0.. and columns col_base.. of the output.  `release` hands the accumulator back to
@@ -355,6 +504,10 @@ __device__ __forceinline__ void epilogue_rows(const GemmArgs& args, const CUtens
                                               bool reduce, int part, Release release) {
   const int n_cols = min(args.bn, args.n - col_base);  // columns of this tile inside N
   const int row = row0 + lane;
+  if constexpr (EPI == kEpiQkv) {
+    qkv_epilogue_rows(args, tm_c, taddr, row0, col_base, sxr, stage_base, sbuf, lane, part, release);
+    return;
+  }
   if constexpr (EPI == kEpiGeluUp) {
     // 256 accumulator columns = 128 gate + 128 up -> output columns col_base / 2 ..+128;
     // this warp (`part` of the four of its lane quarter) finishes output columns
@@ -915,6 +1068,42 @@ static int encode_kchunks(CUtensorMap* map, const void* ptr, int64_t k, int64_t 
   return W8_OK;
 }
 
+// The head-major qkv output [heads, T, D] (bf16) as a 3-D tensor (D, T, heads) with
+// 32-column x 32-row x 1-head boxes, unswizzled: stores clip at T and at the last head.
+static int encode_heads_out(CUtensorMap* map, const void* ptr, int64_t d, int64_t t, int64_t heads,
+                            int64_t ld_tok, int64_t ld_head) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return W8_ERR_CUDA;
+  }
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(t), static_cast<cuuint64_t>(heads)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld_tok * 2), static_cast<cuuint64_t>(ld_head * 2)};
+  const cuuint32_t box[3] = {32, 32, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (heads) failed with CUresult %d (d %lld, t %lld, heads %lld)",
+              static_cast<int>(r), static_cast<long long>(d), static_cast<long long>(t), static_cast<long long>(heads));
+    return W8_ERR_CUDA;
+  }
+  return W8_OK;
+}
+
+// Arguments of the fused qkv glue epilogue (w8_gemm_qkv_norm_rope).
+struct QkvEpiParams {
+  const uint16_t* cos;
+  const uint16_t* sin;
+  int64_t ldcs;
+  const uint16_t* qw;
+  const uint16_t* kw;
+  float eps;
+  int q_heads, k_heads;
+  int64_t ld_head, ld_tok;
+};
+
 int require_sm100(int* device);
 
 template <typename Kernel>
@@ -1039,7 +1228,7 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
                        void* out, int64_t ldo, int out_elem, const float* sx, const float* sw,
                        int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
                        cudaStream_t stream, int epi, float* row_absmax = nullptr,
-                       int64_t clear_words = 0) {
+                       int64_t clear_words = 0, const QkvEpiParams* qkv = nullptr) {
   // Output columns: the GEMM's N, or N / 2 for the gate/up glue (gelu(gate) * up).
   const int64_t n_out = epi == w8::kEpiGeluUp ? n / 2 : n;
   W8_CHECK_ARG(m >= 0 && n >= 0 && k >= 0, "negative size (m=%lld n=%lld k=%lld)", (long long)m,
@@ -1091,8 +1280,12 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   // prompts) take 64 or 128 and spread over more SMs (measured, bf16 out: PLE gate at
   // M = 3658 11.2 -> 8.6 us, qkv at M = 207 10.1 -> 8.5 us, o at M = 858 11.4 -> 10.7 us).
   // Shapes that stream-K will balance keep 256.
+  if (epi == w8::kEpiQkv) {
+    W8_CHECK_ARG(qkv != nullptr && b_layout == W8_B_NK, "the qkv glue takes [N, K] weights and its parameters");
+    W8_CHECK_ARG(n % 256 == 0, "n = %lld must be a whole number of 256-wide heads", (long long)n);
+  }
   int bn = w8::kBN;
-  if (pair && b_layout == W8_B_NK && epi != w8::kEpiGeluUp &&
+  if (pair && b_layout == W8_B_NK && epi != w8::kEpiGeluUp && epi != w8::kEpiQkv &&
       !(epi == w8::kEpiI32 && workspace != nullptr && k >= 24 * w8::kBK)) {
     int cap = 0;
     st = pair_capacity<false, w8::kEpiI32, w8::kBN>(device, &cap);
@@ -1142,12 +1335,30 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   args.stream_k = 0;
   args.flags = static_cast<uint32_t*>(workspace);
   args.row_absmax = row_absmax;
+  args.cos = args.sin = args.qw = args.kw = nullptr;
+  args.ldcs = 0;
+  args.eps = 0.f;
+  args.q_heads = args.k_heads = 0;
+  if (qkv != nullptr) {
+    args.cos = reinterpret_cast<const __nv_bfloat16*>(qkv->cos);
+    args.sin = reinterpret_cast<const __nv_bfloat16*>(qkv->sin);
+    args.ldcs = qkv->ldcs;
+    args.qw = reinterpret_cast<const __nv_bfloat16*>(qkv->qw);
+    args.kw = reinterpret_cast<const __nv_bfloat16*>(qkv->kw);
+    args.eps = qkv->eps;
+    args.q_heads = qkv->q_heads;
+    args.k_heads = qkv->k_heads;
+  }
   const int64_t flag_words = workspace_bytes / 4;
   // Output through TMA when the tensor map can address it (16-byte base and pitch);
   // one box is 32 rows x 128 bytes.  Otherwise the epilogue stores directly.
   memset(&tc, 0, sizeof(tc));
   args.tma_out = 0;
-  if (args.vec_out) {
+  if (epi == w8::kEpiQkv) {
+    st = encode_heads_out(&tc, out, 256, m, n / 256, qkv->ld_tok, qkv->ld_head);
+    if (st != W8_OK) return st;
+    args.tma_out = 1;
+  } else if (args.vec_out) {
     const bool i32 = epi == w8::kEpiI32;
     // The gate/up glue stores 32-row x 32-column bf16 boxes (one per epilogue warp,
     // unswizzled 64-byte rows).
@@ -1170,6 +1381,9 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   if (epi == w8::kEpiGeluUp)
     return pair ? launch_pair<false, w8::kEpiGeluUp, 256>(device, ta, tb, tc, args, flag_words, stream)
                 : launch_single<false, w8::kEpiGeluUp>(device, ta, tb, tc, args, flag_words, stream);
+  if (epi == w8::kEpiQkv)
+    return pair ? launch_pair<false, w8::kEpiQkv, 256>(device, ta, tb, tc, args, flag_words, stream)
+                : launch_single<false, w8::kEpiQkv>(device, ta, tb, tc, args, flag_words, stream);
   if (pair) {
     if (mn)
       return i32 ? launch_pair<true, w8::kEpiI32, 256>(device, ta, tb, tc, args, flag_words, stream)
@@ -1334,4 +1548,34 @@ extern "C" int w8_gemm_dequant_bf16(const int8_t* a, int64_t lda, const int8_t* 
                                     w8_stream_t stream) {
   return w8host::gemm_common(a, lda, b, ldb, b_layout, y, ldy, 2, sx, sw, m, n, k, nullptr, 0,
                              reinterpret_cast<cudaStream_t>(stream), w8::kEpiBf16);
+}
+
+extern "C" int w8_gemm_qkv_norm_rope(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, const float* sx,
+                                     const float* sw, int64_t m, int64_t heads, int64_t kv_heads, int shared,
+                                     const uint16_t* cos, const uint16_t* sin, int64_t ldcs, const uint16_t* qw,
+                                     const uint16_t* kw, float eps, uint16_t* out, int64_t ld_head, int64_t ld_tok,
+                                     int64_t k, w8_stream_t stream) {
+  using namespace w8host;
+  W8_CHECK_ARG(m >= 0 && heads >= 0 && kv_heads >= 0 && heads < 4096 && kv_heads < 4096, "bad size");
+  const int64_t per_tok = shared ? heads : heads + 2 * kv_heads;
+  if (m == 0 || per_tok == 0) return W8_OK;
+  W8_CHECK_ARG(cos != nullptr && sin != nullptr && qw != nullptr && out != nullptr, "null pointer");
+  W8_CHECK_ARG(shared || kv_heads == 0 || kw != nullptr, "null k_norm weight");
+  W8_CHECK_ARG(ldcs >= 256 && ld_tok >= 256 && ld_head >= ld_tok * m, "pitch too small");
+  W8_CHECK_ALIGN(aligned(cos, 16) && aligned(sin, 16) && ldcs % 8 == 0 && aligned(qw, 16) &&
+                     (kw == nullptr || aligned(kw, 16)) && aligned(out, 16) && ld_head % 8 == 0 && ld_tok % 8 == 0,
+                 "weights, cos/sin and the output must be 16-byte aligned with pitches %% 8 == 0");
+  QkvEpiParams q;
+  q.cos = cos;
+  q.sin = sin;
+  q.ldcs = ldcs;
+  q.qw = qw;
+  q.kw = kw;
+  q.eps = eps;
+  q.q_heads = static_cast<int>(heads);
+  q.k_heads = shared ? 0 : static_cast<int>(kv_heads);
+  q.ld_head = ld_head;
+  q.ld_tok = ld_tok;
+  return gemm_common(a, lda, w, ldw, W8_B_NK, out, per_tok * 256, 2, sx, sw, m, per_tok * 256, k, nullptr, 0,
+                     reinterpret_cast<cudaStream_t>(stream), w8::kEpiQkv, nullptr, 0, &q);
 }

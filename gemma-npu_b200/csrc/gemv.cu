@@ -20,6 +20,8 @@
 // memory, and lane r of the team's first warp finishes row r (scale, bf16, softcap, store).
 // Weight loads of the first row batch are issued before waiting for the previous kernel
 // of the stream (programmatic dependent launch): only the activation row depends on it.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace w8 {
@@ -85,6 +87,32 @@ __device__ __forceinline__ void dot16_q(const uint4& w, const uint32_t (&xh)[4],
   lo = dp4a_su(w.w, xl[3], lo);
 }
 
+// One 16-element piece of the activation row (8 words of bf16 pairs) as 16-bit fixed
+// point over its own range: fma(x, qs, 1.5 * 2^23) rounds x * qs to the nearest integer
+// (one rounding), whose two's complement low 16 bits are the float's low 16 bits; byte
+// permutes gather the low bytes (unsigned lo) and the high bytes (signed hi) of four codes
+// per word.  Returns the piece's scale max|x| / 32766.
+__device__ __forceinline__ float piece_codes(const uint32_t (&words)[8], uint32_t (&xh)[4], uint32_t (&xl)[4]) {
+  constexpr float kMagic = 12582912.f;
+  __nv_bfloat162 m2 = __habs2(*reinterpret_cast<const __nv_bfloat162*>(&words[0]));
+#pragma unroll
+  for (int i = 1; i < 8; ++i) m2 = __hmax2(m2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&words[i])));
+  const float am = fmaxf(__low2float(m2), __high2float(m2));
+  // 32766 (not 32767) keeps every code inside int16 under the approximate division.
+  const float qs = am > 0.f ? __fdividef(32766.f, am) : 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t w0 = words[2 * q], w1 = words[2 * q + 1];
+    const uint32_t u0 = __float_as_uint(fmaf(__uint_as_float(w0 << 16), qs, kMagic));
+    const uint32_t u1 = __float_as_uint(fmaf(__uint_as_float(w0 & 0xFFFF0000u), qs, kMagic));
+    const uint32_t u2 = __float_as_uint(fmaf(__uint_as_float(w1 << 16), qs, kMagic));
+    const uint32_t u3 = __float_as_uint(fmaf(__uint_as_float(w1 & 0xFFFF0000u), qs, kMagic));
+    xl[q] = __byte_perm(__byte_perm(u0, u1, 0x0040), __byte_perm(u2, u3, 0x0040), 0x5410);
+    xh[q] = __byte_perm(__byte_perm(u0, u1, 0x0051), __byte_perm(u2, u3, 0x0051), 0x5410);
+  }
+  return am * (1.f / 32766.f);
+}
+
 template <int J, int S, int R, bool LOGITS>
 __global__ void __launch_bounds__(kGemvThreads)
     int8_gemv_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
@@ -127,11 +155,7 @@ __global__ void __launch_bounds__(kGemvThreads)
   for (int t = 0; t < t_count; ++t) {
     const __nv_bfloat16* xt = x + static_cast<int64_t>(t) * ldx;
     // This lane's 16-element pieces of the row, each as 16-bit fixed point over its own
-    // range: no reduction across lanes or warps before the dot products.  fma(x, qs,
-    // 1.5 * 2^23) rounds x * qs to the nearest integer (one rounding), whose two's
-    // complement low 16 bits are the float's low 16 bits; byte permutes gather the low
-    // bytes (unsigned lo) and the high bytes (signed hi) of four codes per word.
-    constexpr float kMagic = 12582912.f;
+    // range: no reduction across lanes or warps before the dot products.
     uint32_t xh[J][4], xl[J][4];
     float dq[J];
 #pragma unroll
@@ -144,23 +168,7 @@ __global__ void __launch_bounds__(kGemvThreads)
         words[0] = a.x, words[1] = a.y, words[2] = a.z, words[3] = a.w;
         words[4] = b.x, words[5] = b.y, words[6] = b.z, words[7] = b.w;
       }
-      __nv_bfloat162 m2 = __habs2(*reinterpret_cast<const __nv_bfloat162*>(&words[0]));
-#pragma unroll
-      for (int i = 1; i < 8; ++i) m2 = __hmax2(m2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&words[i])));
-      const float am = fmaxf(__low2float(m2), __high2float(m2));
-      // 32766 (not 32767) keeps every code inside int16 under the approximate division.
-      const float qs = am > 0.f ? __fdividef(32766.f, am) : 0.f;
-      dq[c] = am * (1.f / 32766.f);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t w0 = words[2 * q], w1 = words[2 * q + 1];
-        const uint32_t u0 = __float_as_uint(fmaf(__uint_as_float(w0 << 16), qs, kMagic));
-        const uint32_t u1 = __float_as_uint(fmaf(__uint_as_float(w0 & 0xFFFF0000u), qs, kMagic));
-        const uint32_t u2 = __float_as_uint(fmaf(__uint_as_float(w1 << 16), qs, kMagic));
-        const uint32_t u3 = __float_as_uint(fmaf(__uint_as_float(w1 & 0xFFFF0000u), qs, kMagic));
-        xl[c][q] = __byte_perm(__byte_perm(u0, u1, 0x0040), __byte_perm(u2, u3, 0x0040), 0x5410);
-        xh[c][q] = __byte_perm(__byte_perm(u0, u1, 0x0051), __byte_perm(u2, u3, 0x0051), 0x5410);
-      }
+      dq[c] = piece_codes(words, xh[c], xl[c]);
     }
 
     for (int n0 = first; n0 < n; n0 += stride) {
@@ -233,6 +241,270 @@ __global__ void __launch_bounds__(kGemvThreads)
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mine = max(mine, __shfl_xor_sync(0xffffffffu, mine, o));
       if (lane == 0 && mine != 0ull) atomicMax(best, mine);
+    }
+  }
+}
+
+// =====================================================================================
+// Decode GEMV chain: a whole decode step's GEMVs in one persistent launch.
+//
+// A chain of dependent GEMVs (step i + 1 may read step i's output as its activation row)
+// is bound, one kernel per GEMV, by each kernel's start-up and drain plus one DRAM round
+// trip: 3-19 MB GEMVs ran at 0.2-0.5 of the HBM bandwidth.  Here one CTA per SM runs the
+// whole chain.  Its producer warp streams the CTA's share of every step's weight rows --
+// which depend on nothing -- through a deep shared-memory ring with 1-D bulk copies,
+// running ahead across step boundaries; only the activation row of a step waits, on a
+// grid-wide counter that every CTA bumps when its rows of the previous step are stored.
+// So the weights keep streaming while the consumers wait for the dependence.
+//
+// Per step, CTA b owns the contiguous weight rows [n b / G, n (b + 1) / G) (G CTAs): a
+// contiguous byte range of the [N, K] row-major weight, copied in chunks of whole rows.
+// Each consumer warp finishes whole rows with the arithmetic of int8_gemv_kernel at the
+// same (J, S) K-split -- the same pieces, the same dp4a sums and the same fp32 order --
+// so every output is bit-identical to the standalone GEMV of that step.
+//
+// All CTAs are co-resident (cooperative launch, one CTA per SM), every wait is bounded,
+// and a CTA that gives up raises a grid-wide abort word so the others stop too; the last
+// CTA to leave resets the counters, so the workspace is all-zero after every launch.
+// =====================================================================================
+constexpr int kChainMaxSteps = 192;
+constexpr int kChainConsumerWarps = 8;
+constexpr int kChainThreads = 32 * (1 + kChainConsumerWarps);
+constexpr int kChainStageBytes = 24 * 1024;
+constexpr int kChainStages = 8;
+constexpr int kChainMaxK = 12288;
+constexpr int kChainRingOff = 0;
+constexpr int kChainXhOff = kChainStages * kChainStageBytes;
+constexpr int kChainXlOff = kChainXhOff + kChainMaxK;
+constexpr int kChainDqOff = kChainXlOff + kChainMaxK;
+constexpr int kChainBarOff = kChainDqOff + (kChainMaxK / 16) * 4;
+constexpr int kChainSmem = kChainBarOff + 2 * kChainStages * 8 + 16;
+static_assert(kChainSmem <= 232448, "decode chain shared memory exceeds one CTA's budget");
+static_assert(kChainStageBytes >= 2 * kChainMaxK, "a stage must hold at least two rows");
+
+__device__ int g_chain_status = 0;  // sticky device status of the chain kernel
+
+struct ChainStep {
+  const __nv_bfloat16* x;
+  const int8_t* w;
+  const __nv_bfloat16* s;
+  void* y;
+  unsigned long long* best;  // greedy key of a logits step (zeroed by the host), or null
+  int n, k;
+  float cap;
+  int logits;  // 0: bf16 y [n]; 1: fp32 logits [n] with the softcap (cap > 0)
+  int J, S;    // the standalone kernel's K split for this K
+};
+
+struct ChainParams {
+  int count;
+  uint32_t* ctr;  // workspace: ctr[i] steps done per CTA; ctr[count] CTAs gone; ctr[count + 1] abort
+  ChainStep step[kChainMaxSteps];
+};
+
+__device__ __forceinline__ void chain_consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kChainConsumerWarps * 32) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until every CTA has finished step `i` (its counter reaches `target`);
+// false if the grid's abort word is raised or the wait times out (then it raises it).
+__device__ __forceinline__ bool chain_wait_step(const uint32_t* ctr, uint32_t target, uint32_t* abort_word) {
+  const unsigned long long t0 = globaltimer();
+#pragma unroll 1
+  while (true) {
+    if (ld_acquire_gpu(ctr) >= target) return true;
+    if (ld_volatile_u32(abort_word) != 0u) return false;
+    __nanosleep(32);
+    if (globaltimer() - t0 > kWaitTimeoutNs) {
+      atomicExch(&g_chain_status, W8_ERR_DEVICE_TIMEOUT);
+      atomicExch(abort_word, 1u);
+      return false;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __grid_constant__ ChainParams p) {
+  extern __shared__ __align__(16) uint8_t chain_smem[];
+  const uint32_t base = smem_u32(chain_smem);
+  const uint32_t bar0 = base + kChainBarOff;
+  auto full_bar = [&](int st) { return bar0 + 8u * st; };
+  auto empty_bar = [&](int st) { return bar0 + 8u * (kChainStages + st); };
+  volatile int* abort_smem = reinterpret_cast<volatile int*>(chain_smem + kChainBarOff + 2 * kChainStages * 8);
+  uint32_t* const abort_word = p.ctr + p.count + 1;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int b = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kChainStages; ++st) {
+      mbar_init(full_bar(st), 1);
+      mbar_init(empty_bar(st), kChainConsumerWarps);
+    }
+    *abort_smem = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer: this CTA's weight rows of every step, in order
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, last_phase = 0;
+      bool ok = true;
+      for (int i = 0; ok && i < p.count; ++i) {
+        const ChainStep& st = p.step[i];
+        const int r0 = static_cast<int>(static_cast<int64_t>(st.n) * b / G);
+        const int r1 = static_cast<int>(static_cast<int64_t>(st.n) * (b + 1) / G);
+        const int rpc = kChainStageBytes / st.k;  // whole rows per chunk
+        for (int c0 = r0; c0 < r1; c0 += rpc) {
+          const int c1 = min(c0 + rpc, r1);
+          if (!mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_smem, &g_chain_status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bytes = static_cast<uint32_t>(c1 - c0) * static_cast<uint32_t>(st.k);
+          mbar_arrive_expect_tx(full_bar(stage), bytes);
+          bulk_load_1d(base + kChainRingOff + stage * kChainStageBytes, st.w + static_cast<int64_t>(c0) * st.k,
+                       bytes, full_bar(stage));
+          issued |= 1u << stage;
+          last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == kChainStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        atomicExch(abort_word, 1u);
+        *abort_smem = 1;
+      }
+      // Copies still in flight land before the CTA may exit (consumed ones already have).
+      for (int st = 0; st < kChainStages; ++st)
+        if (issued & (1u << st)) mbar_wait_bounded(full_bar(st), (last_phase >> st) & 1u, nullptr, &g_chain_status);
+    }
+  } else {
+    // ---------------- consumers: 8 warps, whole rows each
+    const int cw = warp - 1;
+    const int ctid = threadIdx.x - 32;
+    uint8_t* xh_s = chain_smem + kChainXhOff;
+    uint8_t* xl_s = chain_smem + kChainXlOff;
+    float* dq_s = reinterpret_cast<float*>(chain_smem + kChainDqOff);
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int i = 0; i < p.count; ++i) {
+      const ChainStep& st = p.step[i];
+      if (i > 0) {
+        if (ctid == 0 && !chain_wait_step(p.ctr + (i - 1), static_cast<uint32_t>(G), abort_word)) *abort_smem = 1;
+        chain_consumer_sync();
+        if (*abort_smem) break;
+      }
+      // This step's activation row -> per-piece fixed point in shared memory.  x may be the
+      // previous step's output, written by other SMs: read it from L2 (ld.global.cg).
+      const int pieces = st.k / 16;
+      for (int pc = ctid; pc < pieces; pc += kChainConsumerWarps * 32) {
+        const uint4* src = reinterpret_cast<const uint4*>(st.x + pc * 16);
+        uint4 a, c;
+        asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w) : "l"(src));
+        asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(c.x), "=r"(c.y), "=r"(c.z), "=r"(c.w) : "l"(src + 1));
+        const uint32_t words[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+        uint32_t xh[4], xl[4];
+        dq_s[pc] = piece_codes(words, xh, xl);
+        *reinterpret_cast<uint4*>(xh_s + pc * 16) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
+        *reinterpret_cast<uint4*>(xl_s + pc * 16) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
+      }
+      chain_consumer_sync();
+
+      const int r0 = static_cast<int>(static_cast<int64_t>(st.n) * b / G);
+      const int r1 = static_cast<int>(static_cast<int64_t>(st.n) * (b + 1) / G);
+      const int rpc = kChainStageBytes / st.k;
+      const int J = st.J, S = st.S;
+      unsigned long long mine = 0ull;
+      bool ok = true;
+      for (int c0 = r0; c0 < r1; c0 += rpc) {
+        const int c1 = min(c0 + rpc, r1);
+        // Every lane waits on the stage's barrier itself: each reader of the copied rows
+        // observes their completion.
+        const bool got = mbar_wait_bounded(full_bar(stage), phase, abort_smem, &g_chain_status);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* ring = chain_smem + kChainRingOff + stage * kChainStageBytes;
+        for (int r = cw; r < c1 - c0; r += kChainConsumerWarps) {
+          const uint8_t* wrow = ring + static_cast<int64_t>(r) * st.k;
+          float total = 0.f;
+          for (int sl = 0; sl < S; ++sl) {
+            float v = 0.f;
+            for (int c = 0; c < J; ++c) {
+              const int pc = (sl * J + c) * 32 + lane;
+              int hi = 0, lo = 0;
+              float d = 0.f;
+              if (pc < pieces) {
+                const uint4 wv = *reinterpret_cast<const uint4*>(wrow + pc * 16);
+                const uint4 h4 = *reinterpret_cast<const uint4*>(xh_s + pc * 16);
+                const uint4 l4 = *reinterpret_cast<const uint4*>(xl_s + pc * 16);
+                const uint32_t xh[4] = {h4.x, h4.y, h4.z, h4.w};
+                const uint32_t xl[4] = {l4.x, l4.y, l4.z, l4.w};
+                dot16_q(wv, xh, xl, hi, lo);
+                d = dq_s[pc];
+              }
+              v = fmaf(static_cast<float>(256 * hi + lo), d, v);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            total = sl == 0 ? v : total + v;
+          }
+          if (lane == 0) {
+            const int row = c0 + r;
+            if (st.logits) {
+              const float f = write_out<true>(st.y, row, total, st.s[row], st.cap);
+              if (st.best != nullptr) mine = max(mine, argmax_key(f, row));
+            } else {
+              write_out<false>(st.y, row, total, st.s[row], 0.f);
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar(stage));
+        if (++stage == kChainStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        if (lane == 0) {
+          *abort_smem = 1;
+          atomicExch(abort_word, 1u);
+        }
+        break;
+      }
+      if (lane == 0) {
+        if (st.logits && st.best != nullptr && mine != 0ull) atomicMax(st.best, mine);
+        __threadfence();  // this warp's outputs are visible GPU-wide before the step counter moves
+      }
+      chain_consumer_sync();
+      if (ctid == 0) {
+        __threadfence();
+        atomicAdd(p.ctr + i, 1u);
+      }
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // The last CTA to leave resets every counter (and the abort word) for the next launch;
+    // no CTA reads a counter after it has arrived here.
+    __threadfence();
+    if (atomicAdd(p.ctr + p.count, 1u) == static_cast<uint32_t>(G) - 1u) {
+      for (int i = 0; i < p.count + 2; ++i) atomicExch(p.ctr + i, 0u);
+      __threadfence();
     }
   }
 }
@@ -357,4 +629,117 @@ extern "C" int w8_lm_head_argmax_f32(const uint16_t* x, const int8_t* w, const u
   W8_CUDA_TRY(cudaMemsetAsync(best, 0, sizeof(uint64_t), st));
   return w8host::gemv_dispatch<true>(x, k, w, k, s, logits, n, 1, n, k, cap, st,
                                      reinterpret_cast<unsigned long long*>(best));
+}
+
+// ---------------------------------------------------------------- decode GEMV chain (host)
+namespace w8host {
+
+// The standalone kernel's (J, S) K split for a given K (gemv_dispatch's table).
+static void gemv_split(int k, int* J, int* S) {
+  static const int kTable[][3] = {{512, 1, 1},  {1024, 2, 1}, {1536, 3, 1}, {2048, 4, 1},  {3072, 3, 2},
+                                  {4096, 4, 2}, {6144, 3, 4}, {8192, 4, 4}, {12288, 3, 8}, {16384, 4, 8}};
+  for (const auto& e : kTable)
+    if (k <= e[0]) {
+      *J = e[1];
+      *S = e[2];
+      return;
+    }
+  *J = 4;
+  *S = 8;
+}
+
+static int chain_params(const w8_gemv_step* steps, int count, w8::ChainParams* p) {
+  W8_CHECK_ARG(count >= 0 && count <= w8::kChainMaxSteps, "chain of %d steps (1..%d supported)", count,
+               w8::kChainMaxSteps);
+  W8_CHECK_ARG(count == 0 || steps != nullptr, "null step table");
+  p->count = count;
+  for (int i = 0; i < count; ++i) {
+    const w8_gemv_step& s = steps[i];
+    W8_CHECK_ARG(s.n > 0 && s.n < (1ll << 31), "step %d: n = %lld out of range", i, (long long)s.n);
+    W8_CHECK_ARG(s.k > 0 && s.k % 16 == 0 && s.k <= w8::kChainMaxK,
+                 "step %d: k = %lld must be a positive multiple of 16 up to %d", i, (long long)s.k, w8::kChainMaxK);
+    W8_CHECK_ARG(s.x != nullptr && s.w != nullptr && s.s != nullptr && s.y != nullptr, "step %d: null pointer", i);
+    W8_CHECK_ALIGN(aligned(s.x, 16) && aligned(s.w, 16), "step %d: x and w must be 16-byte aligned", i);
+    W8_CHECK_ALIGN(aligned(s.y, s.logits ? 4 : 2) && aligned(s.s, 2), "step %d: y or s misaligned", i);
+    W8_CHECK_ARG(s.logits || s.best == nullptr, "step %d: a greedy key needs a logits step", i);
+    W8_CHECK_ALIGN(s.best == nullptr || aligned(s.best, 8), "step %d: best must be 8-byte aligned", i);
+    W8_CHECK_ARG(!s.logits || s.n < (1ll << 32) - 1, "step %d: n out of range for the argmax", i);
+    w8::ChainStep& d = p->step[i];
+    d.x = reinterpret_cast<const __nv_bfloat16*>(s.x);
+    d.w = s.w;
+    d.s = reinterpret_cast<const __nv_bfloat16*>(s.s);
+    d.y = s.y;
+    d.best = reinterpret_cast<unsigned long long*>(s.best);
+    d.n = static_cast<int>(s.n);
+    d.k = static_cast<int>(s.k);
+    d.cap = s.logits ? s.cap : 0.f;
+    d.logits = s.logits ? 1 : 0;
+    gemv_split(d.k, &d.J, &d.S);
+  }
+  return W8_OK;
+}
+
+int chain_device_status(int clear, int* out) {
+  int v = 0;
+  W8_CUDA_TRY(cudaDeviceSynchronize());
+  W8_CUDA_TRY(cudaMemcpyFromSymbol(&v, w8::g_chain_status, sizeof(int)));
+  if (clear) {
+    const int zero = 0;
+    W8_CUDA_TRY(cudaMemcpyToSymbol(w8::g_chain_status, &zero, sizeof(int)));
+  }
+  *out = v;
+  return W8_OK;
+}
+
+}  // namespace w8host
+
+extern "C" int64_t w8_gemv_chain_workspace_bytes(int count) { return count < 0 ? 0 : 4ll * (count + 2); }
+
+extern "C" int w8_gemv_chain(const w8_gemv_step* steps, int count, void* workspace, int64_t workspace_bytes,
+                             w8_stream_t stream) {
+  static w8::ChainParams params;  // large: built here, copied into the launch
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  int st = w8host::chain_params(steps, count, &params);
+  if (st != W8_OK) return st;
+  if (count == 0) return W8_OK;
+  W8_CHECK_ARG(workspace != nullptr && workspace_bytes >= w8_gemv_chain_workspace_bytes(count),
+               "workspace of %lld bytes < %lld", (long long)workspace_bytes,
+               (long long)w8_gemv_chain_workspace_bytes(count));
+  W8_CHECK_ALIGN(w8host::aligned(workspace, 4), "workspace must be 4-byte aligned");
+  params.ctr = static_cast<uint32_t*>(workspace);
+  int device = 0;
+  st = w8host::require_sm100(&device);
+  if (st != W8_OK) return st;
+  int sms = 0;
+  st = w8host::num_sms(&sms);
+  if (st != W8_OK) return st;
+  static bool done[64] = {};
+  if (!done[device]) {
+    W8_CUDA_TRY(cudaFuncSetAttribute(w8::gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     w8::kChainSmem));
+    done[device] = true;
+  }
+  int per_sm = 0;
+  W8_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, w8::gemv_chain_kernel, w8::kChainThreads,
+                                                            w8::kChainSmem));
+  if (per_sm < 1) {
+    w8host::set_error("w8_gemv_chain: the kernel does not fit on an SM");
+    return W8_ERR_UNSUPPORTED;
+  }
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (int i = 0; i < count; ++i)
+    if (params.step[i].best != nullptr) W8_CUDA_TRY(cudaMemsetAsync(params.step[i].best, 0, 8, s));
+  // One CTA per SM, all co-resident (cooperative launch): the CTAs wait on one another.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms, 1, 1);
+  cfg.blockDim = dim3(w8::kChainThreads, 1, 1);
+  cfg.dynamicSmemBytes = w8::kChainSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeCooperative;
+  attr.val.cooperative = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return w8host::cuda_status(cudaLaunchKernelEx(&cfg, w8::gemv_chain_kernel, params));
 }

@@ -346,6 +346,45 @@ def qkv_norm_rope(y, cos, sin, qw, kw, eps, heads, kv_heads, head_dim, shared=Fa
     return q, out[heads: heads + kv_heads], out[heads + kv_heads:]
 
 
+def gemm_qkv_norm_rope(xq, w, sx, sw, cos, sin, qw, kw, eps, heads, kv_heads, head_dim, shared=False, out=None):
+    """The qkv GEMM and k_qkv (pipeline.py:233-242 + :72-86): xq int8 [T, K] with row scales
+    sx, the resident qkv weight w [N, K] with channel scales sw -> (q [H, T, D], k, v), the
+    same bits as qkv_norm_rope(gemm_dequant(xq, w, sx, sw), ...).  head_dim 256 runs as one
+    kernel (the glue in the GEMM's epilogue, one head per 256-column tile, no bf16 [T, N]
+    intermediate); other head dims run the two kernels."""
+    T = xq.shape[0]
+    per_tok = heads if shared else heads + 2 * kv_heads
+    _need(w.shape[0] == per_tok * head_dim, f"w must have {per_tok * head_dim} rows")
+    if head_dim != 256:
+        return qkv_norm_rope(gemm_dequant(xq, w, sx, sw), cos, sin, qw, kw, eps, heads, kv_heads, head_dim,
+                             shared=shared, out=out)
+    _check_matrix(xq, "xq", torch.int8)
+    _check_matrix(w, "w", torch.int8)
+    K = xq.shape[1]
+    _need(w.shape[1] == K, f"inner sizes differ: xq {tuple(xq.shape)}, w {tuple(w.shape)}")
+    _check_vector(sx, "sx", torch.float32, T)
+    _check_vector(sw, "sw", torch.float32, w.shape[0])
+    _bf16_rows(cos, "cos", head_dim)
+    _bf16_rows(sin, "sin", head_dim)
+    _need(cos.shape[0] == T and sin.shape[0] == T and cos.stride(0) == sin.stride(0),
+          "cos and sin must be [T, D] with the same pitch")
+    _bf16_vec(qw, "qw", head_dim)
+    if not shared and kv_heads:
+        _bf16_vec(kw, "kw", head_dim)
+    if out is None:
+        out = torch.empty((per_tok, T, head_dim), dtype=torch.bfloat16, device=xq.device)
+    _need(out.dtype == torch.bfloat16 and out.is_cuda and tuple(out.shape) == (per_tok, T, head_dim)
+          and out.stride(2) == 1, f"out must be bf16 ({per_tok}, {T}, {head_dim}) with unit stride along D")
+    _lib.call("w8_gemm_qkv_norm_rope", xq.data_ptr(), _ld(xq), w.data_ptr(), _ld(w), sx.data_ptr(), sw.data_ptr(),
+              T, heads, kv_heads, int(bool(shared)), cos.data_ptr(), sin.data_ptr(), cos.stride(0), qw.data_ptr(),
+              None if (shared or not kv_heads) else kw.data_ptr(), float(eps), out.data_ptr(), out.stride(0),
+              out.stride(1), K, _stream(xq))
+    q = out[:heads]
+    if shared:
+        return q, q, q
+    return q, out[heads: heads + kv_heads], out[heads + kv_heads:]
+
+
 def attention_prefill(q, k, v, window=0, out=None, schedule="tc"):
     """Prefill attention of one prompt from position 0 (pipeline.py:139-180): causal, with
     a sliding window when window > 0, scale 1.0, grouped-query heads.  q bf16 [H, T, D],
@@ -516,3 +555,58 @@ def monotone_bits(f):
 def argmax_token(best):
     """Token id (0-dim int64 on the device) from the packed key of w8_lm_head_argmax_f32."""
     return (0xFFFFFFFF - (best & 0xFFFFFFFF))[0]
+
+
+# Counters of the decode chain kernel, one zero-filled buffer per (device, stream), kept
+# apart from the GEMM's so that neither can see the other's words.
+_CHAIN_WORKSPACES = {}
+
+
+class GemvChain:
+    """A decode step's GEMVs as one launch (w8_gemv_chain): the step table is built once.
+
+    `steps` is a list of (x, w, s, y) for a bf16 layer GEMV (the int8_linear of one row)
+    and (x, w, s, logits, cap) or (x, w, s, logits, cap, best) for the LM head (fp32
+    softcapped logits, and the greedy key into the int64 `best` as lm_head_logits(...,
+    argmax="key") gives it).  Steps run in order; a step's x may be the y of the step
+    before it.  Every output is bit-identical to the standalone call.  Calling the object
+    launches the chain on torch's current stream (capturable in a CUDA graph).
+    """
+
+    def __init__(self, steps):
+        _need(0 < len(steps) <= 192, f"a chain holds 1..192 steps (got {len(steps)})")
+        self._keep = []  # tensors the table points into
+        arr = (_lib.W8GemvStep * len(steps))()
+        dev = None
+        for i, st in enumerate(steps):
+            _need(len(st) in (4, 5, 6), f"step {i}: (x, w, s, y) or (x, w, s, logits, cap[, best])")
+            x, w, sc, y = st[:4]
+            logits = len(st) > 4
+            cap = float(st[4]) if logits else 0.0
+            best = st[5] if len(st) > 5 else None
+            _check_matrix(w, f"step {i} w", torch.int8)
+            n, k = w.shape
+            _need(w.is_contiguous(), f"step {i}: w must be contiguous [N, K]")
+            _need(x.is_cuda and x.dtype == torch.bfloat16 and x.numel() == k and x.is_contiguous(),
+                  f"step {i}: x must be a contiguous bf16 CUDA row of {k}")
+            _check_vector(sc, f"step {i} s", torch.bfloat16, n)
+            _check_vector(y, f"step {i} y", torch.float32 if logits else torch.bfloat16, n)
+            if best is not None:
+                _need(logits, f"step {i}: a greedy key needs a logits step")
+                _check_vector(best, f"step {i} best", torch.int64, 1)
+            dev = dev or w.device
+            _need(all(t.device == dev for t in (x, w, sc, y)), "every step must be on one device")
+            arr[i] = _lib.W8GemvStep(x.data_ptr(), w.data_ptr(), sc.data_ptr(), y.data_ptr(),
+                                     best.data_ptr() if best is not None else None, n, k, cap, 1 if logits else 0)
+            self._keep += [x, w, sc, y] + ([best] if best is not None else [])
+        self._arr, self.count, self.device = arr, len(steps), dev
+
+    def __call__(self):
+        stream = _stream(self._keep[0])
+        key = (self.device.index, stream)
+        nbytes = _lib.lib().w8_gemv_chain_workspace_bytes(self.count)
+        ws = _CHAIN_WORKSPACES.get(key)
+        if ws is None or ws.numel() * 4 < nbytes:
+            ws = torch.zeros(max(1024, -(-nbytes // 4)), dtype=torch.int32, device=self.device)
+            _CHAIN_WORKSPACES[key] = ws
+        _lib.call("w8_gemv_chain", self._arr, self.count, ws.data_ptr(), ws.numel() * 4, stream)
