@@ -313,6 +313,7 @@ def build_decode(w8, work, dev):
 
     best = torch.zeros((1,), dtype=torch.int64, device=dev)
     fused = w8.GemvChain([(x[0], wq, s, y[0]) for x, wq, s, y in chain] + [head + (SOFTCAP, best)])
+    fused_independent = w8.GemvChain([(x[0], wq, s, y[0]) for x, wq, s, y in chain], independent=True)
 
     side = [torch.cuda.Stream(device=dev) for _ in range(4)]
     layer_bytes = sum(wq.numel() + 2 * wq.shape[0] + 2 * x.numel() + 2 * y.numel() for x, wq, _, y in chain)
@@ -335,7 +336,7 @@ def build_decode(w8, work, dev):
         for ev in joins:
             cur.wait_event(ev)
 
-    return step, nbytes, len(chain) + 1, head, (step_independent, layer_bytes, len(chain)), fused
+    return step, nbytes, len(chain) + 1, head, (step_independent, layer_bytes, len(chain)), fused, fused_independent
 
 
 def prompt_lengths(count=8, seed=0, lo=200, hi=3700):
@@ -599,8 +600,7 @@ def fused_layer(w8, dev, stream, m, steps, warmup, world, layers=35):
 
 def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35, kv_shared=0):
     """One prompt through every decoder layer's linear set, glue and attention on the GPU,
-    the layer body of pipeline.py:262-310: k_in, qkv GEMM + k_qkv (one kernel for head_dim
-    256), attention, k_attn_out, o GEMM + k_post_attn, gate/up GEMM + k_gelu, down GEMM +
+    the layer body of pipeline.py:262-310: k_in, qkv GEMM + k_qkv, attention, k_attn_out, o GEMM + k_post_attn, gate/up GEMM + k_gelu, down GEMM +
     k_post_ff, PLE gate GEMM (1536 -> 256) + k_ple_gate, PLE projection GEMM (256 -> 1536) +
     k_ple_out.  Gemma E2B attention layout: every 5th layer full causal with head_dim 512
     (qkv 5120 x 1536, o 1536 x 4096), the others sliding window 512 with head_dim 256; 8
@@ -647,13 +647,12 @@ def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35, kv_shared=0
         xq, sx = w8.rms_quant(h, L[0]["w_in"], eps)
         for i, l in enumerate(L):
             d = l["d"]
+            y = w8.gemm_dequant(xq, l["qkv"][0], sx, l["qkv"][1])
             if l["shared"]:
-                q, _, _ = w8.gemm_qkv_norm_rope(xq, l["qkv"][0], sx, l["qkv"][1], *tables[d], l["qn"], None, eps, nh,
-                                                kv, d, shared=True)
+                q, _, _ = w8.qkv_norm_rope(y, *tables[d], l["qn"], None, eps, nh, kv, d, shared=True)
                 k, v = kv_store[d][:kv], kv_store[d][kv:]
             else:
-                q, k, v = w8.gemm_qkv_norm_rope(xq, l["qkv"][0], sx, l["qkv"][1], *tables[d], l["qn"], l["kn"], eps,
-                                                nh, kv, d)
+                q, k, v = w8.qkv_norm_rope(y, *tables[d], l["qn"], l["kn"], eps, nh, kv, d)
                 if i < first_shared and any(x["d"] == d for x in L[first_shared:]) and \
                         all(x["d"] != d for x in L[i + 1: first_shared]):
                     kv_store[d][:kv].copy_(k)  # the last unshared layer of this type stores its K / V
@@ -687,6 +686,40 @@ def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35, kv_shared=0
             "ms_per_prefill": ms, "linear_tops": linear_ops / (ms * 1e-3) / 1e12,
             "reference": "the reference keeps its NPU busy 2.38 s per 3658-token prefill (README.md:61-62), its CPU "
                          "attention on top"}
+
+
+def qkv_paths(w8, dev, stream, m, steps, warmup, world):
+    """The qkv GEMM + k_qkv at head_dim 256 (8 q heads, 1 KV head, M tokens), both ways:
+    the GEMM with the dequant fused then the k_qkv row kernel, and the one kernel with
+    k_qkv in the GEMM epilogue (w8_gemm_qkv_norm_rope); 8 rotated weights, us per call."""
+    nh, kv, d, k = 8, 1, 256, 1536
+    g = torch.Generator(device=dev).manual_seed(33)
+    xq, sx = w8.quant_rows(torch.randn((m, k), device=dev, generator=g, dtype=torch.bfloat16))
+    ws = [w8.quant_rows(torch.randn(((nh + 2 * kv) * d, k), device=dev, generator=g, dtype=torch.bfloat16) * 0.02)
+          for _ in range(8)]
+    ang = torch.arange(m, device=dev)[:, None].float() * (1e4 ** (-torch.arange(0, d, 2, device=dev).float() / d))[None]
+    ang = torch.cat([ang, ang], dim=-1)
+    cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    qn = torch.ones((d,), dtype=torch.bfloat16, device=dev)
+    out = torch.empty(((nh + 2 * kv), m, d), dtype=torch.bfloat16, device=dev)
+    y = torch.empty((m, (nh + 2 * kv) * d), dtype=torch.bfloat16, device=dev)
+
+    def two_step():
+        for wq, sw in ws:
+            w8.gemm_dequant(xq, wq, sx, sw, out=y)
+            w8.qkv_norm_rope(y, cos, sin, qn, qn, 1e-6, nh, kv, d, out=out)
+
+    def fused():
+        for wq, sw in ws:
+            w8.gemm_qkv_norm_rope(xq, wq, sx, sw, cos, sin, qn, qn, 1e-6, nh, kv, d, out=out)
+
+    res = {}
+    for label, fn in (("gemm_then_row_kernel", two_step), ("fused_epilogue", fused)):
+        gr = capture(fn, stream)
+        res[label + "_us"] = timed(lambda: gr.replay(), steps, warmup, stream, world) / steps * 1e3 / len(ws)
+        del gr
+    res["workload"] = f"qkv {(nh + 2 * kv) * d}x{k} at M={m} + k_qkv (D 256, H 8, KV 1)"
+    return res
 
 
 def attention_bench(w8, dev, stream, m, steps, warmup, world):
@@ -1015,7 +1048,7 @@ def main():
                                  "path": "gemma_npu_b200.mm_i8_nk per GEMM: pinned int8 activations H2D, int32 results "
                                          "D2H (pipeline.py's Prefill.gemm data flow); same three-stream pipeline"}
         if not args.no_decode and args.only is None:
-            step, nbytes, launches, head, (istep, ibytes, ilaunches), fused = build_decode(w8, work, dev)
+            step, nbytes, launches, head, (istep, ibytes, ilaunches), fused, fused_ind = build_decode(w8, work, dev)
             # The decode step as one persistent kernel (w8_gemv_chain): the headline.  One
             # launch per token, so it is timed as back-to-back launches on the stream.
             with torch.cuda.stream(stream):
@@ -1040,6 +1073,11 @@ def main():
             ims = timed(lambda: igraph.replay(), args.decode_steps, args.warmup, stream, world) / args.decode_steps
             del igraph
             igbs = ibytes / (ims * 1e-3) / 1e9
+            with torch.cuda.stream(stream):
+                fused_ind()
+            stream.synchronize()
+            fims = timed(fused_ind, args.decode_steps, args.warmup, stream, world) / args.decode_steps
+            fibgs = ibytes / (fims * 1e-3) / 1e9
             line["decode_gemv"] = {
                 "metric": "int8 GEMV GB/s, decode chain (config 2: 140 layer GEMVs + LM head 262144x1536, "
                           "softcap and greedy argmax fused, each GEMV ordered after the previous one)",
@@ -1060,11 +1098,15 @@ def main():
                 "layer_gemvs_independent": {"us": ims * 1e3, "bytes": ibytes, "gbs": igbs,
                                             "frac": igbs / pk["hbm_gbs"], "launches": ilaunches,
                                             "note": "the chain's 140 layer GEMVs with no dependence between them, "
-                                                    "one kernel each, round-robin on 4 streams inside one graph"}}
+                                                    "one kernel each, round-robin on 4 streams inside one graph"},
+                "chain_independent": {"us": fims * 1e3, "bytes": ibytes, "gbs": fibgs, "frac": fibgs / pk["hbm_gbs"],
+                                      "note": "the same 140 layer GEMVs through w8_gemv_chain with independent=1 (no "
+                                              "step waits for the one before): the chain kernel's streaming rate"}}
         if not args.no_fused and args.only is None:
             line["fused_gelu_up"] = fused_gelu_up(w8, work, dev, stream, 10, 3, world)
             line["fused_layer"] = fused_layer(w8, dev, stream, args.m, 5, 3, world)
             line["glue_rows"] = glue_rows(w8, dev, stream, args.m, 10, 3, world, pk)
+            line["qkv_paths"] = qkv_paths(w8, dev, stream, args.m, 10, 3, world)
         if not args.no_attention and args.only is None:
             line["attention"] = attention_bench(w8, dev, stream, args.m, 10, 3, world)
             line["prefill_gpu"] = prefill_gpu(w8, dev, stream, args.m, 3, 3, world)

@@ -112,7 +112,7 @@ class W8GemvStep(ctypes.Structure):
                 ("logits", ctypes.c_int)]
 
 
-SIGNATURES["w8_gemv_chain"] = (_i, [ctypes.POINTER(W8GemvStep), _i, _p, _i64, _p])
+SIGNATURES["w8_gemv_chain"] = (_i, [ctypes.POINTER(W8GemvStep), _i, _i, _p, _i64, _p])
 SIGNATURES["w8_gemv_chain_workspace_bytes"] = (_i64, [_i])
 
 _lock = threading.Lock()

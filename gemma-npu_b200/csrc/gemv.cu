@@ -298,9 +298,19 @@ struct ChainStep {
 
 struct ChainParams {
   int count;
-  uint32_t* ctr;  // workspace: ctr[i] steps done per CTA; ctr[count] CTAs gone; ctr[count + 1] abort
+  int independent;  // 1: no step reads an earlier step's output, so no step waits for the one before
+  uint32_t* ctr;    // workspace: ctr[i] steps done per CTA; ctr[count] CTAs gone; ctr[count + 1] abort
   ChainStep step[kChainMaxSteps];
 };
+
+// This CTA's share of a step's activation row, pulled into L2 ahead of its use: the row
+// is read by every CTA right after the step's dependence resolves, and an L2 hit there
+// keeps that read out of the HBM queue the weight stream fills.  A row that the previous
+// step is still writing may be fetched stale: the writes then update the L2 lines.
+__device__ __forceinline__ void chain_prefetch_x(const ChainStep& st, int b, int G) {
+  const int lines = (st.k * 2 + 127) / 128;
+  for (int l = b; l < lines; l += G) prefetch_l2(reinterpret_cast<const uint8_t*>(st.x) + l * 128);
+}
 
 __device__ __forceinline__ void chain_consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kChainConsumerWarps * 32) : "memory");
@@ -317,10 +327,10 @@ __device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
 __device__ __forceinline__ bool chain_wait_step(const uint32_t* ctr, uint32_t target, uint32_t* abort_word) {
   const unsigned long long t0 = globaltimer();
 #pragma unroll 1
-  while (true) {
+  for (uint32_t spin = 0;; ++spin) {
     if (ld_acquire_gpu(ctr) >= target) return true;
     if (ld_volatile_u32(abort_word) != 0u) return false;
-    __nanosleep(32);
+    if (spin > 4096) __nanosleep(64);  // a long wait: back off
     if (globaltimer() - t0 > kWaitTimeoutNs) {
       atomicExch(&g_chain_status, W8_ERR_DEVICE_TIMEOUT);
       atomicExch(abort_word, 1u);
@@ -358,6 +368,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
       int stage = 0;
       uint32_t phase = 0, issued = 0, last_phase = 0;
       bool ok = true;
+      const uint64_t evict_first = l2_policy_evict_first();  // weights are read once
       for (int i = 0; ok && i < p.count; ++i) {
         const ChainStep& st = p.step[i];
         const int r0 = static_cast<int>(static_cast<int64_t>(st.n) * b / G);
@@ -371,8 +382,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
           }
           const uint32_t bytes = static_cast<uint32_t>(c1 - c0) * static_cast<uint32_t>(st.k);
           mbar_arrive_expect_tx(full_bar(stage), bytes);
-          bulk_load_1d(base + kChainRingOff + stage * kChainStageBytes, st.w + static_cast<int64_t>(c0) * st.k,
-                       bytes, full_bar(stage));
+          bulk_load_1d_hint(base + kChainRingOff + stage * kChainStageBytes, st.w + static_cast<int64_t>(c0) * st.k,
+                            bytes, full_bar(stage), evict_first);
           issued |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == kChainStages) {
@@ -398,9 +409,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
     float* dq_s = reinterpret_cast<float*>(chain_smem + kChainDqOff);
     int stage = 0;
     uint32_t phase = 0;
+    if (ctid == 0) chain_prefetch_x(p.step[0], b, G);
     for (int i = 0; i < p.count; ++i) {
       const ChainStep& st = p.step[i];
-      if (i > 0) {
+      if (ctid == 0 && i + 1 < p.count) chain_prefetch_x(p.step[i + 1], b, G);
+      if (i > 0 && !p.independent) {
         if (ctid == 0 && !chain_wait_step(p.ctr + (i - 1), static_cast<uint32_t>(G), abort_word)) *abort_smem = 1;
         chain_consumer_sync();
         if (*abort_smem) break;
@@ -487,13 +500,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
       }
       if (lane == 0) {
         if (st.logits && st.best != nullptr && mine != 0ull) atomicMax(st.best, mine);
-        __threadfence();  // this warp's outputs are visible GPU-wide before the step counter moves
+        // this warp's outputs are ordered before the step counter moves
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
       }
       chain_consumer_sync();
-      if (ctid == 0) {
-        __threadfence();
-        atomicAdd(p.ctr + i, 1u);
-      }
+      if (ctid == 0 && !p.independent)
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.ctr + i) : "memory");
     }
   }
 
@@ -695,13 +707,14 @@ int chain_device_status(int clear, int* out) {
 
 extern "C" int64_t w8_gemv_chain_workspace_bytes(int count) { return count < 0 ? 0 : 4ll * (count + 2); }
 
-extern "C" int w8_gemv_chain(const w8_gemv_step* steps, int count, void* workspace, int64_t workspace_bytes,
-                             w8_stream_t stream) {
+extern "C" int w8_gemv_chain(const w8_gemv_step* steps, int count, int independent, void* workspace,
+                             int64_t workspace_bytes, w8_stream_t stream) {
   static w8::ChainParams params;  // large: built here, copied into the launch
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
   int st = w8host::chain_params(steps, count, &params);
   if (st != W8_OK) return st;
+  params.independent = independent ? 1 : 0;
   if (count == 0) return W8_OK;
   W8_CHECK_ARG(workspace != nullptr && workspace_bytes >= w8_gemv_chain_workspace_bytes(count),
                "workspace of %lld bytes < %lld", (long long)workspace_bytes,

@@ -570,10 +570,13 @@ class GemvChain:
     softcapped logits, and the greedy key into the int64 `best` as lm_head_logits(...,
     argmax="key") gives it).  Steps run in order; a step's x may be the y of the step
     before it.  Every output is bit-identical to the standalone call.  Calling the object
-    launches the chain on torch's current stream (capturable in a CUDA graph).
+    launches the chain on torch's current stream (capturable in a CUDA graph).  With
+    independent=True the caller declares that no step reads an earlier step's output, and
+    the steps do not wait for one another.
     """
 
-    def __init__(self, steps):
+    def __init__(self, steps, independent=False):
+        self.independent = bool(independent)
         _need(0 < len(steps) <= 192, f"a chain holds 1..192 steps (got {len(steps)})")
         self._keep = []  # tensors the table points into
         arr = (_lib.W8GemvStep * len(steps))()
@@ -609,4 +612,5 @@ class GemvChain:
         if ws is None or ws.numel() * 4 < nbytes:
             ws = torch.zeros(max(1024, -(-nbytes // 4)), dtype=torch.int32, device=self.device)
             _CHAIN_WORKSPACES[key] = ws
-        _lib.call("w8_gemv_chain", self._arr, self.count, ws.data_ptr(), ws.numel() * 4, stream)
+        _lib.call("w8_gemv_chain", self._arr, self.count, int(self.independent), ws.data_ptr(), ws.numel() * 4,
+                  stream)

@@ -326,11 +326,13 @@ typedef struct {
  * persistent CTA per SM streams its share of every step's weight rows ahead through
  * shared memory while the dependences resolve (a cooperative launch; the CTAs wait on
  * one another with bounded waits, W8_ERR_DEVICE_TIMEOUT on expiry).  At most 192 steps.
+ * independent != 0 declares that no step reads an earlier step's output: the steps then
+ * do not wait for one another (the weights still stream in order).
  * `workspace` holds w8_gemv_chain_workspace_bytes(count) bytes, zero-filled before its
  * first use and zero again after each call; calls that may overlap need their own.
  * The step table is read during the call (it may be freed on return). */
-int w8_gemv_chain(const w8_gemv_step* steps, int count, void* workspace, int64_t workspace_bytes,
-                  w8_stream_t stream);
+int w8_gemv_chain(const w8_gemv_step* steps, int count, int independent, void* workspace,
+                  int64_t workspace_bytes, w8_stream_t stream);
 int64_t w8_gemv_chain_workspace_bytes(int count);
 
 #ifdef __cplusplus

@@ -125,3 +125,19 @@ def test_chain_rejects_bad_steps(cuda):
         w8.GemvChain([(x, wq, s, y)])()
     with pytest.raises(ValueError):
         w8.GemvChain([])
+
+
+def test_independent_chain_matches_standalone_calls(cuda):
+    """independent=True (no waits between steps) gives the same bits on independent steps."""
+    gen = torch.Generator(device=cuda).manual_seed(6)
+    steps, want = [], []
+    for n, k in LAYER * 3:
+        wq, s = weights(n, k, gen, cuda)
+        x = row(k, gen, cuda)
+        y = torch.empty((n,), dtype=torch.bfloat16, device=cuda)
+        steps.append((x, wq, s, y))
+        want.append(w8.int8_linear(x[None], wq, s)[0])
+    w8.GemvChain(steps, independent=True)()
+    torch.cuda.synchronize()
+    for i, (st, w_) in enumerate(zip(steps, want)):
+        assert torch.equal(bits(st[3]), bits(w_)), f"step {i}"
