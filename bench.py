@@ -941,6 +941,8 @@ def main():
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 prompts / sharded LM head objects")
     ap.add_argument("--no-fused", action="store_true", help="skip the fused gate/up glue object")
     ap.add_argument("--no-attention", action="store_true", help="skip the prefill attention object")
+    ap.add_argument("--only-decode", action="store_true",
+                    help="time only the decode chain objects (--layers layers + the head; profiling captures)")
     ap.add_argument("--only-attention", action="store_true",
                     help="time only the prefill attention object (--steps / --warmup replays; profiling captures)")
     args = ap.parse_args()
@@ -969,6 +971,22 @@ def main():
             att = attention_bench(w8, dev, stream, args.m, args.steps, args.warmup, world)
             if rank == 0:
                 print(json.dumps({"attention": att}), flush=True)
+            return
+        if args.only_decode:
+            work = build_prefill(w8, dev, 16, seed=rank, layers=args.layers)
+            step, nbytes, launches, head, _, fused, fused_ind = build_decode(w8, work, dev)
+            res = {}
+            for label, fn in (("chain", fused), ("chain_independent", fused_ind)):
+                with torch.cuda.stream(stream):
+                    fn()
+                stream.synchronize()
+                res[label + "_us"] = timed(fn, args.steps, args.warmup, stream, world) / args.steps * 1e3
+            gr = capture(step, stream)
+            res["per_gemv_graph_us"] = timed(lambda: gr.replay(), args.steps, args.warmup, stream, world) / args.steps * 1e3
+            del gr
+            res["bytes_per_token"] = nbytes
+            if rank == 0:
+                print(json.dumps({"decode_only": res, "layers": args.layers}), flush=True)
             return
         if args.gemm_table:
             table = gemm_table(w8, dev, stream, args.steps, args.warmup)

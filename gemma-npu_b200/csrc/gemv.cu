@@ -271,13 +271,11 @@ constexpr int kChainMaxSteps = 192;
 constexpr int kChainConsumerWarps = 8;
 constexpr int kChainThreads = 32 * (1 + kChainConsumerWarps);
 constexpr int kChainStageBytes = 24 * 1024;
-constexpr int kChainStages = 8;
+constexpr int kChainStages = 9;
 constexpr int kChainMaxK = 12288;
 constexpr int kChainRingOff = 0;
-constexpr int kChainXhOff = kChainStages * kChainStageBytes;
-constexpr int kChainXlOff = kChainXhOff + kChainMaxK;
-constexpr int kChainDqOff = kChainXlOff + kChainMaxK;
-constexpr int kChainBarOff = kChainDqOff + (kChainMaxK / 16) * 4;
+constexpr int kChainRedOff = kChainStages * kChainStageBytes;
+constexpr int kChainBarOff = kChainRedOff + kChainConsumerWarps * 4;
 constexpr int kChainSmem = kChainBarOff + 2 * kChainStages * 8 + 16;
 static_assert(kChainSmem <= 232448, "decode chain shared memory exceeds one CTA's budget");
 static_assert(kChainStageBytes >= 2 * kChainMaxK, "a stage must hold at least two rows");
@@ -312,8 +310,20 @@ __device__ __forceinline__ void chain_prefetch_x(const ChainStep& st, int b, int
   for (int l = b; l < lines; l += G) prefetch_l2(reinterpret_cast<const uint8_t*>(st.x) + l * 128);
 }
 
-__device__ __forceinline__ void chain_consumer_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kChainConsumerWarps * 32) : "memory");
+// Barrier of the consumer warps that also ORs a flag over them: every consumer learns
+// whether any of them gave up, so they all leave the step loop together (a warp that
+// left alone would leave the others waiting at the next barrier for good).
+__device__ __forceinline__ bool chain_consumer_sync_or(bool flag) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, 1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(flag ? 1u : 0u), "n"(kChainConsumerWarps * 32)
+      : "memory");
+  return r != 0;
 }
 
 __device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
@@ -401,81 +411,87 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
         if (issued & (1u << st)) mbar_wait_bounded(full_bar(st), (last_phase >> st) & 1u, nullptr, &g_chain_status);
     }
   } else {
-    // ---------------- consumers: 8 warps, whole rows each
+    // ---------------- consumers: 8 warps in teams of S (the step's K split), as in
+    // int8_gemv_kernel: warp sl of a team owns K-slice sl, its lanes hold their pieces of
+    // the activation row as fixed point in registers, and team t finishes rows t,
+    // t + teams, ... of every chunk.
     const int cw = warp - 1;
     const int ctid = threadIdx.x - 32;
-    uint8_t* xh_s = chain_smem + kChainXhOff;
-    uint8_t* xl_s = chain_smem + kChainXlOff;
-    float* dq_s = reinterpret_cast<float*>(chain_smem + kChainDqOff);
+    float* red = reinterpret_cast<float*>(chain_smem + kChainRedOff);  // [8] team partial sums
     int stage = 0;
     uint32_t phase = 0;
     if (ctid == 0) chain_prefetch_x(p.step[0], b, G);
     for (int i = 0; i < p.count; ++i) {
       const ChainStep& st = p.step[i];
+      const int k = st.k, J = st.J, S = st.S;
+      const int teams = kChainConsumerWarps / S, team = cw / S, sl = cw % S;
       if (ctid == 0 && i + 1 < p.count) chain_prefetch_x(p.step[i + 1], b, G);
       if (i > 0 && !p.independent) {
-        if (ctid == 0 && !chain_wait_step(p.ctr + (i - 1), static_cast<uint32_t>(G), abort_word)) *abort_smem = 1;
-        chain_consumer_sync();
-        if (*abort_smem) break;
+        const bool gave_up = ctid == 0 && !chain_wait_step(p.ctr + (i - 1), static_cast<uint32_t>(G), abort_word);
+        if (chain_consumer_sync_or(gave_up)) {
+          if (ctid == 0) *abort_smem = 1;  // the producer stops too
+          break;
+        }
       }
-      // This step's activation row -> per-piece fixed point in shared memory.  x may be the
-      // previous step's output, written by other SMs: read it from L2 (ld.global.cg).
-      const int pieces = st.k / 16;
-      for (int pc = ctid; pc < pieces; pc += kChainConsumerWarps * 32) {
-        const uint4* src = reinterpret_cast<const uint4*>(st.x + pc * 16);
-        uint4 a, c;
-        asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w) : "l"(src));
-        asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(c.x), "=r"(c.y), "=r"(c.z), "=r"(c.w) : "l"(src + 1));
-        const uint32_t words[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-        uint32_t xh[4], xl[4];
-        dq_s[pc] = piece_codes(words, xh, xl);
-        *reinterpret_cast<uint4*>(xh_s + pc * 16) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
-        *reinterpret_cast<uint4*>(xl_s + pc * 16) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
+      // This lane's J pieces of the activation row.  x may be the previous step's output,
+      // written by other SMs: read it from L2 (ld.global.cg).
+      uint32_t xh[4][4], xl[4][4];
+      float dq[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t words[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+        const int k0 = ((sl * J + c) * 32 + lane) * 16;
+        if (c < J && k0 < k) {
+          const uint4* src = reinterpret_cast<const uint4*>(st.x + k0);
+          uint4 a, e;
+          asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w) : "l"(src));
+          asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(e.x), "=r"(e.y), "=r"(e.z), "=r"(e.w) : "l"(src + 1));
+          words[0] = a.x, words[1] = a.y, words[2] = a.z, words[3] = a.w;
+          words[4] = e.x, words[5] = e.y, words[6] = e.z, words[7] = e.w;
+        }
+        dq[c] = piece_codes(words, xh[c], xl[c]);
       }
-      chain_consumer_sync();
 
       const int r0 = static_cast<int>(static_cast<int64_t>(st.n) * b / G);
       const int r1 = static_cast<int>(static_cast<int64_t>(st.n) * (b + 1) / G);
-      const int rpc = kChainStageBytes / st.k;
-      const int J = st.J, S = st.S;
+      const int rpc = kChainStageBytes / k;
       unsigned long long mine = 0ull;
-      bool ok = true;
+      // A warp whose wait gave up keeps walking the chunks (and every team barrier) without
+      // touching their data, so the barriers stay matched; the step's closing barrier then
+      // tells every consumer.
+      bool failed = false;
       for (int c0 = r0; c0 < r1; c0 += rpc) {
         const int c1 = min(c0 + rpc, r1);
         // Every lane waits on the stage's barrier itself: each reader of the copied rows
         // observes their completion.
-        const bool got = mbar_wait_bounded(full_bar(stage), phase, abort_smem, &g_chain_status);
-        if (!__all_sync(0xffffffffu, got)) {
-          ok = false;
-          break;
-        }
+        const bool got = !failed && mbar_wait_bounded(full_bar(stage), phase, abort_smem, &g_chain_status);
+        if (!__all_sync(0xffffffffu, got)) failed = true;
         const uint8_t* ring = chain_smem + kChainRingOff + stage * kChainStageBytes;
-        for (int r = cw; r < c1 - c0; r += kChainConsumerWarps) {
-          const uint8_t* wrow = ring + static_cast<int64_t>(r) * st.k;
-          float total = 0.f;
-          for (int sl = 0; sl < S; ++sl) {
-            float v = 0.f;
-            for (int c = 0; c < J; ++c) {
-              const int pc = (sl * J + c) * 32 + lane;
-              int hi = 0, lo = 0;
-              float d = 0.f;
-              if (pc < pieces) {
-                const uint4 wv = *reinterpret_cast<const uint4*>(wrow + pc * 16);
-                const uint4 h4 = *reinterpret_cast<const uint4*>(xh_s + pc * 16);
-                const uint4 l4 = *reinterpret_cast<const uint4*>(xl_s + pc * 16);
-                const uint32_t xh[4] = {h4.x, h4.y, h4.z, h4.w};
-                const uint32_t xl[4] = {l4.x, l4.y, l4.z, l4.w};
-                dot16_q(wv, xh, xl, hi, lo);
-                d = dq_s[pc];
-              }
-              v = fmaf(static_cast<float>(256 * hi + lo), d, v);
-            }
+        for (int r = team; r < c1 - c0; r += teams) {
+          const uint8_t* wrow = ring + static_cast<int64_t>(r) * k;
+          float v = 0.f;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            total = sl == 0 ? v : total + v;
+          for (int c = 0; c < 4; ++c) {
+            if (c >= J || failed) break;
+            const int k0 = ((sl * J + c) * 32 + lane) * 16;
+            int hi = 0, lo = 0;
+            if (k0 < k) dot16_q(*reinterpret_cast<const uint4*>(wrow + k0), xh[c], xl[c], hi, lo);
+            v = fmaf(static_cast<float>(256 * hi + lo), dq[c], v);
           }
-          if (lane == 0) {
-            const int row = c0 + r;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          const int row = c0 + r;
+          float total = v;
+          if (S > 1) {  // the team's K-slices meet in shared memory, in slice order
+            if (lane == 0) red[cw] = v;
+            asm volatile("bar.sync %0, %1;" ::"r"(2 + team), "r"(S * 32) : "memory");
+            if (sl == 0 && lane == 0) {
+              total = red[team * S];
+              for (int q = 1; q < S; ++q) total += red[team * S + q];
+            }
+            asm volatile("bar.sync %0, %1;" ::"r"(2 + team), "r"(S * 32) : "memory");
+          }
+          if (sl == 0 && lane == 0 && !failed) {
             if (st.logits) {
               const float f = write_out<true>(st.y, row, total, st.s[row], st.cap);
               if (st.best != nullptr) mine = max(mine, argmax_key(f, row));
@@ -491,19 +507,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
           phase ^= 1u;
         }
       }
-      if (!ok) {
-        if (lane == 0) {
+      if (lane == 0 && !failed && st.logits && st.best != nullptr && mine != 0ull) atomicMax(st.best, mine);
+      // Every consumer warp's outputs of this step are stored; one release publishes them.
+      if (chain_consumer_sync_or(failed)) {
+        if (ctid == 0) {
           *abort_smem = 1;
           atomicExch(abort_word, 1u);
         }
         break;
       }
-      if (lane == 0) {
-        if (st.logits && st.best != nullptr && mine != 0ull) atomicMax(st.best, mine);
-        // this warp's outputs are ordered before the step counter moves
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
-      }
-      chain_consumer_sync();
       if (ctid == 0 && !p.independent)
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.ctr + i) : "memory");
     }
