@@ -443,9 +443,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
         const int k0 = ((sl * J + c) * 32 + lane) * 16;
         if (c < J && k0 < k) {
           const uint4* src = reinterpret_cast<const uint4*>(st.x + k0);
-          uint4 a, e;
-          asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w) : "l"(src));
-          asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(e.x), "=r"(e.y), "=r"(e.z), "=r"(e.w) : "l"(src + 1));
+          const uint4 a = __ldcg(src), e = __ldcg(src + 1);
           words[0] = a.x, words[1] = a.y, words[2] = a.z, words[3] = a.w;
           words[4] = e.x, words[5] = e.y, words[6] = e.z, words[7] = e.w;
         }
@@ -467,7 +465,18 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
         const bool got = !failed && mbar_wait_bounded(full_bar(stage), phase, abort_smem, &g_chain_status);
         if (!__all_sync(0xffffffffu, got)) failed = true;
         const uint8_t* ring = chain_smem + kChainRingOff + stage * kChainStageBytes;
-        for (int r = team; r < c1 - c0; r += teams) {
+        // The channel scales of this team's rows in the chunk, fetched up front (lane j holds
+        // the scale of the team's j-th row of each group of 32): a load per row at its store
+        // would hold the whole warp for a memory round trip on every row.
+        uint32_t s_mine = 0u;
+        for (int r = team, j = 0; r < c1 - c0; r += teams, ++j) {
+          if ((j & 31) == 0) {
+            const int rr = r + lane * teams;
+            s_mine = (!failed && rr < c1 - c0) ? static_cast<uint32_t>(__ldg(
+                                                    reinterpret_cast<const unsigned short*>(st.s) + c0 + rr))
+                                               : 0u;
+          }
+          const uint32_t s_bits = __shfl_sync(0xffffffffu, s_mine, j & 31);
           const uint8_t* wrow = ring + static_cast<int64_t>(r) * k;
           float v = 0.f;
 #pragma unroll
@@ -492,11 +501,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
             asm volatile("bar.sync %0, %1;" ::"r"(2 + team), "r"(S * 32) : "memory");
           }
           if (sl == 0 && lane == 0 && !failed) {
+            const __nv_bfloat16 sc = __ushort_as_bfloat16(static_cast<unsigned short>(s_bits));
             if (st.logits) {
-              const float f = write_out<true>(st.y, row, total, st.s[row], st.cap);
+              const float f = write_out<true>(st.y, row, total, sc, st.cap);
               if (st.best != nullptr) mine = max(mine, argmax_key(f, row));
             } else {
-              write_out<false>(st.y, row, total, st.s[row], 0.f);
+              write_out<false>(st.y, row, total, sc, 0.f);
             }
           }
         }
