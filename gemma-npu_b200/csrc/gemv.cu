@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
       bool ok = true;
       const uint64_t evict_first = l2_policy_evict_first();  // weights are read once
       for (int i = 0; ok && i < p.count; ++i) {
-        const ChainStep& st = p.step[i];
+        const ChainStep st = p.step[i];
         const int r0 = static_cast<int>(static_cast<int64_t>(st.n) * b / G);
         const int r1 = static_cast<int>(static_cast<int64_t>(st.n) * (b + 1) / G);
         const int rpc = kChainStageBytes / st.k;  // whole rows per chunk
@@ -422,7 +422,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_chain_kernel(const __gr
     uint32_t phase = 0;
     if (ctid == 0) chain_prefetch_x(p.step[0], b, G);
     for (int i = 0; i < p.count; ++i) {
-      const ChainStep& st = p.step[i];
+      // The step's fields in registers: read through a reference into the kernel's
+      // parameters, each use in the row loop would be a load of its own.
+      const ChainStep st = p.step[i];
       const int k = st.k, J = st.J, S = st.S;
       const int teams = kChainConsumerWarps / S, team = cw / S, sl = cw % S;
       if (ctid == 0 && i + 1 < p.count) chain_prefetch_x(p.step[i + 1], b, G);
