@@ -311,9 +311,6 @@ def build_decode(w8, work, dev):
         h, hq, hsc, logits = head
         w8.lm_head_logits(h, hq, hsc, SOFTCAP, out=logits, argmax=True)  # + the greedy token
 
-    best = torch.zeros((1,), dtype=torch.int64, device=dev)
-    fused = w8.GemvChain([(x[0], wq, s, y[0]) for x, wq, s, y in chain] + [head + (SOFTCAP, best)])
-    fused_independent = w8.GemvChain([(x[0], wq, s, y[0]) for x, wq, s, y in chain], independent=True)
 
     side = [torch.cuda.Stream(device=dev) for _ in range(4)]
     layer_bytes = sum(wq.numel() + 2 * wq.shape[0] + 2 * x.numel() + 2 * y.numel() for x, wq, _, y in chain)
@@ -336,7 +333,7 @@ def build_decode(w8, work, dev):
         for ev in joins:
             cur.wait_event(ev)
 
-    return step, nbytes, len(chain) + 1, head, (step_independent, layer_bytes, len(chain)), fused, fused_independent
+    return step, nbytes, len(chain) + 1, head, (step_independent, layer_bytes, len(chain))
 
 
 def prompt_lengths(count=8, seed=0, lo=200, hi=3700):
@@ -941,8 +938,6 @@ def main():
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 prompts / sharded LM head objects")
     ap.add_argument("--no-fused", action="store_true", help="skip the fused gate/up glue object")
     ap.add_argument("--no-attention", action="store_true", help="skip the prefill attention object")
-    ap.add_argument("--only-decode", action="store_true",
-                    help="time only the decode chain objects (--layers layers + the head; profiling captures)")
     ap.add_argument("--only-attention", action="store_true",
                     help="time only the prefill attention object (--steps / --warmup replays; profiling captures)")
     args = ap.parse_args()
@@ -971,22 +966,6 @@ def main():
             att = attention_bench(w8, dev, stream, args.m, args.steps, args.warmup, world)
             if rank == 0:
                 print(json.dumps({"attention": att}), flush=True)
-            return
-        if args.only_decode:
-            work = build_prefill(w8, dev, 16, seed=rank, layers=args.layers)
-            step, nbytes, launches, head, _, fused, fused_ind = build_decode(w8, work, dev)
-            res = {}
-            for label, fn in (("chain", fused), ("chain_independent", fused_ind)):
-                with torch.cuda.stream(stream):
-                    fn()
-                stream.synchronize()
-                res[label + "_us"] = timed(fn, args.steps, args.warmup, stream, world) / args.steps * 1e3
-            gr = capture(step, stream)
-            res["per_gemv_graph_us"] = timed(lambda: gr.replay(), args.steps, args.warmup, stream, world) / args.steps * 1e3
-            del gr
-            res["bytes_per_token"] = nbytes
-            if rank == 0:
-                print(json.dumps({"decode_only": res, "layers": args.layers}), flush=True)
             return
         if args.gemm_table:
             table = gemm_table(w8, dev, stream, args.steps, args.warmup)
@@ -1066,16 +1045,7 @@ def main():
                                  "path": "gemma_npu_b200.mm_i8_nk per GEMM: pinned int8 activations H2D, int32 results "
                                          "D2H (pipeline.py's Prefill.gemm data flow); same three-stream pipeline"}
         if not args.no_decode and args.only is None:
-            step, nbytes, launches, head, (istep, ibytes, ilaunches), fused, fused_ind = build_decode(w8, work, dev)
-            # The decode step as one persistent kernel (w8_gemv_chain): the headline.  One
-            # launch per token, so it is timed as back-to-back launches on the stream.
-            with torch.cuda.stream(stream):
-                fused()
-            stream.synchronize()
-            cms = timed(fused, args.decode_steps, args.warmup, stream, world)
-            cper = cms / args.decode_steps
-            cgbs = nbytes / (cper * 1e-3) / 1e9
-            # The same chain as one kernel per GEMV in a graph (programmatic dependent launch).
+            step, nbytes, launches, head, (istep, ibytes, ilaunches) = build_decode(w8, work, dev)
             dgraph = capture(step, stream)
             dms = timed(lambda: dgraph.replay(), args.decode_steps, args.warmup, stream, world)
             per = dms / args.decode_steps
@@ -1091,35 +1061,22 @@ def main():
             ims = timed(lambda: igraph.replay(), args.decode_steps, args.warmup, stream, world) / args.decode_steps
             del igraph
             igbs = ibytes / (ims * 1e-3) / 1e9
-            with torch.cuda.stream(stream):
-                fused_ind()
-            stream.synchronize()
-            fims = timed(fused_ind, args.decode_steps, args.warmup, stream, world) / args.decode_steps
-            fibgs = ibytes / (fims * 1e-3) / 1e9
             line["decode_gemv"] = {
                 "metric": "int8 GEMV GB/s, decode chain (config 2: 140 layer GEMVs + LM head 262144x1536, "
-                          "softcap and greedy argmax fused, each GEMV ordered after the previous one)",
-                "value": world * cgbs, "unit": "GB/s", "ms_per_token": cper, "bytes_per_token": nbytes,
-                "launches_per_token": 1,
-                "path": "w8_gemv_chain: one persistent kernel, one CTA per SM; each SM streams its rows of every "
-                        "GEMV through shared memory, each GEMV's activation read waits on a grid-wide counter",
-                "roofline": {"bound": "hbm", "achieved": cgbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                             "frac": cgbs / pk["hbm_gbs"], "traffic": None,
+                          "softcap and greedy argmax fused, one CUDA graph, each GEMV ordered after the previous one)",
+                "value": world * gbs, "unit": "GB/s", "ms_per_token": per, "bytes_per_token": nbytes,
+                "launches_per_token": launches,
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                             "frac": gbs / pk["hbm_gbs"], "traffic": None,
                              "peak_note": f"{pk['source']} HBM copy bandwidth"},
-                "per_gemv_kernels": {"ms_per_token": per, "gbs": gbs, "frac": gbs / pk["hbm_gbs"],
-                                     "launches_per_token": launches,
-                                     "note": "the same chain as one int8_gemv_kernel per GEMV, captured in one "
-                                             "graph with programmatic dependent launch"},
                 "lm_head": {"us": hms * 1e3, "bytes": head_bytes, "gbs": head_gbs,
                             "frac": head_gbs / pk["hbm_gbs"],
-                            "note": "the 262144x1536 head GEMV alone (402.7 MB int8)"},
+                            "note": "the 262144x1536 head GEMV alone (402.7 MB int8): the chain's per-layer "
+                                    "GEMVs (3.1-18.9 MB) are bound by the dependent step's latency, not bandwidth"},
                 "layer_gemvs_independent": {"us": ims * 1e3, "bytes": ibytes, "gbs": igbs,
                                             "frac": igbs / pk["hbm_gbs"], "launches": ilaunches,
                                             "note": "the chain's 140 layer GEMVs with no dependence between them, "
-                                                    "one kernel each, round-robin on 4 streams inside one graph"},
-                "chain_independent": {"us": fims * 1e3, "bytes": ibytes, "gbs": fibgs, "frac": fibgs / pk["hbm_gbs"],
-                                      "note": "the same 140 layer GEMVs through w8_gemv_chain with independent=1 (no "
-                                              "step waits for the one before): the chain kernel's streaming rate"}}
+                                                    "round-robin on 4 streams inside one graph so that they overlap"}}
         if not args.no_fused and args.only is None:
             line["fused_gelu_up"] = fused_gelu_up(w8, work, dev, stream, 10, 3, world)
             line["fused_layer"] = fused_layer(w8, dev, stream, args.m, 5, 3, world)

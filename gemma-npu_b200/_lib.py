@@ -105,16 +105,6 @@ SIGNATURES = {
     "w8_lm_head_argmax_f32": (_i, [_p, _p, _p, _f, _p, _i64, _i64, _p, _p]),
 }
 
-class W8GemvStep(ctypes.Structure):
-    """w8_gemv_step (w8a8_b200.h): one GEMV of a decode chain."""
-    _fields_ = [("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("s", ctypes.c_void_p), ("y", ctypes.c_void_p),
-                ("best", ctypes.c_void_p), ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("cap", ctypes.c_float),
-                ("logits", ctypes.c_int)]
-
-
-SIGNATURES["w8_gemv_chain"] = (_i, [ctypes.POINTER(W8GemvStep), _i, _i, _p, _i64, _p])
-SIGNATURES["w8_gemv_chain_workspace_bytes"] = (_i64, [_i])
-
 _lock = threading.Lock()
 _lib = None
 

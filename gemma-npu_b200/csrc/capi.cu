@@ -67,7 +67,6 @@ int num_sms(int* out) {
 
 int gemm_device_status(int clear, int* out);
 int attention_device_status(int clear, int* out);
-int chain_device_status(int clear, int* out);
 
 }  // namespace w8host
 
@@ -97,8 +96,5 @@ extern "C" int w8_device_status(int clear) {
   int va = W8_OK;
   st = w8host::attention_device_status(clear, &va);
   if (st != W8_OK) return st;
-  int vc = W8_OK;
-  st = w8host::chain_device_status(clear, &vc);
-  if (st != W8_OK) return st;
-  return v != W8_OK ? v : (va != W8_OK ? va : vc);
+  return v != W8_OK ? v : va;
 }

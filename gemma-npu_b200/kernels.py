@@ -556,61 +556,3 @@ def argmax_token(best):
     """Token id (0-dim int64 on the device) from the packed key of w8_lm_head_argmax_f32."""
     return (0xFFFFFFFF - (best & 0xFFFFFFFF))[0]
 
-
-# Counters of the decode chain kernel, one zero-filled buffer per (device, stream), kept
-# apart from the GEMM's so that neither can see the other's words.
-_CHAIN_WORKSPACES = {}
-
-
-class GemvChain:
-    """A decode step's GEMVs as one launch (w8_gemv_chain): the step table is built once.
-
-    `steps` is a list of (x, w, s, y) for a bf16 layer GEMV (the int8_linear of one row)
-    and (x, w, s, logits, cap) or (x, w, s, logits, cap, best) for the LM head (fp32
-    softcapped logits, and the greedy key into the int64 `best` as lm_head_logits(...,
-    argmax="key") gives it).  Steps run in order; a step's x may be the y of the step
-    before it.  Every output is bit-identical to the standalone call.  Calling the object
-    launches the chain on torch's current stream (capturable in a CUDA graph).  With
-    independent=True the caller declares that no step reads an earlier step's output, and
-    the steps do not wait for one another.
-    """
-
-    def __init__(self, steps, independent=False):
-        self.independent = bool(independent)
-        _need(0 < len(steps) <= 192, f"a chain holds 1..192 steps (got {len(steps)})")
-        self._keep = []  # tensors the table points into
-        arr = (_lib.W8GemvStep * len(steps))()
-        dev = None
-        for i, st in enumerate(steps):
-            _need(len(st) in (4, 5, 6), f"step {i}: (x, w, s, y) or (x, w, s, logits, cap[, best])")
-            x, w, sc, y = st[:4]
-            logits = len(st) > 4
-            cap = float(st[4]) if logits else 0.0
-            best = st[5] if len(st) > 5 else None
-            _check_matrix(w, f"step {i} w", torch.int8)
-            n, k = w.shape
-            _need(w.is_contiguous(), f"step {i}: w must be contiguous [N, K]")
-            _need(x.is_cuda and x.dtype == torch.bfloat16 and x.numel() == k and x.is_contiguous(),
-                  f"step {i}: x must be a contiguous bf16 CUDA row of {k}")
-            _check_vector(sc, f"step {i} s", torch.bfloat16, n)
-            _check_vector(y, f"step {i} y", torch.float32 if logits else torch.bfloat16, n)
-            if best is not None:
-                _need(logits, f"step {i}: a greedy key needs a logits step")
-                _check_vector(best, f"step {i} best", torch.int64, 1)
-            dev = dev or w.device
-            _need(all(t.device == dev for t in (x, w, sc, y)), "every step must be on one device")
-            arr[i] = _lib.W8GemvStep(x.data_ptr(), w.data_ptr(), sc.data_ptr(), y.data_ptr(),
-                                     best.data_ptr() if best is not None else None, n, k, cap, 1 if logits else 0)
-            self._keep += [x, w, sc, y] + ([best] if best is not None else [])
-        self._arr, self.count, self.device = arr, len(steps), dev
-
-    def __call__(self):
-        stream = _stream(self._keep[0])
-        key = (self.device.index, stream)
-        nbytes = _lib.lib().w8_gemv_chain_workspace_bytes(self.count)
-        ws = _CHAIN_WORKSPACES.get(key)
-        if ws is None or ws.numel() * 4 < nbytes:
-            ws = torch.zeros(max(1024, -(-nbytes // 4)), dtype=torch.int32, device=self.device)
-            _CHAIN_WORKSPACES[key] = ws
-        _lib.call("w8_gemv_chain", self._arr, self.count, int(self.independent), ws.data_ptr(), ws.numel() * 4,
-                  stream)

@@ -20,8 +20,6 @@
  *   w8_int8_linear_bf16     gemma_npu.py:155-156 (cpu_int8_linear = torch._weight_int8pack_mm)
  *   w8_lm_head_f32          gemma_npu.py:170-172 (Int8Head.forward) + pipeline.py:335-338 (softcap)
  *   w8_lm_head_argmax_f32   the same + the greedy token argmax (gemma_npu.py:291)
- *   w8_gemv_chain           a decode step's per-layer cpu_int8_linear calls (gemma_npu.py:155-156)
- *                           and the LM head (gemma_npu.py:170-172, pipeline.py:335-338) in order
  *   w8_gemm_gelu_up_quant   pipeline.py:102-107 (k_gelu) fused onto the gate/up GEMM of
  *                           pipeline.py:233-242 (Prefill.gemm)
  *   w8_rms_quant_bf16       pipeline.py:66-69 (k_in)
@@ -303,37 +301,6 @@ int w8_lm_head_f32(const uint16_t* x, const int8_t* w, const uint16_t* s, float 
  * first; each warp folds its rows into it with one 64-bit atomicMax. */
 int w8_lm_head_argmax_f32(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap,
                           float* logits, int64_t n, int64_t k, uint64_t* best, w8_stream_t stream);
-
-/* One GEMV of a decode chain: y = w8_int8_linear_bf16 of one row (logits == 0: bf16 y [n])
- * or w8_lm_head_f32 / w8_lm_head_argmax_f32 (logits != 0: fp32 softcapped logits [n], the
- * greedy key into *best when best != NULL).  w is [n, k] row-major with row pitch k. */
-typedef struct {
-  const uint16_t* x; /* bf16 [k], 16-byte aligned                         */
-  const int8_t* w;   /* int8 [n, k], pitch k, 16-byte aligned              */
-  const uint16_t* s; /* bf16 [n] per-channel scales                       */
-  void* y;           /* bf16 [n], or fp32 [n] for a logits step            */
-  uint64_t* best;    /* logits step only: greedy key (as w8_lm_head_argmax_f32), or NULL */
-  int64_t n, k;      /* k % 16 == 0, k <= 12288                           */
-  float cap;         /* logits step: softcap (0 = none)                   */
-  int logits;
-} w8_gemv_step;
-
-/* A decode step's chain of weight-only int8 GEMVs (gemma_npu.py:155-156 per layer, then
- * Int8Head + the softcap, gemma_npu.py:170-172 / pipeline.py:335-338, and the greedy
- * argmax, gemma_npu.py:291) in one launch.  Steps run in order: step i + 1 reads its x
- * only after every output of step i is stored, so x of a step may be the y of the step
- * before it.  Each output is bit-identical to the standalone call of that step.  One
- * persistent CTA per SM streams its share of every step's weight rows ahead through
- * shared memory while the dependences resolve (a cooperative launch; the CTAs wait on
- * one another with bounded waits, W8_ERR_DEVICE_TIMEOUT on expiry).  At most 192 steps.
- * independent != 0 declares that no step reads an earlier step's output: the steps then
- * do not wait for one another (the weights still stream in order).
- * `workspace` holds w8_gemv_chain_workspace_bytes(count) bytes, zero-filled before its
- * first use and zero again after each call; calls that may overlap need their own.
- * The step table is read during the call (it may be freed on return). */
-int w8_gemv_chain(const w8_gemv_step* steps, int count, int independent, void* workspace,
-                  int64_t workspace_bytes, w8_stream_t stream);
-int64_t w8_gemv_chain_workspace_bytes(int count);
 
 #ifdef __cplusplus
 }
