@@ -370,6 +370,12 @@ def prompts_dp(w8, dev, stream, world, rank, steps, warmup):
             "partition": "rows"}
 
 
+def _head_weight(dev):
+    """The config-4 LM head weight (seeded, the same on every rank)."""
+    g = torch.Generator(device=dev).manual_seed(77)
+    return torch.randn((VOCAB, HIDDEN), device=dev, generator=g, dtype=torch.bfloat16) * 0.02
+
+
 def sharded_head(w8, dev, stream, world, steps, warmup, pk):
     """Config 4: the 262144-wide LM head column-sharded over the N ranks (local int8 GEMV
     with the softcap + NCCL all-gather of the fp32 logits), time per token, max over ranks.
@@ -379,11 +385,8 @@ def sharded_head(w8, dev, stream, world, steps, warmup, pk):
     share of a token is measured, not inferred.  The eager path is reported beside it."""
     import torch.distributed as dist
 
-    g = torch.Generator(device=dev).manual_seed(77)
-    weight = torch.randn((VOCAB, HIDDEN), device=dev, generator=g, dtype=torch.bfloat16) * 0.02
-    head = w8.ShardedInt8Head(weight, device=dev, cap=SOFTCAP)
-    del weight
-    h = torch.randn((HIDDEN,), device=dev, generator=g).to(torch.bfloat16)
+    head = w8.ShardedInt8Head(_head_weight(dev), device=dev, cap=SOFTCAP)
+    h = torch.randn((HIDDEN,), device=dev, generator=torch.Generator(device=dev).manual_seed(78)).to(torch.bfloat16)
     eager_ms = timed(lambda: head(h), steps, warmup, stream, world) / steps
     graph = capture(lambda: head(h), stream)
     ms = timed(lambda: graph.replay(), steps, warmup, stream, world) / steps
@@ -399,9 +402,25 @@ def sharded_head(w8, dev, stream, world, steps, warmup, pk):
         agraph = capture(lambda: dist.all_gather_into_tensor(head.full, head.local), stream)
         ag_ms = timed(lambda: agraph.replay(), steps, warmup, stream, world) / steps
         del agraph
+    peer = {}
+    if world > 1:
+        # the all-gather inside the GEMV: every logit stored into every rank's buffer over NVLink
+        head_p = w8.ShardedInt8Head(_head_weight(dev), device=dev, cap=SOFTCAP, transport="peer")
+        pgraph = capture(lambda: head_p(h), stream)
+        pms = timed(lambda: pgraph.replay(), steps, warmup, stream, world) / steps
+        del pgraph
+        pggraph = capture(lambda: head_p.greedy(h), stream)
+        pgms = timed(lambda: pggraph.replay(), steps, warmup, stream, world) / steps
+        del pggraph
+        torch.cuda.synchronize()
+        peer = {"us_per_token_peer": pms * 1e3, "us_per_token_peer_greedy": pgms * 1e3,
+                "peer_note": "w8_lm_head_peer_f32: one kernel per rank, each logit stored into every rank's gathered "
+                             "buffer through CUDA IPC peer pointers, ready/done flags in the same buffers; no NCCL"}
+        head_p.close()
     shard_bytes = (head.r1 - head.r0) * (HIDDEN + 2)
     return {"workload": f"config 4: LM head {VOCAB}x{HIDDEN} int8 split by rows over {world} GPU(s), "
                         "fused softcap, NCCL all-gather of fp32 logits" + (" (no collective at N=1)" if world == 1 else ""),
+            **peer,
             "us_per_token": ms * 1e3, "us_per_token_eager": eager_ms * 1e3, "us_per_token_greedy": gms * 1e3,
             "us_local_gemv": lms * 1e3, "us_allgather": None if ag_ms is None else ag_ms * 1e3,
             "shard_rows": head.r1 - head.r0, "local_gemv_gbs": shard_bytes / (lms * 1e-3) / 1e9,

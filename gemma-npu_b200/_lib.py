@@ -105,6 +105,16 @@ SIGNATURES = {
     "w8_lm_head_argmax_f32": (_i, [_p, _p, _p, _f, _p, _i64, _i64, _p, _p]),
 }
 
+SIGNATURES.update({
+    "w8_lm_head_peer_bytes": (_i64, [_i64]),
+    "w8_peer_alloc": (_i, [_i64, ctypes.POINTER(ctypes.c_void_p), _p]),
+    "w8_peer_open": (_i, [_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "w8_peer_close": (_i, [_p]),
+    "w8_peer_free": (_i, [_p]),
+    "w8_lm_head_peer_f32": (_i, [_p, _p, _p, _f, _i64, _i64, _i64, _i64, _i, _i, ctypes.POINTER(ctypes.c_void_p), _p,
+                                 _p]),
+})
+
 _lock = threading.Lock()
 _lib = None
 

@@ -67,6 +67,7 @@ int num_sms(int* out) {
 
 int gemm_device_status(int clear, int* out);
 int attention_device_status(int clear, int* out);
+int peer_device_status(int clear, int* out);
 
 }  // namespace w8host
 
@@ -96,5 +97,8 @@ extern "C" int w8_device_status(int clear) {
   int va = W8_OK;
   st = w8host::attention_device_status(clear, &va);
   if (st != W8_OK) return st;
-  return v != W8_OK ? v : va;
+  int vp = W8_OK;
+  st = w8host::peer_device_status(clear, &vp);
+  if (st != W8_OK) return st;
+  return v != W8_OK ? v : (va != W8_OK ? va : vp);
 }

@@ -20,6 +20,7 @@
  *   w8_int8_linear_bf16     gemma_npu.py:155-156 (cpu_int8_linear = torch._weight_int8pack_mm)
  *   w8_lm_head_f32          gemma_npu.py:170-172 (Int8Head.forward) + pipeline.py:335-338 (softcap)
  *   w8_lm_head_argmax_f32   the same + the greedy token argmax (gemma_npu.py:291)
+ *   w8_lm_head_peer_f32     the same split by rows over a node's GPUs, all-gathered over NVLink
  *   w8_gemm_gelu_up_quant   pipeline.py:102-107 (k_gelu) fused onto the gate/up GEMM of
  *                           pipeline.py:233-242 (Prefill.gemm)
  *   w8_rms_quant_bf16       pipeline.py:66-69 (k_in)
@@ -301,6 +302,41 @@ int w8_lm_head_f32(const uint16_t* x, const int8_t* w, const uint16_t* s, float 
  * first; each warp folds its rows into it with one 64-bit atomicMax. */
 int w8_lm_head_argmax_f32(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap,
                           float* logits, int64_t n, int64_t k, uint64_t* best, w8_stream_t stream);
+
+/* ---- column-sharded LM head with the all-gather over NVLink peer memory ---- */
+
+/* Bytes of the gathered-logits buffer every rank holds for w8_lm_head_peer_f32:
+ * the fp32 logits [vocab, padded to 64] plus 256 bytes of flags and keys. */
+int64_t w8_lm_head_peer_bytes(int64_t vocab);
+/* A zero-filled device buffer other processes of the node can map: *ptr gets it and
+ * `handle` (64 bytes, a cudaIpcMemHandle_t) the handle to send to them.  Free with
+ * w8_peer_free. */
+int w8_peer_alloc(int64_t bytes, void** ptr, void* handle);
+/* Map another process's buffer from its 64-byte handle (peer access is enabled as
+ * needed); unmap with w8_peer_close. */
+int w8_peer_open(const void* handle, void** ptr);
+int w8_peer_close(void* ptr);
+int w8_peer_free(void* ptr);
+
+/* The LM head of a node's G ranks (one process per GPU), column-sharded, with its
+ * all-gather fused in: Int8Head.forward (gemma_npu.py:170-172) + the softcap
+ * (pipeline.py:335-338) + the greedy token (gemma_npu.py:291), replacing the GEMV
+ * followed by an NCCL all-gather.  Rank `rank` holds rows [row0, row0 + n) of the
+ * [vocab, k] int8 head weight (w [n, k], pitch k, bf16 scales s [n]); every rank passes
+ * the same G buffers of w8_lm_head_peer_bytes(vocab) bytes (bufs[r] = rank r's buffer:
+ * its own from w8_peer_alloc, the others mapped with w8_peer_open), in rank order.  Each
+ * logit (bit-identical to w8_lm_head_f32 of the whole head) is stored into every rank's
+ * buffer as it is computed; when the call completes on the stream, this rank's buffer
+ * holds all vocab logits (fp32, from its start) and *best (if not NULL) the greedy key
+ * over all ranks, in w8_lm_head_argmax_f32's format.  Every rank makes the same calls in
+ * the same order; a rank writes into a peer only after that peer has started the same
+ * call, so each rank must consume one call's logits before it makes the next call on the
+ * same stream.  Waits are bounded: a rank that never arrives makes the others return
+ * with W8_ERR_DEVICE_TIMEOUT in w8_device_status(), after which the buffers must be
+ * reallocated.  At most 8 ranks; k % 16 == 0, k <= 16384. */
+int w8_lm_head_peer_f32(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap, int64_t n, int64_t k,
+                        int64_t row0, int64_t vocab, int world, int rank, void* const* bufs, uint64_t* best,
+                        w8_stream_t stream);
 
 #ifdef __cplusplus
 }
