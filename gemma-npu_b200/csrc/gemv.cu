@@ -160,11 +160,11 @@ __global__ void __launch_bounds__(kGemvThreads)
 // ---------------------------------------------------------------- staged GEMV (one row, batch 1)
 // A decode step's layer GEMVs are short (3-10 MB) and each waits for the previous one, so
 // a GEMV that starts streaming its weights only when it starts is bound by that wait
-// plus a DRAM round trip.  Here each of G CTAs (one per SM) owns the contiguous weight
-// rows [n b / G, n (b + 1) / G) and copies them whole (at most kStagedMaxBytes) into
+// plus a DRAM round trip.  Here each of G CTAs (one or two per SM) owns the contiguous
+// weight rows [n b / G, n (b + 1) / G) and copies them whole (at most kStagedMaxBytes) into
 // shared memory with one bulk copy, issued before the wait on the previous kernel
 // (programmatic dependent launch): the weights depend on nothing, and a CTA of this
-// kernel fits on an SM beside one of the previous kernel, so the copy overlaps it.  After
+// kernel fits on an SM beside those of the previous kernel, so the copy overlaps it.  After
 // the wait, the activation row becomes fixed-point pieces in registers exactly as in
 // int8_gemv_kernel, and teams of S warps finish the rows from shared memory with the same
 // (J, S) arithmetic, so every output has the same bits as int8_gemv_kernel's.
@@ -313,7 +313,7 @@ static int launch_gemv(const __nv_bfloat16* x, int64_t ldx, const int8_t* w, int
 // The staged GEMV for one activation row when each CTA's rows fit its shared memory.
 template <int J, int S>
 static int launch_staged(const __nv_bfloat16* x, const int8_t* w, const __nv_bfloat16* s, __nv_bfloat16* y, int n,
-                         int k, int sms, cudaStream_t stream) {
+                         int k, int grid, cudaStream_t stream) {
   auto kern = w8::int8_gemv_staged_kernel<J, S>;
   int device = 0;
   W8_CUDA_TRY(cudaGetDevice(&device));
@@ -323,10 +323,10 @@ static int launch_staged(const __nv_bfloat16* x, const int8_t* w, const __nv_bfl
     W8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, w8::kStagedMaxBytes));
     done[device] = true;
   }
-  const int64_t rows = (static_cast<int64_t>(n) + sms - 1) / sms;
+  const int64_t rows = (static_cast<int64_t>(n) + grid - 1) / grid;
   const int smem = static_cast<int>(rows * k);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(sms, 1, 1);
+  cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(w8::kGemvThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -382,13 +382,18 @@ static int gemv_dispatch(const uint16_t* xh, int64_t ldx, const int8_t* w, int64
   // a matrix too short to give one CTA per SM at that R takes one row per team (measured
   // in a dependent chain: down 1536 x 6144 5.2 -> 4.2 us and 8960 x 1536 5.5 -> 4.4 us with
   // R = 4 at one or more CTAs per SM, against R = 1 at two).
-  // One bf16 row whose per-CTA weight rows fit shared memory (contiguous [N, K]): the
-  // staged kernel, which copies them before waiting on the previous kernel.
-  const bool staged = !LOGITS && ti == 1 && ldw == k && aligned(w, 16) &&
-                      (static_cast<int64_t>(n) + sms - 1) / sms * k <= w8::kStagedMaxBytes;
+  // One bf16 row whose weight rows fit shared memory at one or two CTAs per SM (at most
+  // 96 KB each, so a CTA of the next kernel still fits beside them and copies its own
+  // rows early; contiguous [N, K]): the staged kernel.
+  int staged_grid = 0;
+  if (!LOGITS && ti == 1 && ldw == k && aligned(w, 16))
+    for (int per_sm = 1; per_sm <= 2 && staged_grid == 0; ++per_sm)
+      if ((static_cast<int64_t>(n) + sms * per_sm - 1) / (sms * per_sm) * k <= w8::kStagedMaxBytes)
+        staged_grid = sms * per_sm;
+  const bool staged = staged_grid > 0;
 #define W8_STAGED(J, S)                                                                                \
   if (staged)                                                                                          \
-    return launch_staged<J, S>(x, w, s, reinterpret_cast<__nv_bfloat16*>(y), ni, ki, sms, stream)
+    return launch_staged<J, S>(x, w, s, reinterpret_cast<__nv_bfloat16*>(y), ni, ki, staged_grid, stream)
   if (k <= 512) { W8_STAGED(1, 1); } else if (k <= 1024) { W8_STAGED(2, 1); } else if (k <= 1536) { W8_STAGED(3, 1); }
   else if (k <= 2048) { W8_STAGED(4, 1); } else if (k <= 3072) { W8_STAGED(3, 2); } else if (k <= 4096) { W8_STAGED(4, 2); }
   else if (k <= 6144) { W8_STAGED(3, 4); } else if (k <= 8192) { W8_STAGED(4, 4); } else if (k <= 12288) { W8_STAGED(3, 8); }

@@ -109,7 +109,8 @@ def test_lm_head_argmax_equals_torch_argmax(cuda, cap):
 # kernel (weights copied before the wait on the previous kernel); two rows take the
 # register kernel.  Both must give every output the same bits.
 STAGED_SHAPES = [(2560, 1536), (1536, 2048), (1536, 6144), (2048, 1536), (1536, 4096), (5120, 1536),
-                 (256, 1536), (1536, 256), (100, 16), (44400, 16), (7, 4096), (1000, 48)]
+                 (256, 1536), (1536, 256), (100, 16), (44400, 16), (7, 4096), (1000, 48), (12288, 1536),
+                 (1536, 12288), (8960, 1536)]
 
 
 @pytest.mark.parametrize("n,k", STAGED_SHAPES)
