@@ -288,20 +288,28 @@ def e2e_prefill(w8, work, dev, steps, warmup, world, dequant=True):
 
 
 def build_decode(w8, work, dev):
-    """The decode GEMV chain over the prefill's resident weights + an int8 LM head."""
+    """The decode GEMV chain over the prefill's resident weights + an int8 LM head.
+
+    Each GEMV reads the previous one's output as its activation row (its first K values:
+    every config-2 output is at least as wide as the next input), and the head reads the
+    last one, so the chain is dependent through its data as a decode step is, and every
+    activation row is the freshly written output of the kernel before.  The independent
+    variant gives each GEMV a row of its own."""
     g = torch.Generator(device=dev).manual_seed(4242)
-    chain, nbytes = [], 0
+    chain, indep, nbytes = [], [], 0
+    prev = torch.randn((1, HIDDEN), device=dev, generator=g).to(torch.bfloat16)
     for per in work["weights"]:
         for name, n, k in LAYER_SHAPES:
             wq = per[name]
             s = (torch.rand((n,), device=dev, generator=g) * 1e-3 + 1e-4).to(torch.bfloat16)
-            x = torch.randn((1, k), device=dev, generator=g).to(torch.bfloat16)
             y = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
-            chain.append((x, wq, s, y))
+            chain.append((prev[:, :k], wq, s, y))
+            indep.append((torch.randn((1, k), device=dev, generator=g).to(torch.bfloat16), wq, s,
+                          torch.empty((1, n), dtype=torch.bfloat16, device=dev)))
+            prev = y
             nbytes += n * k + 2 * n + 2 * k + 2 * n
     hw, hs = w8.quant_rows(torch.randn((VOCAB, HIDDEN), device=dev, generator=g, dtype=torch.bfloat16) * 0.02)
-    head = (torch.randn((HIDDEN,), device=dev, generator=g).to(torch.bfloat16), hw, hs.to(torch.bfloat16),
-            torch.empty((VOCAB,), dtype=torch.float32, device=dev))
+    head = (prev[0, :HIDDEN], hw, hs.to(torch.bfloat16), torch.empty((VOCAB,), dtype=torch.float32, device=dev))
     nbytes += VOCAB * HIDDEN + 2 * VOCAB + 2 * HIDDEN + 4 * VOCAB
     torch.cuda.synchronize()
 
@@ -313,7 +321,7 @@ def build_decode(w8, work, dev):
 
 
     side = [torch.cuda.Stream(device=dev) for _ in range(4)]
-    layer_bytes = sum(wq.numel() + 2 * wq.shape[0] + 2 * x.numel() + 2 * y.numel() for x, wq, _, y in chain)
+    layer_bytes = sum(wq.numel() + 2 * wq.shape[0] + 2 * x.numel() + 2 * y.numel() for x, wq, _, y in indep)
 
     def step_independent():
         """The same layer GEMVs with no order between them: round-robin on 4 streams that
@@ -325,7 +333,7 @@ def build_decode(w8, work, dev):
         for j, sj in enumerate(side):
             sj.wait_event(fork)
             with torch.cuda.stream(sj):
-                for x, wq, sc, y in chain[j::len(side)]:
+                for x, wq, sc, y in indep[j::len(side)]:
                     w8.int8_linear(x, wq, sc, out=y)
             ev = torch.cuda.Event()
             ev.record(sj)

@@ -68,7 +68,6 @@ int num_sms(int* out) {
 int gemm_device_status(int clear, int* out);
 int attention_device_status(int clear, int* out);
 int peer_device_status(int clear, int* out);
-int gemv_device_status(int clear, int* out);
 
 }  // namespace w8host
 
@@ -101,10 +100,6 @@ extern "C" int w8_device_status(int clear) {
   int vp = W8_OK;
   st = w8host::peer_device_status(clear, &vp);
   if (st != W8_OK) return st;
-  int vg = W8_OK;
-  st = w8host::gemv_device_status(clear, &vg);
-  if (st != W8_OK) return st;
   if (v != W8_OK) return v;
-  if (va != W8_OK) return va;
-  return vp != W8_OK ? vp : vg;
+  return va != W8_OK ? va : vp;
 }

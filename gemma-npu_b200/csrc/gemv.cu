@@ -157,113 +157,6 @@ __global__ void __launch_bounds__(kGemvThreads)
   }
 }
 
-// ---------------------------------------------------------------- staged GEMV (one row, batch 1)
-// A decode step's layer GEMVs are short (3-10 MB) and each waits for the previous one, so
-// a GEMV that starts streaming its weights only when it starts is bound by that wait
-// plus a DRAM round trip.  Here each of G CTAs (one or two per SM) owns the contiguous
-// weight rows [n b / G, n (b + 1) / G) and copies them whole (at most kStagedMaxBytes) into
-// shared memory with one bulk copy, issued before the wait on the previous kernel
-// (programmatic dependent launch): the weights depend on nothing, and a CTA of this
-// kernel fits on an SM beside those of the previous kernel, so the copy overlaps it.  After
-// the wait, the activation row becomes fixed-point pieces in registers exactly as in
-// int8_gemv_kernel, and teams of S warps finish the rows from shared memory with the same
-// (J, S) arithmetic, so every output has the same bits as int8_gemv_kernel's.
-constexpr int kStagedMaxBytes = 96 * 1024;
-
-__device__ int g_gemv_status = 0;  // sticky device status of the staged GEMV's bounded wait
-
-__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
-               : "memory");
-}
-
-template <int J, int S>
-__global__ void __launch_bounds__(kGemvThreads)
-    int8_gemv_staged_kernel(const __nv_bfloat16* __restrict__ x, const int8_t* __restrict__ w,
-                            const __nv_bfloat16* __restrict__ s, __nv_bfloat16* __restrict__ y, int n, int k) {
-  static_assert(kGemvWarps % S == 0, "S must divide the CTA's warps");
-  constexpr int kTeams = kGemvWarps / S;
-  extern __shared__ __align__(128) uint8_t staged_smem[];
-  __shared__ __align__(8) uint64_t bar_storage;
-  __shared__ float red[kTeams][S];
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int team = warp / S;
-  const int sl = warp % S;
-  const int r0 = static_cast<int>(static_cast<int64_t>(n) * blockIdx.x / gridDim.x);
-  const int r1 = static_cast<int>(static_cast<int64_t>(n) * (blockIdx.x + 1) / gridDim.x);
-  const uint32_t bytes = static_cast<uint32_t>(r1 - r0) * static_cast<uint32_t>(k);
-  const uint32_t bar = smem_u32(&bar_storage);
-  pdl_launch_dependents();
-  if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
-    fence_mbar_init();
-    if (bytes > 0) {
-      mbar_arrive_expect_tx(bar, bytes);
-      bulk_copy_g2s(smem_u32(staged_smem), w + static_cast<int64_t>(r0) * k, bytes, bar);
-    } else {
-      mbar_arrive(bar);
-    }
-  }
-  __syncthreads();  // the barrier is initialised before anyone waits on it
-  pdl_wait();       // only the activation row depends on the previous kernel
-
-  uint32_t xh[J][4], xl[J][4];
-  float dq[J];
-#pragma unroll
-  for (int c = 0; c < J; ++c) {
-    const int k0 = ((sl * J + c) * 32 + lane) * 16;
-    uint32_t words[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-    if (k0 < k) {
-      const uint4* p = reinterpret_cast<const uint4*>(x + k0);
-      const uint4 u = __ldg(p), v = __ldg(p + 1);
-      words[0] = u.x, words[1] = u.y, words[2] = u.z, words[3] = u.w;
-      words[4] = v.x, words[5] = v.y, words[6] = v.z, words[7] = v.w;
-    }
-    dq[c] = piece_codes(words, xh[c], xl[c]);
-  }
-  // The channel scales of this team's first 32 rows, one per lane, fetched while the
-  // weights land: a load at each row's store would cost the warp a round trip per row.
-  uint32_t s_mine = 0u;
-  {
-    const int rr = team + lane * kTeams;
-    if (rr < r1 - r0) s_mine = __ldg(reinterpret_cast<const unsigned short*>(s) + r0 + rr);
-  }
-  // Every reader waits on the copy's barrier itself; a copy that never lands ends the
-  // kernel with a status instead of a hang (a CTA whose wait gave up skips its rows).
-  const bool landed = mbar_wait_bounded(bar, 0, nullptr, &g_gemv_status);
-  if (!__syncthreads_and(landed)) return;
-
-  for (int r = team, j = 0; r < r1 - r0; r += kTeams, ++j) {
-    const uint8_t* wrow = staged_smem + static_cast<int64_t>(r) * k;
-    float v = 0.f;
-#pragma unroll
-    for (int c = 0; c < J; ++c) {
-      const int k0 = ((sl * J + c) * 32 + lane) * 16;
-      int hi = 0, lo = 0;
-      if (k0 < k) dot16_q(*reinterpret_cast<const uint4*>(wrow + k0), xh[c], xl[c], hi, lo);
-      v = fmaf(static_cast<float>(256 * hi + lo), dq[c], v);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if constexpr (S > 1) {
-      if (lane == 0) red[team][sl] = v;
-      asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");
-      if (sl == 0) {
-        v = red[team][0];
-#pragma unroll
-        for (int q = 1; q < S; ++q) v += red[team][q];
-      }
-      asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(S * 32) : "memory");
-    }
-    const uint32_t sb = j < 32 ? __shfl_sync(0xffffffffu, s_mine, j)
-                               : __ldg(reinterpret_cast<const unsigned short*>(s) + r0 + r);
-    if (sl == 0 && lane == 0)
-      write_out<false>(y, r0 + r, v, __ushort_as_bfloat16(static_cast<unsigned short>(sb)), 0.f);
-  }
-}
-
 }  // namespace w8
 
 namespace w8host {
@@ -310,46 +203,6 @@ static int launch_gemv(const __nv_bfloat16* x, int64_t ldx, const int8_t* w, int
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, x, ldx, w, ldw, s, y, ldy, t, n, k, cap, best));
 }
 
-// The staged GEMV for one activation row when each CTA's rows fit its shared memory.
-template <int J, int S>
-static int launch_staged(const __nv_bfloat16* x, const int8_t* w, const __nv_bfloat16* s, __nv_bfloat16* y, int n,
-                         int k, int grid, cudaStream_t stream) {
-  auto kern = w8::int8_gemv_staged_kernel<J, S>;
-  int device = 0;
-  W8_CUDA_TRY(cudaGetDevice(&device));
-  static bool done[64] = {};
-  if (device < 0 || device >= 64) return W8_ERR_UNSUPPORTED;
-  if (!done[device]) {
-    W8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, w8::kStagedMaxBytes));
-    done[device] = true;
-  }
-  const int64_t rows = (static_cast<int64_t>(n) + grid - 1) / grid;
-  const int smem = static_cast<int>(rows * k);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(w8::kGemvThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr.val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, kern, x, w, s, y, n, k));
-}
-
-int gemv_device_status(int clear, int* out) {
-  int v = 0;
-  W8_CUDA_TRY(cudaDeviceSynchronize());
-  W8_CUDA_TRY(cudaMemcpyFromSymbol(&v, w8::g_gemv_status, sizeof(int)));
-  if (clear) {
-    const int zero = 0;
-    W8_CUDA_TRY(cudaMemcpyToSymbol(w8::g_gemv_status, &zero, sizeof(int)));
-  }
-  *out = v;
-  return W8_OK;
-}
-
 template <bool LOGITS>
 static int gemv_dispatch(const uint16_t* xh, int64_t ldx, const int8_t* w, int64_t ldw,
                          const uint16_t* sh, void* y, int64_t ldy, int64_t t, int64_t n, int64_t k,
@@ -382,23 +235,6 @@ static int gemv_dispatch(const uint16_t* xh, int64_t ldx, const int8_t* w, int64
   // a matrix too short to give one CTA per SM at that R takes one row per team (measured
   // in a dependent chain: down 1536 x 6144 5.2 -> 4.2 us and 8960 x 1536 5.5 -> 4.4 us with
   // R = 4 at one or more CTAs per SM, against R = 1 at two).
-  // One bf16 row whose weight rows fit shared memory at one or two CTAs per SM (at most
-  // 96 KB each, so a CTA of the next kernel still fits beside them and copies its own
-  // rows early; contiguous [N, K]): the staged kernel.
-  int staged_grid = 0;
-  if (!LOGITS && ti == 1 && ldw == k && aligned(w, 16))
-    for (int per_sm = 1; per_sm <= 2 && staged_grid == 0; ++per_sm)
-      if ((static_cast<int64_t>(n) + sms * per_sm - 1) / (sms * per_sm) * k <= w8::kStagedMaxBytes)
-        staged_grid = sms * per_sm;
-  const bool staged = staged_grid > 0;
-#define W8_STAGED(J, S)                                                                                \
-  if (staged)                                                                                          \
-    return launch_staged<J, S>(x, w, s, reinterpret_cast<__nv_bfloat16*>(y), ni, ki, staged_grid, stream)
-  if (k <= 512) { W8_STAGED(1, 1); } else if (k <= 1024) { W8_STAGED(2, 1); } else if (k <= 1536) { W8_STAGED(3, 1); }
-  else if (k <= 2048) { W8_STAGED(4, 1); } else if (k <= 3072) { W8_STAGED(3, 2); } else if (k <= 4096) { W8_STAGED(4, 2); }
-  else if (k <= 6144) { W8_STAGED(3, 4); } else if (k <= 8192) { W8_STAGED(4, 4); } else if (k <= 12288) { W8_STAGED(3, 8); }
-  else { W8_STAGED(4, 8); }
-#undef W8_STAGED
 #define W8_GEMV(J, S, R)                                                                      \
   return n < sms * (w8::kGemvWarps / (S)) * (R)                                                \
              ? launch_gemv<J, S, 1, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream, best) \

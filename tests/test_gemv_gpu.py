@@ -104,25 +104,3 @@ def test_lm_head_argmax_equals_torch_argmax(cuda, cap):
     logits, tok = w8.lm_head_logits(h, wq[:5000], s[:5000] * -1, cap, argmax=True)
     assert int(tok) == int(logits.argmax())
 
-
-# One activation row whose per-SM share of the weight fits shared memory takes the staged
-# kernel (weights copied before the wait on the previous kernel); two rows take the
-# register kernel.  Both must give every output the same bits.
-STAGED_SHAPES = [(2560, 1536), (1536, 2048), (1536, 6144), (2048, 1536), (1536, 4096), (5120, 1536),
-                 (256, 1536), (1536, 256), (100, 16), (44400, 16), (7, 4096), (1000, 48), (12288, 1536),
-                 (1536, 12288), (8960, 1536)]
-
-
-@pytest.mark.parametrize("n,k", STAGED_SHAPES)
-def test_staged_gemv_equals_register_gemv(cuda, n, k):
-    gen = torch.Generator(device=cuda).manual_seed(n + 7 * k)
-    wq, sw = w8.quant_rows((torch.randn(n, k, device=cuda, generator=gen) * 0.02).to(torch.bfloat16))
-    s = sw.to(torch.bfloat16)
-    x = torch.randn(2, k, device=cuda, generator=gen).to(torch.bfloat16)
-    both = w8.int8_linear(x, wq, s)           # two rows: the register kernel
-    one0 = w8.int8_linear(x[:1], wq, s)       # one row: the staged kernel
-    one1 = w8.int8_linear(x[1:2].clone(), wq, s)
-    torch.cuda.synchronize()
-    assert torch.equal(one0[0].view(torch.int16), both[0].view(torch.int16))
-    assert torch.equal(one1[0].view(torch.int16), both[1].view(torch.int16))
-    assert w8.device_status() == 0
