@@ -96,6 +96,12 @@ __global__ void __launch_bounds__(kGemvThreads)
   static_assert(kGemvWarps % S == 0, "S must divide the CTA's warps");
   constexpr int kTeams = kGemvWarps / S;
   __shared__ float red[kTeams][S][R];
+  // A CTA finishes kChunk contiguous rows per step; they are sent to the other ranks as
+  // 16-byte stores of whole chunks (a 4-byte remote store per logit made the transfer,
+  // not the GEMV, the cost).  Two buffers, so a step's stores need one barrier.
+  constexpr int kChunk = kTeams * R;
+  constexpr bool kVec = kChunk % 4 == 0;
+  __shared__ __align__(16) float tile[2][kChunk];
   __shared__ uint32_t s_epoch;
   __shared__ int s_ok;
   const int warp = threadIdx.x >> 5;
@@ -106,8 +112,9 @@ __global__ void __launch_bounds__(kGemvThreads)
   unsigned long long mine = 0ull;
   pdl_launch_dependents();
 
-  const int stride = gridDim.x * kTeams * R;
-  const int first = (blockIdx.x * kTeams + team) * R;
+  const int stride = gridDim.x * kChunk;
+  const int cta_first = blockIdx.x * kChunk;
+  const int first = cta_first + team * R;
   uint4 wv[R][J];
   auto load_w = [&](int n0) {
 #pragma unroll
@@ -151,8 +158,13 @@ __global__ void __launch_bounds__(kGemvThreads)
     dq[c] = piece_codes(words, xh[c], xl[c]);
   }
 
-  for (int n0 = first; ok && n0 < n; n0 += stride) {
-    if (n0 != first) load_w(n0);
+  const bool vec = kVec && a.row0 % 4 == 0;
+  int buf = 0;
+  // Every thread of the CTA walks the same steps (the barriers below need it); a team
+  // whose rows lie past n computes zeros and writes nothing.
+  for (int base = cta_first; ok && base < n; base += stride, buf ^= 1) {
+    const int n0 = base + team * R;
+    if (base != cta_first) load_w(n0);
     float acc[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -190,11 +202,32 @@ __global__ void __launch_bounds__(kGemvThreads)
     }
     if (writer) {
       const int row = n0 + lane;
-      // write_out's rounding and softcap, then the logit into every rank's buffer
+      // write_out's rounding and softcap into this rank's buffer, then to the others
       const float f = write_out<true>(a.logits[a.me], a.row0 + row, v, s[row], a.cap);
-      for (int r = 0; r < a.world; ++r)
-        if (r != a.me) a.logits[r][a.row0 + row] = f;
       mine = max(mine, argmax_key(f, a.row0 + row));
+      if (vec) {
+        tile[buf][n0 - base + lane] = f;
+      } else {
+        for (int r = 0; r < a.world; ++r)
+          if (r != a.me) a.logits[r][a.row0 + row] = f;
+      }
+    }
+    if (vec) {
+      __syncthreads();
+      if (warp == 0) {
+        const int valid = min(kChunk, n - base);
+        for (int e = 4 * lane; e < kChunk; e += 128) {
+          if (e + 4 <= valid) {
+            const float4 v4 = *reinterpret_cast<const float4*>(&tile[buf][e]);
+            for (int r = 0; r < a.world; ++r)
+              if (r != a.me) *reinterpret_cast<float4*>(a.logits[r] + a.row0 + base + e) = v4;
+          } else {
+            for (int j = e; j < valid; ++j)
+              for (int r = 0; r < a.world; ++r)
+                if (r != a.me) a.logits[r][a.row0 + base + j] = tile[buf][j];
+          }
+        }
+      }
     }
   }
 #pragma unroll

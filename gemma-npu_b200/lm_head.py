@@ -28,8 +28,11 @@ TRANSPORTS = ("nccl", "peer")
 
 
 def shard_rows(vocab, world, rank):
-    """Row range [r0, r1) of the head weight owned by `rank`; shards are ceil(V/G) rows."""
+    """Row range [r0, r1) of the head weight owned by `rank`; shards are ceil(V/G) rows
+    rounded up to a multiple of 4 (so every shard starts on a 16-byte boundary of the
+    gathered fp32 logits), the last one shorter."""
     per = -(-vocab // world)
+    per = -(-per // 4) * 4
     r0 = min(rank * per, vocab)
     return r0, min(r0 + per, vocab), per
 
