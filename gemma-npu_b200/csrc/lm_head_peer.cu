@@ -131,16 +131,22 @@ __global__ void __launch_bounds__(kGemvThreads)
   pdl_wait();
 
   uint32_t* const abort_word = a.state + 2;
+  const bool vec = kVec && a.row0 % 4 == 0;
   if (threadIdx.x == 0) {
     const uint32_t t = ld_relaxed_gpu(a.state + 1) + 1u;
     // "This rank has started call t": written by every CTA (the same value), so the
     // signal does not depend on which of this rank's CTAs runs first.
     for (int r = 0; r < a.world; ++r) st_relaxed_sys(a.ready[r] + a.me, t);
     s_epoch = t;
-    s_ok = wait_all_sys(a.ready[a.me], a.world, a.me, t, abort_word) ? 1 : 0;
+    // Rows whose logits go out one by one (no 16-byte chunks) wait for every peer here;
+    // chunked rows are computed first and only the sending warp waits, before its first
+    // send (by then the peers have started as well).
+    s_ok = vec ? 1 : (wait_all_sys(a.ready[a.me], a.world, a.me, t, abort_word) ? 1 : 0);
   }
   __syncthreads();
   const bool ok = s_ok != 0;
+  const uint32_t epoch = s_epoch;
+  bool peers_ready = !vec;  // warp 0's knowledge that every peer has started this call
 
   // This lane's 16-element pieces of the activation row as 16-bit fixed point.
   uint32_t xh[J][4], xl[J][4];
@@ -158,8 +164,8 @@ __global__ void __launch_bounds__(kGemvThreads)
     dq[c] = piece_codes(words, xh[c], xl[c]);
   }
 
-  const bool vec = kVec && a.row0 % 4 == 0;
   int buf = 0;
+  bool vec_failed = false;
   // Every thread of the CTA walks the same steps (the barriers below need it); a team
   // whose rows lie past n computes zeros and writes nothing.
   for (int base = cta_first; ok && base < n; base += stride, buf ^= 1) {
@@ -214,7 +220,13 @@ __global__ void __launch_bounds__(kGemvThreads)
     }
     if (vec) {
       __syncthreads();
-      if (warp == 0) {
+      if (warp == 0 && !peers_ready) {
+        bool seen = false;
+        if (lane == 0) seen = wait_all_sys(a.ready[a.me], a.world, a.me, epoch, abort_word);
+        peers_ready = __shfl_sync(0xffffffffu, seen, 0);
+        if (!peers_ready) vec_failed = true;  // the abort word is set: nothing is sent
+      }
+      if (warp == 0 && !vec_failed) {
         const int valid = min(kChunk, n - base);
         for (int e = 4 * lane; e < kChunk; e += 128) {
           if (e + 4 <= valid) {
@@ -236,16 +248,21 @@ __global__ void __launch_bounds__(kGemvThreads)
 
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();  // this CTA's stores into every rank's buffer come first
+    // This CTA's stores into every rank's buffer are ordered before its count (an
+    // acquire-release fence at system scope: the CTA barrier above makes them this
+    // thread's to order).
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
     if (atomicAdd(a.state + 0, 1u) == gridDim.x - 1u) {
       // The last CTA of this rank: publish the rank's key and flag, then wait for all.
-      __threadfence_system();
-      const uint32_t t = s_epoch;
-      const bool healthy = ld_relaxed_gpu(abort_word) == 0u;
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      const uint32_t t = epoch;
+      // A peer's key slot may be written only once it has started this call.
+      const bool healthy = ld_relaxed_gpu(abort_word) == 0u &&
+                           wait_all_sys(a.ready[a.me], a.world, a.me, t, abort_word);
       if (healthy) {
         const unsigned long long key = *reinterpret_cast<volatile unsigned long long*>(a.best_local);
         for (int r = 0; r < a.world; ++r) a.keys[r][a.me] = key;
-        __threadfence_system();
+        // each release orders the key stores (and the counted CTAs' logits) before the flag
         for (int r = 0; r < a.world; ++r) st_release_sys(a.flags[r] + a.me, t);
         if (wait_all_sys(a.flags[a.me], a.world, -1, t, abort_word) && a.best != nullptr) {
           unsigned long long m = 0ull;
