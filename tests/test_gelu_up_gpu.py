@@ -92,11 +92,12 @@ def test_repeat_calls_are_identical(cuda):
     assert torch.equal(q1, q2) and torch.equal(s1, s2)
 
 
-def test_equals_unfused_gpu_chain(cuda):
+@pytest.mark.parametrize("m,inter,k", [(512, 1024, 1536), (3658, 6144, 1536)])
+def test_equals_unfused_gpu_chain(cuda, m, inter, k):
     """Fused result == the unfused GPU chain: int32 GEMM, then the glue on the int32
-    output (torch ops with the reference's expression), on all rows."""
-    m, inter, k = 512, 1024, 1536
-    gen = torch.Generator(device=cuda).manual_seed(9)
+    output (torch ops with the reference's expression), on all rows -- at config 1's full
+    gate/up size too."""
+    gen = torch.Generator(device=cuda).manual_seed(9 + m)
     x, sx = w8.quant_rows(torch.randn((m, k), device=cuda, generator=gen, dtype=torch.bfloat16))
     w, sw = w8.quant_rows(torch.randn((2 * inter, k), device=cuda, generator=gen, dtype=torch.bfloat16) * 0.02)
     wp, swp = w8.pack_gelu_up(w, sw)

@@ -239,3 +239,54 @@ def test_ple_branch_matches_oracle(cuda, t):
     # Without the next layer's weight: h only, the same values.
     h2 = w8.ple_out(yp, res0, w_post, scalar, 1e-6)
     assert torch.equal(h2, h)
+
+
+# ---- every row at config 1's size: the int32 product from torch._int_mm (cuBLASLt,
+# bit-exact to the oracle's int_mm), the glue of all 3658 rows from the oracle.
+
+def test_k_in_all_rows(cuda):
+    t, n = 3658, 1536
+    gen = torch.Generator(device=cuda).manual_seed(101)
+    h = (torch.randn((t, n), device=cuda, generator=gen) * 3).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn((n,), device=cuda, generator=gen)).to(torch.bfloat16)
+    q, s = w8.rms_quant(h, w, 1e-6)
+    qr, sr = ref.k_in(h.float().cpu().numpy(), w.float().cpu().numpy(), 1e-6)
+    close_q(q.cpu().numpy(), qr)
+    np.testing.assert_allclose(s.cpu().numpy(), sr, rtol=2.0 ** -7)
+
+
+@pytest.mark.parametrize("two", [True, False])
+def test_post_norm_all_rows(cuda, two):
+    t, n, k = 3658, 1536, 2048 if two else 6144
+    gen = torch.Generator(device=cuda).manual_seed(102 + two)
+    x, sx = w8.quant_rows(torch.randn((t, k), device=cuda, generator=gen, dtype=torch.bfloat16))
+    wq, sw = w8.quant_rows(torch.randn((n, k), device=cuda, generator=gen, dtype=torch.bfloat16) * 0.02)
+    res = torch.randn((t, n), device=cuda, generator=gen).to(torch.bfloat16)
+    w1 = (1 + 0.1 * torch.randn((n,), device=cuda, generator=gen)).to(torch.bfloat16)
+    w2 = (1 + 0.1 * torch.randn((n,), device=cuda, generator=gen)).to(torch.bfloat16) if two else None
+    res0 = res.clone()
+    h, q, s = w8.post_norm_quant(w8.gemm_dequant(x, wq, sx, sw), res, w1, w2, 1e-6, h=res)
+    acc = torch._int_mm(x, wq.t()).cpu().numpy()
+    yr = ref.bf16_bits_to_f32(ref.dequant(acc, sx.cpu().numpy(), sw.cpu().numpy()))
+    hr, qr, sr = ref.k_post(yr, res0.float().cpu().numpy(), w1.float().cpu().numpy(),
+                            None if w2 is None else w2.float().cpu().numpy(), 1e-6)
+    close_bf16(bits(h), ref.f32_to_bf16_bits(hr), res=res0.float().cpu().numpy())
+    close_q(q.cpu().numpy(), qr)
+    np.testing.assert_allclose(s.cpu().numpy(), sr, rtol=2.0 ** -7)
+
+
+def test_qkv_norm_rope_all_rows(cuda):
+    t, nh, kv, d, k = 3658, 8, 1, 256, 1536
+    n = (nh + 2 * kv) * d
+    gen = torch.Generator(device=cuda).manual_seed(103)
+    x, sx = w8.quant_rows(torch.randn((t, k), device=cuda, generator=gen, dtype=torch.bfloat16))
+    wq, sw = w8.quant_rows(torch.randn((n, k), device=cuda, generator=gen, dtype=torch.bfloat16) * 0.02)
+    cos, sin = _rope_tables(t, d, cuda)
+    qw = (1 + 0.1 * torch.randn((d,), device=cuda, generator=gen)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn((d,), device=cuda, generator=gen)).to(torch.bfloat16)
+    q, kk, v = w8.qkv_norm_rope(w8.gemm_dequant(x, wq, sx, sw), cos, sin, qw, kw, 1e-6, nh, kv, d)
+    acc = torch._int_mm(x, wq.t()).cpu().numpy()
+    f = lambda z: z.float().cpu().numpy()
+    qr, kr, vr = ref.k_qkv(acc, f(sx), f(sw), f(cos), f(sin), f(qw), f(kw), 1e-6, nh, kv, d, False)
+    for mine, theirs in ((q, qr), (kk, kr), (v, vr)):
+        close_bf16(bits(mine), ref.f32_to_bf16_bits(theirs), per_vector=True)
