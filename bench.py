@@ -320,6 +320,17 @@ def build_decode(w8, work, dev):
         w8.lm_head_logits(h, hq, hsc, SOFTCAP, out=logits, argmax=True)  # + the greedy token
 
 
+    hq16 = head[1][:, :16].contiguous()
+
+    def step_floor():
+        """The same dependent chain (same launches, grids, activation hand-offs and output
+        rows) with every GEMV cut to its first 16 columns of K: what a dependent step costs
+        without its weight stream."""
+        for x, wq, s, y in chain:
+            w8.int8_linear(x[:, :16], wq[:, :16], s, out=y)
+        h, hq, hsc, logits = head
+        w8.lm_head_logits(h[:16], hq16, hsc, SOFTCAP, out=logits, argmax=True)
+
     side = [torch.cuda.Stream(device=dev) for _ in range(4)]
     layer_bytes = sum(wq.numel() + 2 * wq.shape[0] + 2 * x.numel() + 2 * y.numel() for x, wq, _, y in indep)
 
@@ -341,7 +352,7 @@ def build_decode(w8, work, dev):
         for ev in joins:
             cur.wait_event(ev)
 
-    return step, nbytes, len(chain) + 1, head, (step_independent, layer_bytes, len(chain))
+    return step, nbytes, len(chain) + 1, head, (step_independent, layer_bytes, len(chain)), step_floor
 
 
 def prompt_lengths(count=8, seed=0, lo=200, hi=3700):
@@ -1072,7 +1083,7 @@ def main():
                                  "path": "gemma_npu_b200.mm_i8_nk per GEMM: pinned int8 activations H2D, int32 results "
                                          "D2H (pipeline.py's Prefill.gemm data flow); same three-stream pipeline"}
         if not args.no_decode and args.only is None:
-            step, nbytes, launches, head, (istep, ibytes, ilaunches) = build_decode(w8, work, dev)
+            step, nbytes, launches, head, (istep, ibytes, ilaunches), fstep = build_decode(w8, work, dev)
             dgraph = capture(step, stream)
             dms = timed(lambda: dgraph.replay(), args.decode_steps, args.warmup, stream, world)
             per = dms / args.decode_steps
@@ -1088,6 +1099,10 @@ def main():
             ims = timed(lambda: igraph.replay(), args.decode_steps, args.warmup, stream, world) / args.decode_steps
             del igraph
             igbs = ibytes / (ims * 1e-3) / 1e9
+            fgraph = capture(fstep, stream)
+            fms = timed(lambda: fgraph.replay(), args.decode_steps, args.warmup, stream, world) / args.decode_steps
+            del fgraph
+            rest_gbs = nbytes / ((per - fms) * 1e-3) / 1e9 if per > fms else None
             line["decode_gemv"] = {
                 "metric": "int8 GEMV GB/s, decode chain (config 2: 140 layer GEMVs + LM head 262144x1536, "
                           "softcap and greedy argmax fused, one CUDA graph, each GEMV ordered after the previous one)",
@@ -1100,6 +1115,13 @@ def main():
                             "frac": head_gbs / pk["hbm_gbs"],
                             "note": "the 262144x1536 head GEMV alone (402.7 MB int8): the chain's per-layer "
                                     "GEMVs (3.1-18.9 MB) are bound by the dependent step's latency, not bandwidth"},
+                "dependent_step_floor": {
+                    "us": fms * 1e3, "us_per_launch": fms * 1e3 / launches,
+                    "remainder_us": (per - fms) * 1e3, "remainder_gbs": rest_gbs,
+                    "remainder_frac": None if rest_gbs is None else rest_gbs / pk["hbm_gbs"],
+                    "note": "the same 141-launch dependent chain with every GEMV cut to K = 16 (same grids, "
+                            "activation hand-offs and outputs, no weight stream): the latency floor of a "
+                            "dependent batch-1 step; remainder = chain - floor, the time the weight bytes add"},
                 "layer_gemvs_independent": {"us": ims * 1e3, "bytes": ibytes, "gbs": igbs,
                                             "frac": igbs / pk["hbm_gbs"], "launches": ilaunches,
                                             "note": "the chain's 140 layer GEMVs with no dependence between them, "
