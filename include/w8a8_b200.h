@@ -278,6 +278,12 @@ int w8_dequant_bf16(const int32_t* acc, int64_t ldacc, const float* sx, const fl
 
 /* ---- decode: weight-only int8 GEMV / LM head -------------------------- */
 
+/* These kernels start loading w before they wait for the previous kernel on the stream
+ * (only x is taken to depend on it).  w must therefore not be written by the kernel
+ * just before them on the stream when that kernel is one of this library's GEMM, GEMV,
+ * glue or attention kernels, which let their successor start early; w8_quant_rows_*
+ * and kernels from outside the library do not. */
+
 /* y[t,n] (bf16) = bf16(float(s[n]) * sum_k float(x[t,k]) * w[n,k]) within max-rel 1e-2:
  * x as 16-bit fixed point over each 16-element piece's range, exact int32 dot products.
  * x bf16 [T,K], w int8 [N,K] row-major, s bf16 [N].  K % 16 == 0, ldw % 16 == 0,
