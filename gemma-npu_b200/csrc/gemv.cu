@@ -60,9 +60,12 @@ __global__ void __launch_bounds__(kGemvThreads)
       }
   };
   // The weights do not depend on the previous kernel: start streaming them before
-  // waiting for it (only the activation row does).
+  // waiting for it (only the activation row does).  The wait sits in its own basic block
+  // (t_count >= 1 on every launch): with the loads and the wait in one block the code
+  // generator was free to issue the loads after the wait, and a dependent decode chain
+  // of 140 layer GEMVs ran 550 us per token instead of 451 us.
   load_w(wv, first);
-  pdl_wait();
+  if (t_count > 0) pdl_wait();
 
   for (int t = 0; t < t_count; ++t) {
     const __nv_bfloat16* xt = x + static_cast<int64_t>(t) * ldx;

@@ -128,7 +128,9 @@ __global__ void __launch_bounds__(kGemvThreads)
       }
   };
   load_w(first);  // the weights do not depend on the previous kernel
-  pdl_wait();
+  // The wait in its own basic block (k >= 16 on every launch), so that the weight loads
+  // above stay ahead of it (as in int8_gemv_kernel).
+  if (k > 0) pdl_wait();
 
   uint32_t* const abort_word = a.state + 2;
   const bool vec = kVec && a.row0 % 4 == 0;
