@@ -1121,7 +1121,10 @@ def main():
                     "remainder_frac": None if rest_gbs is None else rest_gbs / pk["hbm_gbs"],
                     "note": "the same 141-launch dependent chain with every GEMV cut to K = 16 (same grids, "
                             "activation hand-offs and outputs, no weight stream): the latency floor of a "
-                            "dependent batch-1 step; remainder = chain - floor, the time the weight bytes add"},
+                            "dependent batch-1 step; remainder = chain - floor, the time the weight bytes add "
+                            "(a remainder_frac above 1 means part of the weight stream is hidden under the "
+                            "steps' latency: each GEMV issues its first weight loads before waiting for the "
+                            "previous one)"},
                 "layer_gemvs_independent": {"us": ims * 1e3, "bytes": ibytes, "gbs": igbs,
                                             "frac": igbs / pk["hbm_gbs"], "launches": ilaunches,
                                             "note": "the chain's 140 layer GEMVs with no dependence between them, "
