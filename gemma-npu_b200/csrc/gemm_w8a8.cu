@@ -1175,9 +1175,14 @@ static thread_local LastSchedule g_last_schedule = {0, 0, 0, 0};
 
 // Stream-K pays off when whole tiles would leave the last wave of workers mostly idle
 // and each tile is long enough (K) that splitting it costs little next to its MMAs.
+// One wave of whole tiles that keeps at least half the workers busy stays whole: there the
+// split tiles' waits and reduce-adds cost more than the idle workers give back (down
+// 1536 x 6144 at M = 1607, 42 tiles on 74 pairs: 22.5 us whole, 23.7 us stream-K; at
+// M = 858, 24 tiles: 21.5 us whole, 19.5 us stream-K).
 static bool want_stream_k(int64_t tiles, int workers, int k) {
   if (k < 24 * w8::kBK) return false;
   const int64_t waves = (tiles + workers - 1) / workers;
+  if (waves == 1 && 2 * tiles >= workers) return false;
   return tiles * 100 < waves * workers * 90;  // whole-tile efficiency below 90 %
 }
 
