@@ -25,7 +25,7 @@ for _m in (_lib, build, kernels, gemm, lm_head, npu_kernels):
     _sys.modules.setdefault("gemma_npu_b200." + _m.__name__.rsplit(".", 1)[-1], _m)
 
 from .kernels import (  # noqa: E402,F401
-    BLOCK_K, BLOCK_M, BLOCK_N, attention_prefill, attention_quant, attn_out_quant, dequant, gelu_up_quant, gemm_dequant, gemm_qkv_norm_rope, int8_linear,
+    BLOCK_K, BLOCK_M, BLOCK_N, attention_prefill, attention_quant, attn_out_quant, dequant, gelu_up_quant, gemm_dequant, gemm_qkv_norm_rope, rope_tiles, int8_linear,
     lm_head_logits, mm_i8, mm_i8_nk, pack_gelu_up, ple_gate_quant, ple_out, post_norm_quant, qkv_norm_rope,
     quant_rows, rms_quant, use_device, use_npu)
 from .gemm import (  # noqa: E402,F401
@@ -33,7 +33,7 @@ from .gemm import (  # noqa: E402,F401
 from .lm_head import ShardedInt8Head  # noqa: E402,F401
 from ._lib import W8Error, device_status  # noqa: E402,F401
 
-__all__ = ["mm_i8", "mm_i8_nk", "gemm_qkv_norm_rope", "gemm_dequant", "gelu_up_quant", "pack_gelu_up", "rms_quant", "post_norm_quant",
+__all__ = ["mm_i8", "mm_i8_nk", "gemm_qkv_norm_rope", "rope_tiles", "gemm_dequant", "gelu_up_quant", "pack_gelu_up", "rms_quant", "post_norm_quant",
            "ple_gate_quant", "ple_out",
            "attn_out_quant", "attention_prefill", "attention_quant", "qkv_norm_rope", "quant_rows", "dequant",
            "int8_linear",

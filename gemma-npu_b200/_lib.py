@@ -96,6 +96,8 @@ SIGNATURES = {
                                         _i64, _p, _i64, _p, _p]),
     "w8_gemm_qkv_norm_rope": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _i, _p, _p, _i64, _p, _p, _f, _p,
                                    _i64, _i64, _i64, _p]),
+    "w8_gemm_qkv_norm_rope_tiled": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _i, _p, _p, _i64, _p, _p, _f, _p,
+                                   _i64, _i64, _i64, _p]),
     "w8_gemm_gelu_up_quant": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _p, _p]),
     "w8_quant_rows_bf16": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _p]),
     "w8_quant_rows_f32": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _p]),

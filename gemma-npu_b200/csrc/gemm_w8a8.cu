@@ -96,7 +96,8 @@ struct GemmArgs {
   // kEpiQkv: heads [0, q_heads) are q, [q_heads, q_heads + k_heads) k, the rest v.
   const __nv_bfloat16* cos;  // [T, >= 256] row pitch ldcs
   const __nv_bfloat16* sin;
-  int64_t ldcs;
+  int64_t ldcs;   // [T, D] tables: the row pitch; 8-column tiled tables: the pitch of a tile
+  int cs_tiled;   // cos / sin as [D / 8][T][8] (each token's 8 columns of a tile contiguous)
   const __nv_bfloat16* qw;   // q_norm weight [256]
   const __nv_bfloat16* kw;   // k_norm weight [256]
   float eps;
@@ -384,6 +385,20 @@ __device__ __forceinline__ void put_box64_3d(const CUtensorMap* tm_c, const uint
   }
 }
 
+// 16 words of bf16 pairs: columns c0 .. c0 + 31 (c0 % 8 == 0) of token `row` of an
+// 8-column tiled table [D / 8][T][8] whose tiles lie `pitch` elements apart, or zeros for a
+// row past M.  The 32 lanes (32 consecutive tokens) of a warp read 512 contiguous bytes
+// per load.
+__device__ __forceinline__ void load_row32_tiled(const __nv_bfloat16* base, int64_t pitch, int row, int c0, bool valid,
+                                                 uint32_t (&out)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 v = valid ? __ldg(reinterpret_cast<const uint4*>(base + ((c0 >> 3) + j) * pitch + static_cast<int64_t>(row) * 8))
+                          : make_uint4(0u, 0u, 0u, 0u);
+    out[4 * j] = v.x, out[4 * j + 1] = v.y, out[4 * j + 2] = v.z, out[4 * j + 3] = v.w;
+  }
+}
+
 // 16 words of bf16 pairs (32 consecutive columns of one row) from global memory, or zeros
 // for a row past M.
 __device__ __forceinline__ void load_row32_bf16(const __nv_bfloat16* p, bool valid, uint32_t (&out)[16]) {
@@ -440,8 +455,8 @@ __device__ __forceinline__ void qkv_epilogue_rows(const GemmArgs& args, const CU
   const bool is_q = head < args.q_heads;
   const bool is_k = !is_q && head < args.q_heads + args.k_heads;
   const __nv_bfloat16* wnorm = is_q ? args.qw : (is_k ? args.kw : nullptr);
-  const __nv_bfloat16* crow = args.cos + static_cast<int64_t>(row) * args.ldcs;
-  const __nv_bfloat16* srow = args.sin + static_cast<int64_t>(row) * args.ldcs;
+  const __nv_bfloat16* crow = args.cos + (args.cs_tiled ? 0 : static_cast<int64_t>(row) * args.ldcs);
+  const __nv_bfloat16* srow = args.sin + (args.cs_tiled ? 0 : static_cast<int64_t>(row) * args.ldcs);
   // ---- pass 2: this warp's column pairs (c, c + 128), 32 columns at a time
 #pragma unroll 1
   for (int cc = 0; cc < 2; ++cc) {
@@ -475,10 +490,17 @@ __device__ __forceinline__ void qkv_epilogue_rows(const GemmArgs& args, const CU
     }
     if (wnorm != nullptr) {  // q and k heads: RoPE with rotate_half's partner c <-> c + 128
       uint32_t ca[16], cb[16], sa[16], sb[16];
-      load_row32_bf16(crow + c0, valid, ca);
-      load_row32_bf16(crow + 128 + c0, valid, cb);
-      load_row32_bf16(srow + c0, valid, sa);
-      load_row32_bf16(srow + 128 + c0, valid, sb);
+      if (args.cs_tiled) {
+        load_row32_tiled(args.cos, args.ldcs, row, c0, valid, ca);
+        load_row32_tiled(args.cos, args.ldcs, row, 128 + c0, valid, cb);
+        load_row32_tiled(args.sin, args.ldcs, row, c0, valid, sa);
+        load_row32_tiled(args.sin, args.ldcs, row, 128 + c0, valid, sb);
+      } else {
+        load_row32_bf16(crow + c0, valid, ca);
+        load_row32_bf16(crow + 128 + c0, valid, cb);
+        load_row32_bf16(srow + c0, valid, sa);
+        load_row32_bf16(srow + 128 + c0, valid, sb);
+      }
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
         const uint32_t oa = bf16x2_add(bf16x2_mul(xa[q], ca[q]), bf16x2_mul(xb[q] ^ 0x80008000u, sa[q]));
@@ -1097,6 +1119,7 @@ struct QkvEpiParams {
   const uint16_t* cos;
   const uint16_t* sin;
   int64_t ldcs;
+  int cs_tiled;
   const uint16_t* qw;
   const uint16_t* kw;
   float eps;
@@ -1275,7 +1298,22 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
 
   // 256-row tiles on CTA pairs; their operand copies cover two 128-byte K chunks, which
   // needs K to be a multiple of 128.  Otherwise one CTA per 128 x 256 tile.
-  const bool pair = m > w8::kBM && k % w8::kBK == 0;
+  bool pair = m > w8::kBM && k % w8::kBK == 0;
+  if (pair && epi == w8::kEpiQkv) {
+    // The qkv glue needs whole 256-column tiles (one head each), so its wave count cannot
+    // be evened out by a narrower tile: take 128-row tiles on single CTAs when they need
+    // fewer waves than 256-row tiles on CTA pairs (M = 3658, 10 heads: 290 tiles on 148
+    // SMs in 2 waves, against 150 on 74 pairs in 3, the last with 2 tiles).
+    int cap = 0, sms = 0;
+    st = pair_capacity<false, w8::kEpiQkv, w8::kBN>(device, &cap);
+    if (st != W8_OK) return st;
+    st = num_sms(&sms);
+    if (st != W8_OK) return st;
+    const int64_t heads_n = n / 256;
+    const int64_t pair_waves = ((m + 255) / 256 * heads_n + cap - 1) / cap;
+    const int64_t single_waves = ((m + 127) / 128 * heads_n + sms - 1) / sms;
+    if (single_waves < pair_waves) pair = false;
+  }
   const int rows_per_tile = pair ? 2 * w8::kBM : w8::kBM;
   // Tile width on CTA pairs over a K-major B: the narrowest of 64, 128, 192 and 256
   // columns that needs no more waves of workers than any other.  A narrower tile costs
@@ -1342,12 +1380,14 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
   args.row_absmax = row_absmax;
   args.cos = args.sin = args.qw = args.kw = nullptr;
   args.ldcs = 0;
+  args.cs_tiled = 0;
   args.eps = 0.f;
   args.q_heads = args.k_heads = 0;
   if (qkv != nullptr) {
     args.cos = reinterpret_cast<const __nv_bfloat16*>(qkv->cos);
     args.sin = reinterpret_cast<const __nv_bfloat16*>(qkv->sin);
     args.ldcs = qkv->ldcs;
+    args.cs_tiled = qkv->cs_tiled;
     args.qw = reinterpret_cast<const __nv_bfloat16*>(qkv->qw);
     args.kw = reinterpret_cast<const __nv_bfloat16*>(qkv->kw);
     args.eps = qkv->eps;
@@ -1555,18 +1595,18 @@ extern "C" int w8_gemm_dequant_bf16(const int8_t* a, int64_t lda, const int8_t* 
                              reinterpret_cast<cudaStream_t>(stream), w8::kEpiBf16);
 }
 
-extern "C" int w8_gemm_qkv_norm_rope(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, const float* sx,
-                                     const float* sw, int64_t m, int64_t heads, int64_t kv_heads, int shared,
-                                     const uint16_t* cos, const uint16_t* sin, int64_t ldcs, const uint16_t* qw,
-                                     const uint16_t* kw, float eps, uint16_t* out, int64_t ld_head, int64_t ld_tok,
-                                     int64_t k, w8_stream_t stream) {
-  using namespace w8host;
+namespace w8host {
+static int qkv_norm_rope_common(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, const float* sx,
+                                const float* sw, int64_t m, int64_t heads, int64_t kv_heads, int shared,
+                                const uint16_t* cos, const uint16_t* sin, int64_t ldcs, int tiled, const uint16_t* qw,
+                                const uint16_t* kw, float eps, uint16_t* out, int64_t ld_head, int64_t ld_tok,
+                                int64_t k, w8_stream_t stream) {
   W8_CHECK_ARG(m >= 0 && heads >= 0 && kv_heads >= 0 && heads < 4096 && kv_heads < 4096, "bad size");
   const int64_t per_tok = shared ? heads : heads + 2 * kv_heads;
   if (m == 0 || per_tok == 0) return W8_OK;
   W8_CHECK_ARG(cos != nullptr && sin != nullptr && qw != nullptr && out != nullptr, "null pointer");
   W8_CHECK_ARG(shared || kv_heads == 0 || kw != nullptr, "null k_norm weight");
-  W8_CHECK_ARG(ldcs >= 256 && ld_tok >= 256 && ld_head >= ld_tok * m, "pitch too small");
+  W8_CHECK_ARG(ldcs >= (tiled ? 8 * m : 256) && ld_tok >= 256 && ld_head >= ld_tok * m, "pitch too small");
   W8_CHECK_ALIGN(aligned(cos, 16) && aligned(sin, 16) && ldcs % 8 == 0 && aligned(qw, 16) &&
                      (kw == nullptr || aligned(kw, 16)) && aligned(out, 16) && ld_head % 8 == 0 && ld_tok % 8 == 0,
                  "weights, cos/sin and the output must be 16-byte aligned with pitches %% 8 == 0");
@@ -1574,6 +1614,7 @@ extern "C" int w8_gemm_qkv_norm_rope(const int8_t* a, int64_t lda, const int8_t*
   q.cos = cos;
   q.sin = sin;
   q.ldcs = ldcs;
+  q.cs_tiled = tiled;
   q.qw = qw;
   q.kw = kw;
   q.eps = eps;
@@ -1583,4 +1624,24 @@ extern "C" int w8_gemm_qkv_norm_rope(const int8_t* a, int64_t lda, const int8_t*
   q.ld_tok = ld_tok;
   return gemm_common(a, lda, w, ldw, W8_B_NK, out, per_tok * 256, 2, sx, sw, m, per_tok * 256, k, nullptr, 0,
                      reinterpret_cast<cudaStream_t>(stream), w8::kEpiQkv, nullptr, 0, &q);
+}
+}  // namespace w8host
+
+extern "C" int w8_gemm_qkv_norm_rope(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, const float* sx,
+                                     const float* sw, int64_t m, int64_t heads, int64_t kv_heads, int shared,
+                                     const uint16_t* cos, const uint16_t* sin, int64_t ldcs, const uint16_t* qw,
+                                     const uint16_t* kw, float eps, uint16_t* out, int64_t ld_head, int64_t ld_tok,
+                                     int64_t k, w8_stream_t stream) {
+  return w8host::qkv_norm_rope_common(a, lda, w, ldw, sx, sw, m, heads, kv_heads, shared, cos, sin, ldcs, 0, qw, kw,
+                                      eps, out, ld_head, ld_tok, k, stream);
+}
+
+extern "C" int w8_gemm_qkv_norm_rope_tiled(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw,
+                                           const float* sx, const float* sw, int64_t m, int64_t heads,
+                                           int64_t kv_heads, int shared, const uint16_t* cos_t,
+                                           const uint16_t* sin_t, int64_t tile_pitch, const uint16_t* qw,
+                                           const uint16_t* kw, float eps, uint16_t* out, int64_t ld_head,
+                                           int64_t ld_tok, int64_t k, w8_stream_t stream) {
+  return w8host::qkv_norm_rope_common(a, lda, w, ldw, sx, sw, m, heads, kv_heads, shared, cos_t, sin_t, tile_pitch,
+                                      1, qw, kw, eps, out, ld_head, ld_tok, k, stream);
 }

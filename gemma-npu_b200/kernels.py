@@ -346,12 +346,26 @@ def qkv_norm_rope(y, cos, sin, qw, kw, eps, heads, kv_heads, head_dim, shared=Fa
     return q, out[heads: heads + kv_heads], out[heads + kv_heads:]
 
 
-def gemm_qkv_norm_rope(xq, w, sx, sw, cos, sin, qw, kw, eps, heads, kv_heads, head_dim, shared=False, out=None):
+def rope_tiles(cos, sin):
+    """cos / sin [T, D] bf16 -> the 8-column tiled tables (cos_t, sin_t), each [D / 8, T, 8],
+    that gemm_qkv_norm_rope(..., tiles=) reads with coalesced loads.  The tables depend only
+    on the positions, so a prefill lays them out once and every layer with the same RoPE
+    reuses them."""
+    _need(isinstance(cos, torch.Tensor) and isinstance(sin, torch.Tensor) and cos.shape == sin.shape,
+          "cos and sin must be tensors of one shape")
+    T, D = cos.shape
+    _need(D % 8 == 0, f"head_dim {D} must be a multiple of 8")
+    return tuple(t.contiguous().reshape(T, D // 8, 8).transpose(0, 1).contiguous() for t in (cos, sin))
+
+
+def gemm_qkv_norm_rope(xq, w, sx, sw, cos, sin, qw, kw, eps, heads, kv_heads, head_dim, shared=False, out=None,
+                       tiles=None):
     """The qkv GEMM and k_qkv (pipeline.py:233-242 + :72-86): xq int8 [T, K] with row scales
     sx, the resident qkv weight w [N, K] with channel scales sw -> (q [H, T, D], k, v), the
     same bits as qkv_norm_rope(gemm_dequant(xq, w, sx, sw), ...).  head_dim 256 runs as one
     kernel (the glue in the GEMM's epilogue, one head per 256-column tile, no bf16 [T, N]
-    intermediate); other head dims run the two kernels."""
+    intermediate); other head dims run the two kernels.  `tiles`: rope_tiles(cos, sin),
+    the same tables laid out for the fused kernel's loads (same result bits)."""
     T = xq.shape[0]
     per_tok = heads if shared else heads + 2 * kv_heads
     _need(w.shape[0] == per_tok * head_dim, f"w must have {per_tok * head_dim} rows")
@@ -375,10 +389,21 @@ def gemm_qkv_norm_rope(xq, w, sx, sw, cos, sin, qw, kw, eps, heads, kv_heads, he
         out = torch.empty((per_tok, T, head_dim), dtype=torch.bfloat16, device=xq.device)
     _need(out.dtype == torch.bfloat16 and out.is_cuda and tuple(out.shape) == (per_tok, T, head_dim)
           and out.stride(2) == 1, f"out must be bf16 ({per_tok}, {T}, {head_dim}) with unit stride along D")
-    _lib.call("w8_gemm_qkv_norm_rope", xq.data_ptr(), _ld(xq), w.data_ptr(), _ld(w), sx.data_ptr(), sw.data_ptr(),
-              T, heads, kv_heads, int(bool(shared)), cos.data_ptr(), sin.data_ptr(), cos.stride(0), qw.data_ptr(),
-              None if (shared or not kv_heads) else kw.data_ptr(), float(eps), out.data_ptr(), out.stride(0),
-              out.stride(1), K, _stream(xq))
+    kw_ptr = None if (shared or not kv_heads) else kw.data_ptr()
+    if tiles is None:
+        _lib.call("w8_gemm_qkv_norm_rope", xq.data_ptr(), _ld(xq), w.data_ptr(), _ld(w), sx.data_ptr(),
+                  sw.data_ptr(), T, heads, kv_heads, int(bool(shared)), cos.data_ptr(), sin.data_ptr(), cos.stride(0),
+                  qw.data_ptr(), kw_ptr, float(eps), out.data_ptr(), out.stride(0), out.stride(1), K, _stream(xq))
+    else:
+        ct, st = tiles
+        for t_, name in ((ct, "cos tiles"), (st, "sin tiles")):
+            _need(isinstance(t_, torch.Tensor) and t_.is_cuda and t_.dtype == torch.bfloat16
+                  and tuple(t_.shape) == (head_dim // 8, T, 8) and t_.stride(2) == 1 and (T == 1 or t_.stride(1) == 8),
+                  f"{name} must be bf16 [{head_dim // 8}, {T}, 8] as rope_tiles returns them")
+        _need(ct.stride(0) == st.stride(0), "cos and sin tiles must have the same pitch")
+        _lib.call("w8_gemm_qkv_norm_rope_tiled", xq.data_ptr(), _ld(xq), w.data_ptr(), _ld(w), sx.data_ptr(),
+                  sw.data_ptr(), T, heads, kv_heads, int(bool(shared)), ct.data_ptr(), st.data_ptr(), ct.stride(0),
+                  qw.data_ptr(), kw_ptr, float(eps), out.data_ptr(), out.stride(0), out.stride(1), K, _stream(xq))
     q = out[:heads]
     if shared:
         return q, q, q

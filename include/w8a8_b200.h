@@ -168,6 +168,19 @@ int w8_gemm_qkv_norm_rope(const int8_t* a, int64_t lda, const int8_t* w, int64_t
                           const uint16_t* kw, float eps, uint16_t* out, int64_t ld_head, int64_t ld_tok,
                           int64_t k, w8_stream_t stream);
 
+/* w8_gemm_qkv_norm_rope with cos / sin in an 8-column tiled layout, the same result bits:
+ * column d of token t at cos_t[(d / 8) * tile_pitch + t * 8 + d % 8] (tile_pitch >= 8 T,
+ * % 8 == 0), i.e. [D / 8][T][8].  The epilogue holds one token per thread, so with [T, D]
+ * tables every 16-byte load of a warp touches 32 rows; tiled, the warp's 32 tokens read
+ * 512 contiguous bytes.  The tables are per prompt (positions), shared by every layer with
+ * the same RoPE, so a caller lays them out once.  Same reference call as
+ * w8_gemm_qkv_norm_rope. */
+int w8_gemm_qkv_norm_rope_tiled(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, const float* sx,
+                                const float* sw, int64_t m, int64_t heads, int64_t kv_heads, int shared,
+                                const uint16_t* cos_t, const uint16_t* sin_t, int64_t tile_pitch,
+                                const uint16_t* qw, const uint16_t* kw, float eps, uint16_t* out,
+                                int64_t ld_head, int64_t ld_tok, int64_t k, w8_stream_t stream);
+
 /* ---- the RMSNorm / residual glue around the GEMMs (bf16 rows) ------------
  * One warp per row, the row held in registers: row length n <= 2048, n % 8 == 0, rows
  * and norm weights 16-byte aligned, pitches in elements % 8 == 0, q 8-byte aligned.

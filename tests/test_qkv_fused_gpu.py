@@ -57,6 +57,14 @@ def test_fused_equals_two_step_path(cuda, t, nh, kv, shared, k):
     for name, g, w_ in zip("qkv", got, want):
         assert torch.equal(g.view(torch.int16), w_.view(torch.int16)), name
     assert torch.isnan(big[:, t:].float()).all() and torch.isnan(big[:, :, 256:].float()).all()  # nothing outside
+    # the same kernel reading cos / sin from the 8-column tiled tables: the same bits
+    big.fill_(float("nan"))
+    got = w8.gemm_qkv_norm_rope(x, wq, sx, sw, cos, sin, qw, kw, eps, nh, kv, 256, shared, out=out,
+                                tiles=w8.rope_tiles(cos, sin))
+    torch.cuda.synchronize()
+    for name, g, w_ in zip("qkv", got, want):
+        assert torch.equal(g.view(torch.int16), w_.view(torch.int16)), "tiled " + name
+    assert torch.isnan(big[:, t:].float()).all() and torch.isnan(big[:, :, 256:].float()).all()
 
 
 def test_fused_against_oracle(cuda):
