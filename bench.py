@@ -47,6 +47,10 @@ NOMINAL_INT8_TOPS = 4500.0
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 TRAFFIC_FILE = os.path.join(ROOT, "profiles", "gemm_traffic_config1.txt")
 SUSTAINED_REGION_S = 1.0  # timed regions at least this long are judged against the sustained peak
+# prefill_gpu's qkv at head_dim 256: the GEMM + k_qkv row kernel.  The fused kernel
+# (w8_gemm_qkv_norm_rope_tiled) is faster alone (25.9 against 30.5 us) but, inside the
+# whole dependent prefill, measured 9.43 against 9.40 ms per prefill.
+FUSED_QKV_IN_PREFILL = False
 
 
 def macs_per_token():
@@ -555,7 +559,8 @@ def fused_layer(w8, dev, stream, m, steps, warmup, world, layers=35):
     on the GPU (k_in, qkv + k_qkv, k_attn_out, o + k_post_attn, gate_up + k_gelu,
     down + k_post_ff; pipeline.py:66-114), attention excluded (a synthetic o of the right
     shape stands in).  Fused: dequant / gelu in the GEMM epilogues plus warp-per-row glue
-    kernels.  Unfused: int32 GEMMs, then the reference's glue expressions as torch ops on
+    kernels (k_qkv as the row kernel: inside the dependent layer chain it measured as fast
+    as the qkv GEMM with k_qkv in its epilogue, 180 against 181 us per layer).  Unfused: int32 GEMMs, then the reference's glue expressions as torch ops on
     the same GPU."""
     eps, nh, kv, d, hid = 1e-6, 8, 1, 256, 1536
     g = torch.Generator(device=dev).manual_seed(57)
@@ -635,7 +640,7 @@ def fused_layer(w8, dev, stream, m, steps, warmup, world, layers=35):
 
 def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35, kv_shared=0):
     """One prompt through every decoder layer's linear set, glue and attention on the GPU,
-    the layer body of pipeline.py:262-310: k_in, qkv GEMM + k_qkv, attention, k_attn_out, o GEMM + k_post_attn, gate/up GEMM + k_gelu, down GEMM +
+    the layer body of pipeline.py:262-310: k_in, qkv GEMM + k_qkv (one kernel at head_dim 256), attention, k_attn_out, o GEMM + k_post_attn, gate/up GEMM + k_gelu, down GEMM +
     k_post_ff, PLE gate GEMM (1536 -> 256) + k_ple_gate, PLE projection GEMM (256 -> 1536) +
     k_ple_out.  Gemma E2B attention layout: every 5th layer full causal with head_dim 512
     (qkv 5120 x 1536, o 1536 x 4096), the others sliding window 512 with head_dim 256; 8
@@ -677,17 +682,29 @@ def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35, kv_shared=0
     # keys / values of the last unshared layer of each attention type, for the shared layers
     kv_store = {d: torch.empty((2 * kv, m, d), dtype=torch.bfloat16, device=dev) for d in tables}
 
+    tiles = w8.rope_tiles(*tables[256])  # per prompt, like the tables: shared by every 256 layer
+
+    def qkv(xq, sx, l, shared):
+        """Unshared head_dim-256 layers: k_qkv in the qkv GEMM's epilogue (RoPE tables tiled);
+        KV-shared q-only layers and head_dim 512: the GEMM, then the k_qkv row kernel."""
+        d = l["d"]
+        kn = None if shared else l["kn"]
+        if d == 256 and not shared and FUSED_QKV_IN_PREFILL:
+            return w8.gemm_qkv_norm_rope(xq, l["qkv"][0], sx, l["qkv"][1], *tables[d], l["qn"], kn, eps, nh, kv, d,
+                                         shared=shared, tiles=tiles)
+        y = w8.gemm_dequant(xq, l["qkv"][0], sx, l["qkv"][1])
+        return w8.qkv_norm_rope(y, *tables[d], l["qn"], kn, eps, nh, kv, d, shared=shared)
+
     def step():
         h.copy_(h0)
         xq, sx = w8.rms_quant(h, L[0]["w_in"], eps)
         for i, l in enumerate(L):
             d = l["d"]
-            y = w8.gemm_dequant(xq, l["qkv"][0], sx, l["qkv"][1])
             if l["shared"]:
-                q, _, _ = w8.qkv_norm_rope(y, *tables[d], l["qn"], None, eps, nh, kv, d, shared=True)
+                q, _, _ = qkv(xq, sx, l, True)
                 k, v = kv_store[d][:kv], kv_store[d][kv:]
             else:
-                q, k, v = w8.qkv_norm_rope(y, *tables[d], l["qn"], l["kn"], eps, nh, kv, d)
+                q, k, v = qkv(xq, sx, l, False)
                 if i < first_shared and any(x["d"] == d for x in L[first_shared:]) and \
                         all(x["d"] != d for x in L[i + 1: first_shared]):
                     kv_store[d][:kv].copy_(k)  # the last unshared layer of this type stores its K / V
@@ -748,8 +765,15 @@ def qkv_paths(w8, dev, stream, m, steps, warmup, world):
         for wq, sw in ws:
             w8.gemm_qkv_norm_rope(xq, wq, sx, sw, cos, sin, qn, qn, 1e-6, nh, kv, d, out=out)
 
+    tiles = w8.rope_tiles(cos, sin)  # once per prompt
+
+    def fused_tiled():
+        for wq, sw in ws:
+            w8.gemm_qkv_norm_rope(xq, wq, sx, sw, cos, sin, qn, qn, 1e-6, nh, kv, d, out=out, tiles=tiles)
+
     res = {}
-    for label, fn in (("gemm_then_row_kernel", two_step), ("fused_epilogue", fused)):
+    for label, fn in (("gemm_then_row_kernel", two_step), ("fused_epilogue", fused),
+                      ("fused_epilogue_tiled_rope", fused_tiled)):
         gr = capture(fn, stream)
         res[label + "_us"] = timed(lambda: gr.replay(), steps, warmup, stream, world) / steps * 1e3 / len(ws)
         del gr
