@@ -1314,7 +1314,7 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
     const int64_t single_waves = ((m + 127) / 128 * heads_n + sms - 1) / sms;
     if (single_waves < pair_waves) pair = false;
   }
-  const int rows_per_tile = pair ? 2 * w8::kBM : w8::kBM;
+  int rows_per_tile = pair ? 2 * w8::kBM : w8::kBM;
   // Tile width on CTA pairs over a K-major B: the narrowest of 64, 128, 192 and 256
   // columns that needs no more waves of workers than any other.  A narrower tile costs
   // more per column (a 192-wide tile ~1.28x of a 256-wide one, a 64-wide one ~3x) but
@@ -1342,6 +1342,22 @@ static int gemm_common(const int8_t* a, int64_t lda, const int8_t* b, int64_t ld
       if (v <= best) {
         best = v;
         bn = w;
+      }
+    }
+    // 128 x 256 tiles on single CTAs instead, when they need fewer waves than the best pair
+    // width and that width is a narrow one (its tiles already cost more per column): qkv
+    // 3658 x 2560 x 1536 as 290 single-CTA tiles on 148 SMs takes 2 waves and 18.5 us,
+    // against 3 waves of 210 192-wide pair tiles, 21.1 us.  Against 256-wide pair tiles the
+    // pairs stay faster even with a wave more (PLE 8960 x 1536: 51.6 against 52.3 us).
+    if (bn < w8::kBN) {
+      int sms = 0;
+      st = num_sms(&sms);
+      if (st != W8_OK) return st;
+      const int64_t single_waves = ((m + w8::kBM - 1) / w8::kBM * ((n + w8::kBN - 1) / w8::kBN) + sms - 1) / sms;
+      if (single_waves < best) {
+        pair = false;
+        rows_per_tile = w8::kBM;
+        bn = w8::kBN;
       }
     }
   }
