@@ -104,7 +104,7 @@ def gemm_traffic_per_launch(layers, m):
     total = layers * sum(per[name] for name, _, _ in LAYER_SHAPES) + per[PLE_SHAPE[0]]
     return {"bytes": total / (layers * len(LAYER_SHAPES) + 1),
             "note": "per GEMM launch, averaged over one step: dram__bytes_read.sum + 32 x "
-                    "lts__t_sectors_op_write.sum of each shape's single-launch ncu capture "
+                    "lts__t_sectors_srcunit_tex_op_write.sum of each shape's single-launch ncu capture "
                     f"({os.path.relpath(TRAFFIC_FILE, ROOT)})"}
 
 
