@@ -47,10 +47,6 @@ NOMINAL_INT8_TOPS = 4500.0
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 TRAFFIC_FILE = os.path.join(ROOT, "profiles", "gemm_traffic_config1.txt")
 SUSTAINED_REGION_S = 1.0  # timed regions at least this long are judged against the sustained peak
-# prefill_gpu's qkv at head_dim 256: the GEMM + k_qkv row kernel.  The fused kernel
-# (w8_gemm_qkv_norm_rope_tiled) is faster alone (25.9 against 30.5 us) but, inside the
-# whole dependent prefill, measured 9.43 against 9.40 ms per prefill.
-FUSED_QKV_IN_PREFILL = False
 
 
 def macs_per_token():
@@ -640,7 +636,7 @@ def fused_layer(w8, dev, stream, m, steps, warmup, world, layers=35):
 
 def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35, kv_shared=0):
     """One prompt through every decoder layer's linear set, glue and attention on the GPU,
-    the layer body of pipeline.py:262-310: k_in, qkv GEMM + k_qkv (one kernel at head_dim 256), attention, k_attn_out, o GEMM + k_post_attn, gate/up GEMM + k_gelu, down GEMM +
+    the layer body of pipeline.py:262-310: k_in, qkv GEMM + k_qkv, attention, k_attn_out, o GEMM + k_post_attn, gate/up GEMM + k_gelu, down GEMM +
     k_post_ff, PLE gate GEMM (1536 -> 256) + k_ple_gate, PLE projection GEMM (256 -> 1536) +
     k_ple_out.  Gemma E2B attention layout: every 5th layer full causal with head_dim 512
     (qkv 5120 x 1536, o 1536 x 4096), the others sliding window 512 with head_dim 256; 8
@@ -682,18 +678,13 @@ def prefill_gpu(w8, dev, stream, m, steps, warmup, world, layers=35, kv_shared=0
     # keys / values of the last unshared layer of each attention type, for the shared layers
     kv_store = {d: torch.empty((2 * kv, m, d), dtype=torch.bfloat16, device=dev) for d in tables}
 
-    tiles = w8.rope_tiles(*tables[256])  # per prompt, like the tables: shared by every 256 layer
-
     def qkv(xq, sx, l, shared):
-        """Unshared head_dim-256 layers: k_qkv in the qkv GEMM's epilogue (RoPE tables tiled);
-        KV-shared q-only layers and head_dim 512: the GEMM, then the k_qkv row kernel."""
+        """The qkv GEMM (dequant fused), then the k_qkv row kernel.  The GEMM with k_qkv in its
+        epilogue (w8_gemm_qkv_norm_rope_tiled) is faster alone (bench qkv_paths) but measured
+        9.43 against 9.40 ms per prefill inside this dependent chain."""
         d = l["d"]
-        kn = None if shared else l["kn"]
-        if d == 256 and not shared and FUSED_QKV_IN_PREFILL:
-            return w8.gemm_qkv_norm_rope(xq, l["qkv"][0], sx, l["qkv"][1], *tables[d], l["qn"], kn, eps, nh, kv, d,
-                                         shared=shared, tiles=tiles)
         y = w8.gemm_dequant(xq, l["qkv"][0], sx, l["qkv"][1])
-        return w8.qkv_norm_rope(y, *tables[d], l["qn"], kn, eps, nh, kv, d, shared=shared)
+        return w8.qkv_norm_rope(y, *tables[d], l["qn"], None if shared else l["kn"], eps, nh, kv, d, shared=shared)
 
     def step():
         h.copy_(h0)
