@@ -234,17 +234,20 @@ static int gemv_dispatch(const uint16_t* xh, int64_t ldx, const int8_t* w, int64
   const int st2 = num_sms(&sms);
   if (st2 != W8_OK) return st2;
   // Smallest (S, J) whose slice covers K: x stays within 64 fp32 registers per lane.
-  // R rows per team per step: the smallest R whose CTAs (two per SM) cover the matrix in
-  // one wave, so that no CTA waits for a second DRAM round trip of weights; a matrix no R
-  // covers in one wave (the LM head) takes R = 4 (J <= 3) or 2 (J = 4), which keep the most
-  // weight bytes in flight per warp that the registers allow.  One row per team (R = 1)
+  // R rows per team per step: the smallest R whose CTAs (two per SM; one per SM when K >
+  // 1536) cover the matrix in one wave, so that no CTA waits for a second DRAM round trip
+  // of weights; a matrix no R covers in one wave (the LM head) takes R = 4 (J <= 3) or 2
+  // (J = 4), which keep the most weight bytes in flight per warp that the registers allow.
+  // The long-K GEMVs of a decode step (o 1536 x 2048, down 1536 x 6144) take one CTA per
+  // SM: they then leave SM slots free, and the next GEMV of the dependent chain starts its
+  // weight loads there while they run (140 layer GEMVs: 451 -> 427 us).  One row per team (R = 1)
   // also prefetches a second step's rows (measured in a dependent chain: down 1536 x 6144
   // 5.2 -> 4.2 us and 8960 x 1536 5.5 -> 4.4 us with R = 4 at one or more CTAs per SM,
   // against R = 1 at two).
 #define W8_GEMV_R(J, S, R) launch_gemv<J, S, R, LOGITS>(x, ldx, w, ldw, s, y, ldy, ti, ni, ki, cap, stream, best)
 #define W8_GEMV(J, S, RMAX)                                                                  \
   {                                                                                          \
-    const int64_t teams = 2ll * sms * (w8::kGemvWarps / (S));                                \
+    const int64_t teams = ((J) * (S) > 3 ? 1ll : 2ll) * sms * (w8::kGemvWarps / (S));         \
     if (n <= teams * 1) return W8_GEMV_R(J, S, 1);                                           \
     if (n <= teams * 2) return W8_GEMV_R(J, S, 2);                                           \
     if constexpr ((RMAX) == 4) {                                                             \
