@@ -175,17 +175,20 @@ static int launch_gemv(const __nv_bfloat16* x, int64_t ldx, const int8_t* w, int
   int st = num_sms(&sms);
   if (st != W8_OK) return st;
   // The (unused) dynamic shared memory caps residency at two CTAs per SM: with three or
-  // four, a chain of dependent GEMVs ran slower (qkv 2560 x 1536: 3.07 against 3.74 us).
+  // four, a chain of dependent GEMVs ran slower (qkv 2560 x 1536: 3.07 against 3.74 us;
+  // the 140-GEMV decode chain 497 against 524 us).  The LM head, a long stream of its own,
+  // takes three (65.8 -> 63.5 us).
+  constexpr int smem = LOGITS ? w8::kGemvSmemCapHead : w8::kGemvSmemCap;
   int device = 0;
   W8_CUDA_TRY(cudaGetDevice(&device));
   static bool done[64] = {};
   if (device < 0 || device >= 64) return W8_ERR_UNSUPPORTED;
   if (!done[device]) {
-    W8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, w8::kGemvSmemCap));
+    W8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     done[device] = true;
   }
   int per_sm = 0;
-  W8_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, w8::kGemvThreads, w8::kGemvSmemCap));
+  W8_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, w8::kGemvThreads, smem));
   if (per_sm < 1) per_sm = 1;
   constexpr int rows_per_cta = (w8::kGemvWarps / S) * R;
   const int64_t need = (static_cast<int64_t>(n) + rows_per_cta - 1) / rows_per_cta;
@@ -196,7 +199,7 @@ static int launch_gemv(const __nv_bfloat16* x, int64_t ldx, const int8_t* w, int
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(w8::kGemvThreads, 1, 1);
-  cfg.dynamicSmemBytes = w8::kGemvSmemCap;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -10,7 +10,8 @@ namespace w8 {
 
 constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
-constexpr int kGemvSmemCap = 96 * 1024;  // dynamic shared memory per CTA: at most 2 CTAs per SM
+constexpr int kGemvSmemCap = 96 * 1024;      // dynamic shared memory per CTA: at most 2 CTAs per SM
+constexpr int kGemvSmemCapHead = 72 * 1024;  // the LM head: at most 3 CTAs per SM
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;
