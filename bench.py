@@ -508,46 +508,62 @@ def glue_rows(w8, dev, stream, m, steps, warmup, world, pk):
     widths: hidden 1536, 8 query heads on 1 KV head of 256, PLE width 256).  Each kernel runs
     over 8 sets of distinct buffers in one graph (> 126 MB of L2 per pass, except the
     256-wide k_ple_gate), so it streams from HBM; us per call, algorithmic GB/s (bytes read + written
-    once) and the fraction of the measured HBM copy bandwidth."""
-    eps, hid, nh, kv, d, pw, sets = 1e-6, 1536, 8, 1, 256, 256, 8
+    once) and the fraction of the measured HBM copy bandwidth.  `floor_us` is the same kernel
+    over 8 rows in the same graph (its launch, its wait for the previous kernel and one row's
+    round trip); `remainder_frac` is the HBM fraction of the time the other rows add."""
+    eps, hid, nh, kv, d, pw, sets, few = 1e-6, 1536, 8, 1, 256, 256, 8, 8
     g = torch.Generator(device=dev).manual_seed(91)
 
     def bf(*shape, scale=1.0):
         return (torch.randn(shape, device=dev, generator=g) * scale).to(torch.bfloat16)
 
     w1, w2, qn, kn = bf(hid, scale=0.1) + 1, bf(hid, scale=0.1) + 1, bf(d, scale=0.1) + 1, bf(d, scale=0.1) + 1
-    cos, sin = bf(m, d), bf(m, d)
-    cases = {
-        "k_in": (lambda i, b: w8.rms_quant(b[0], w1, eps), lambda: [bf(m, hid)], 3 * m * hid + 4 * m),
-        "k_qkv_d256": (lambda i, b: w8.qkv_norm_rope(b[0], cos, sin, qn, kn, eps, nh, kv, d, out=b[1]),
-                       lambda: [bf(m, (nh + 2 * kv) * d), torch.empty(((nh + 2 * kv), m, d), dtype=torch.bfloat16,
-                                                                     device=dev)],
-                       4 * m * (nh + 2 * kv) * d + 4 * m * d),
-        "k_attn_out": (lambda i, b: w8.attn_out_quant(b[0]), lambda: [bf(nh, m, d)], 3 * m * nh * d + 4 * m),
-        "k_post_attn": (lambda i, b: w8.post_norm_quant(b[0], b[1], w1, w2, eps, h=b[2]),
-                        lambda: [bf(m, hid), bf(m, hid), torch.empty((m, hid), dtype=torch.bfloat16, device=dev)],
-                        7 * m * hid + 4 * m),
-        "k_post_ff": (lambda i, b: w8.post_norm_quant(b[0], b[1], w1, None, eps, h=b[2]),
-                      lambda: [bf(m, hid), bf(m, hid), torch.empty((m, hid), dtype=torch.bfloat16, device=dev)],
-                      7 * m * hid + 4 * m),
-        "k_ple_gate": (lambda i, b: w8.ple_gate_quant(b[0], b[1]), lambda: [bf(m, pw), bf(m, pw)], 5 * m * pw + 4 * m),
-        "k_ple_out+k_in": (lambda i, b: w8.ple_out(b[0], b[1], w1, 0.75, eps, w_next=w2, h=b[2]),
-                           lambda: [bf(m, hid), bf(m, hid), torch.empty((m, hid), dtype=torch.bfloat16, device=dev)],
-                           7 * m * hid + 4 * m),
-    }
-    out = {}
-    for name, (call, make, nbytes) in cases.items():
+    cos_all, sin_all = bf(m, d), bf(m, d)
+
+    def make_cases(t):
+        cos, sin = cos_all[:t], sin_all[:t]
+        return {
+            "k_in": (lambda i, b: w8.rms_quant(b[0], w1, eps), lambda: [bf(t, hid)], 3 * t * hid + 4 * t),
+            "k_qkv_d256": (lambda i, b: w8.qkv_norm_rope(b[0], cos, sin, qn, kn, eps, nh, kv, d, out=b[1]),
+                           lambda: [bf(t, (nh + 2 * kv) * d),
+                                    torch.empty(((nh + 2 * kv), t, d), dtype=torch.bfloat16, device=dev)],
+                           4 * t * (nh + 2 * kv) * d + 4 * t * d),
+            "k_attn_out": (lambda i, b: w8.attn_out_quant(b[0]), lambda: [bf(nh, t, d)], 3 * t * nh * d + 4 * t),
+            "k_post_attn": (lambda i, b: w8.post_norm_quant(b[0], b[1], w1, w2, eps, h=b[2]),
+                            lambda: [bf(t, hid), bf(t, hid), torch.empty((t, hid), dtype=torch.bfloat16, device=dev)],
+                            7 * t * hid + 4 * t),
+            "k_post_ff": (lambda i, b: w8.post_norm_quant(b[0], b[1], w1, None, eps, h=b[2]),
+                          lambda: [bf(t, hid), bf(t, hid), torch.empty((t, hid), dtype=torch.bfloat16, device=dev)],
+                          7 * t * hid + 4 * t),
+            "k_ple_gate": (lambda i, b: w8.ple_gate_quant(b[0], b[1]), lambda: [bf(t, pw), bf(t, pw)],
+                           5 * t * pw + 4 * t),
+            "k_ple_out+k_in": (lambda i, b: w8.ple_out(b[0], b[1], w1, 0.75, eps, w_next=w2, h=b[2]),
+                               lambda: [bf(t, hid), bf(t, hid), torch.empty((t, hid), dtype=torch.bfloat16, device=dev)],
+                               7 * t * hid + 4 * t),
+        }
+
+    def run(call, make):
         bufs = [make() for _ in range(sets)]
         graph = capture(lambda: [call(i, b) for i, b in enumerate(bufs)], stream)
         us = timed(lambda: graph.replay(), steps, warmup, stream, world) / (steps * sets) * 1e3
-        gbs = nbytes / (us * 1e-6) / 1e9
-        out[name] = {"us": us, "bytes": nbytes, "gbs": gbs, "frac_hbm": gbs / pk["hbm_gbs"]}
         del graph, bufs
+        return us
+
+    out = {}
+    full, small = make_cases(m), make_cases(few)
+    for name, (call, make, nbytes) in full.items():
+        us = run(call, make)
+        floor = run(*small[name][:2])
+        gbs = nbytes / (us * 1e-6) / 1e9
+        rest = nbytes / ((us - floor) * 1e-6) / 1e9 if us > floor else None
+        out[name] = {"us": us, "bytes": nbytes, "gbs": gbs, "frac_hbm": gbs / pk["hbm_gbs"], "floor_us": floor,
+                     "remainder_frac": None if rest is None else rest / pk["hbm_gbs"]}
     torch.cuda.synchronize()
     return {"workload": f"glue row kernels at M={m} (hidden 1536, H=8 / KV=1 / D=256, PLE 256), 8 buffer sets "
                         "rotated per graph so each call streams from HBM",
             "kernels": out,
-            "note": "bound by each warp's instruction chain (one row per warp, one wave), not by HBM"}
+            "note": "each call pays a floor (launch, wait for the previous kernel, one row's DRAM round trip: "
+                    "floor_us, the same kernel over 8 rows) before its rows stream; one row per warp, one wave"}
 
 
 def fused_layer(w8, dev, stream, m, steps, warmup, world, layers=35):

@@ -30,6 +30,7 @@
  *   w8_ple_out_bf16         pipeline.py:124-127 (k_ple_out) [+ :66-69, the next layer's k_in]
  *   w8_qkv_norm_rope_bf16   pipeline.py:72-86 (k_qkv)
  *   w8_gemm_qkv_norm_rope   pipeline.py:233-242 (the qkv GEMM) + :72-86 (k_qkv) in one kernel
+ *   w8_gemm_qkv_norm_rope_tiled  the same, cos / sin in an 8-column tiled layout
  *   w8_attention_prefill_bf16 pipeline.py:139-180 (full_attention / sliding_attention)
  *   w8_attention_prefill_quant the same followed by pipeline.py:88-92 (k_attn_out)
  */
