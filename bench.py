@@ -434,7 +434,8 @@ def sharded_head(w8, dev, stream, world, steps, warmup, pk):
         torch.cuda.synchronize()
         peer = {"us_per_token_peer": pms * 1e3, "us_per_token_peer_greedy": pgms * 1e3,
                 "peer_note": "w8_lm_head_peer_f32: one kernel per rank, each logit stored into every rank's gathered "
-                             "buffer through CUDA IPC peer pointers, ready/done flags in the same buffers; no NCCL"}
+                             "buffer through CUDA IPC peer pointers, ready/done flags in the same buffers; no NCCL. "
+                             "The greedy path (w8_lm_head_peer_argmax) sends only the 8-byte keys"}
         head_p.close()
     shard_bytes = (head.r1 - head.r0) * (HIDDEN + 2)
     return {"workload": f"config 4: LM head {VOCAB}x{HIDDEN} int8 split by rows over {world} GPU(s), "

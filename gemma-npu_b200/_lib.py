@@ -115,6 +115,8 @@ SIGNATURES.update({
     "w8_peer_free": (_i, [_p]),
     "w8_lm_head_peer_f32": (_i, [_p, _p, _p, _f, _i64, _i64, _i64, _i64, _i, _i, ctypes.POINTER(ctypes.c_void_p), _p,
                                  _p]),
+    "w8_lm_head_peer_argmax": (_i, [_p, _p, _p, _f, _i64, _i64, _i64, _i64, _i, _i, ctypes.POINTER(ctypes.c_void_p), _p,
+                                 _p]),
 })
 
 _lock = threading.Lock()

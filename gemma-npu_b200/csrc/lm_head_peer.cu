@@ -49,6 +49,7 @@ struct PeerHeadArgs {
   uint32_t* state;                       // this rank's: [0] CTAs done, [1] epoch, [2] abort
   unsigned long long* best_local;        // this rank's greedy key of the call
   unsigned long long* best;              // output: the greedy key over all ranks (or null)
+  int keys_only;                         // 1: only the greedy keys travel; logits stay local
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
@@ -134,6 +135,7 @@ __global__ void __launch_bounds__(kGemvThreads)
 
   uint32_t* const abort_word = a.state + 2;
   const bool vec = kVec && a.row0 % 4 == 0;
+  const bool send = !a.keys_only;  // the logits go to the other ranks (not for keys only)
   if (threadIdx.x == 0) {
     const uint32_t t = ld_relaxed_gpu(a.state + 1) + 1u;
     // "This rank has started call t": written by every CTA (the same value), so the
@@ -143,7 +145,7 @@ __global__ void __launch_bounds__(kGemvThreads)
     // Rows whose logits go out one by one (no 16-byte chunks) wait for every peer here;
     // chunked rows are computed first and only the sending warp waits, before its first
     // send (by then the peers have started as well).
-    s_ok = vec ? 1 : (wait_all_sys(a.ready[a.me], a.world, a.me, t, abort_word) ? 1 : 0);
+    s_ok = (vec || !send) ? 1 : (wait_all_sys(a.ready[a.me], a.world, a.me, t, abort_word) ? 1 : 0);
   }
   __syncthreads();
   const bool ok = s_ok != 0;
@@ -215,12 +217,12 @@ __global__ void __launch_bounds__(kGemvThreads)
       mine = max(mine, argmax_key(f, a.row0 + row));
       if (vec) {
         tile[buf][n0 - base + lane] = f;
-      } else {
+      } else if (send) {
         for (int r = 0; r < a.world; ++r)
           if (r != a.me) a.logits[r][a.row0 + row] = f;
       }
     }
-    if (vec) {
+    if (vec && send) {
       __syncthreads();
       if (warp == 0 && !peers_ready) {
         bool seen = false;
@@ -250,10 +252,12 @@ __global__ void __launch_bounds__(kGemvThreads)
 
   __syncthreads();
   if (threadIdx.x == 0) {
-    // This CTA's stores into every rank's buffer are ordered before its count (an
-    // acquire-release fence at system scope: the CTA barrier above makes them this
-    // thread's to order).
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    // This CTA's stores into every rank's buffer are ordered before its count at GPU
+    // scope (the CTA barrier above makes them this thread's to order); the last CTA,
+    // having seen every count, orders them all at system scope with one fence before it
+    // raises this rank's flags (release is cumulative), so only one CTA per call pays a
+    // system-scope fence.
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
     if (atomicAdd(a.state + 0, 1u) == gridDim.x - 1u) {
       // The last CTA of this rank: publish the rank's key and flag, then wait for all.
       asm volatile("fence.acq_rel.sys;" ::: "memory");
@@ -373,9 +377,28 @@ extern "C" int w8_peer_free(void* ptr) {
   return W8_OK;
 }
 
+namespace w8host {
+static int lm_head_peer(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap, int64_t n, int64_t k,
+                        int64_t row0, int64_t vocab, int world, int rank, void* const* bufs, uint64_t* best,
+                        int keys_only, w8_stream_t stream);
+}  // namespace w8host
+
 extern "C" int w8_lm_head_peer_f32(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap, int64_t n,
                                    int64_t k, int64_t row0, int64_t vocab, int world, int rank, void* const* bufs,
                                    uint64_t* best, w8_stream_t stream) {
+  return w8host::lm_head_peer(x, w, s, cap, n, k, row0, vocab, world, rank, bufs, best, 0, stream);
+}
+
+extern "C" int w8_lm_head_peer_argmax(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap, int64_t n,
+                                      int64_t k, int64_t row0, int64_t vocab, int world, int rank,
+                                      void* const* bufs, uint64_t* best, w8_stream_t stream) {
+  W8_CHECK_ARG(best != nullptr, "null greedy-key output");
+  return w8host::lm_head_peer(x, w, s, cap, n, k, row0, vocab, world, rank, bufs, best, 1, stream);
+}
+
+int w8host::lm_head_peer(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap, int64_t n, int64_t k,
+                         int64_t row0, int64_t vocab, int world, int rank, void* const* bufs, uint64_t* best,
+                         int keys_only, w8_stream_t stream) {
   using namespace w8host;
   W8_CHECK_ARG(world >= 1 && world <= w8::kPeerMax && rank >= 0 && rank < world,
                "world %d / rank %d out of range (1..%d ranks)", world, rank, w8::kPeerMax);
@@ -407,6 +430,7 @@ extern "C" int w8_lm_head_peer_f32(const uint16_t* x, const int8_t* w, const uin
   a.state = reinterpret_cast<uint32_t*>(own + off + 128);
   a.best_local = reinterpret_cast<unsigned long long*>(own + off + 144);
   a.best = reinterpret_cast<unsigned long long*>(best);
+  a.keys_only = keys_only;
   int device = 0;
   const int st = require_sm100(&device);
   if (st != W8_OK) return st;

@@ -132,10 +132,11 @@ class ShardedInt8Head:
             self.peer = PeerBuffers(self.vocab, group, self.device)
             self.best = torch.zeros((1,), dtype=torch.int64, device=self.device)
 
-    def _peer_call(self, h, best):
+    def _peer_call(self, h, best, keys_only=False):
         h = h.reshape(-1).to(torch.bfloat16).contiguous()
         n = self.r1 - self.r0
-        _lib.call("w8_lm_head_peer_f32", h.data_ptr(), self.wq.data_ptr() if n else None, self.sw.data_ptr(),
+        entry = "w8_lm_head_peer_argmax" if keys_only else "w8_lm_head_peer_f32"
+        _lib.call(entry, h.data_ptr(), self.wq.data_ptr() if n else None, self.sw.data_ptr(),
                   self.cap, n, self.hidden, self.r0, self.vocab, self.world, self.rank, self.peer.table,
                   best.data_ptr() if best is not None else None, torch.cuda.current_stream(self.device).cuda_stream)
         return self.peer.logits
@@ -163,9 +164,10 @@ class ShardedInt8Head:
         """The greedy token (gemma_npu.py:291, logits.argmax()) without gathering the logits:
         each rank folds its shard's argmax inside the head GEMV, re-keys it with the global
         row id, and one 8-byte all-gather per rank picks the winner (ties: lowest id).
-        With transport "peer" the keys travel with the logits inside the one kernel."""
+        With transport "peer" only the keys travel, inside the head kernel
+        (w8_lm_head_peer_argmax); the logits stay on their rank."""
         if self.peer is not None:
-            self._peer_call(h, self.best)
+            self._peer_call(h, self.best, keys_only=True)
             return (0xFFFFFFFF - (self.best.reshape(()) & 0xFFFFFFFF))
         n = self.r1 - self.r0
         if n > 0:

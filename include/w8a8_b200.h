@@ -21,6 +21,7 @@
  *   w8_lm_head_f32          gemma_npu.py:170-172 (Int8Head.forward) + pipeline.py:335-338 (softcap)
  *   w8_lm_head_argmax_f32   the same + the greedy token argmax (gemma_npu.py:291)
  *   w8_lm_head_peer_f32     the same split by rows over a node's GPUs, all-gathered over NVLink
+ *   w8_lm_head_peer_argmax  its greedy token only (gemma_npu.py:291), keys exchanged over NVLink
  *   w8_gemm_gelu_up_quant   pipeline.py:102-107 (k_gelu) fused onto the gate/up GEMM of
  *                           pipeline.py:233-242 (Prefill.gemm)
  *   w8_rms_quant_bf16       pipeline.py:66-69 (k_in)
@@ -357,6 +358,17 @@ int w8_peer_free(void* ptr);
 int w8_lm_head_peer_f32(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap, int64_t n, int64_t k,
                         int64_t row0, int64_t vocab, int world, int rank, void* const* bufs, uint64_t* best,
                         w8_stream_t stream);
+
+/* The greedy token of the same sharded head without gathering the logits
+ * (gemma_npu.py:291, logits.argmax()): each rank's kernel computes its shard's logits into
+ * its own buffer only (the other ranks' parts of it are left as they were), and only the
+ * 8-byte greedy keys travel, so a decode step pays one flag round trip over NVLink instead
+ * of a 1 MB all-gather.  *best gets the winning key as w8_lm_head_argmax_f32 packs it
+ * (global row ids).  Calls of either entry point share one sequence of epochs: every rank
+ * makes the same calls, of the same kind, in the same order. */
+int w8_lm_head_peer_argmax(const uint16_t* x, const int8_t* w, const uint16_t* s, float cap, int64_t n,
+                           int64_t k, int64_t row0, int64_t vocab, int world, int rank, void* const* bufs,
+                           uint64_t* best, w8_stream_t stream);
 
 #ifdef __cplusplus
 }
