@@ -336,6 +336,88 @@ __global__ void __launch_bounds__(32 * kGlueWarps) qkv_rows_kernel(const QkvArgs
     if (j < slots && active) *reinterpret_cast<uint4*>(orow + (lane + 32 * j) * 8) = v[j];
 }
 
+// k_qkv at head_dim 256 with two (token, head) jobs per warp: both jobs' rows are in flight
+// together and their reductions interleave, where one job per warp left each warp a short
+// dependent chain (load, reduce, load, RoPE, store) and the launch 7.7 waves of them at
+// M = 3658.  Every element takes the operations of qkv_rows_kernel in the same order, so
+// the output bits are the same.
+__global__ void __launch_bounds__(32 * kGlueWarps) qkv_rows256x2_kernel(const QkvArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();  // y comes from the previous kernel
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per_tok = a.shared ? a.heads : a.heads + 2 * a.kv_heads;
+  const int64_t njobs = static_cast<int64_t>(a.t) * per_tok;
+  const int64_t job0 = (static_cast<int64_t>(blockIdx.x) * kGlueWarps + warp) * 2;
+  if (job0 >= njobs) return;
+  uint4 v[2];
+  int tok[2], head[2];
+  bool valid[2];
+  float ss[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int64_t job = job0 + q;
+    valid[q] = job < njobs;
+    tok[q] = valid[q] ? static_cast<int>(job / per_tok) : 0;
+    head[q] = valid[q] ? static_cast<int>(job - static_cast<int64_t>(tok[q]) * per_tok) : 0;
+    v[q] = valid[q] ? ld16(a.y + static_cast<int64_t>(tok[q]) * a.ldy + static_cast<int64_t>(head[q]) * 256 + lane * 8)
+                    : make_uint4(0u, 0u, 0u, 0u);
+    float f[8];
+    unpack8(v[q], f);
+    ss[q] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss[q] = __fmaf_rn(f[e], f[e], ss[q]);  // = ss + x * x, as in rms_factor
+  }
+  float r[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) r[q] = __frsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(ss[q]), 256.f), a.eps));
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const bool is_v = head[q] >= a.heads + a.kv_heads;
+    const __nv_bfloat16* w = head[q] < a.heads ? a.qw : (is_v ? nullptr : a.kw);
+    const uint64_t r2 = f2_pack(r[q], r[q]);
+    uint32_t xw[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+    if (w != nullptr) {
+      const uint4 gv = ld16(w + lane * 8);
+      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        xw[i] = bf16x2_from_f2(f2_mul(f2_mul(f2_from_bf16x2(xw[i]), r2), f2_from_bf16x2(gw[i])));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) xw[i] = bf16x2_from_f2(f2_mul(f2_from_bf16x2(xw[i]), r2));
+    }
+    v[q] = make_uint4(xw[0], xw[1], xw[2], xw[3]);
+  }
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const bool is_v = head[q] >= a.heads + a.kv_heads;
+    // rotate_half partner: lane ^ 16 (32 vectors of 8 columns); every lane takes part in
+    // the shuffles, a v head's lanes discard the result.
+    uint4 p;
+    p.x = __shfl_sync(0xffffffffu, v[q].x, lane ^ 16);
+    p.y = __shfl_sync(0xffffffffu, v[q].y, lane ^ 16);
+    p.z = __shfl_sync(0xffffffffu, v[q].z, lane ^ 16);
+    p.w = __shfl_sync(0xffffffffu, v[q].w, lane ^ 16);
+    if (!is_v && valid[q]) {
+      const int c = lane * 8;
+      const uint4 cv = ld16(a.cos + static_cast<int64_t>(tok[q]) * a.ldcs + c);
+      const uint4 sv = ld16(a.sin + static_cast<int64_t>(tok[q]) * a.ldcs + c);
+      const uint32_t xw[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+      const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+      const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
+      const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+      const uint32_t flip = lane < 16 ? 0x80008000u : 0u;
+      uint32_t ow[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ow[i] = bf16x2_add(bf16x2_mul(xw[i], cw[i]), bf16x2_mul(pw[i] ^ flip, sw[i]));
+      v[q] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+    if (valid[q])
+      *reinterpret_cast<uint4*>(a.out + static_cast<int64_t>(head[q]) * a.ld_head +
+                                static_cast<int64_t>(tok[q]) * a.ld_tok + lane * 8) = v[q];
+  }
+}
+
 }  // namespace w8
 
 namespace w8host {
@@ -573,6 +655,10 @@ extern "C" int w8_qkv_norm_rope_bf16(const uint16_t* y, int64_t ldy, const uint1
   a.d = static_cast<int>(head_dim);
   a.shared = shared != 0;
   const int64_t jobs = t * per_tok;
+  if (head_dim == 256) {  // two (token, head) jobs per warp
+    const unsigned grid2 = static_cast<unsigned>((jobs + 2 * w8::kGlueWarps - 1) / (2 * w8::kGlueWarps));
+    return launch_pdl_glue(w8::qkv_rows256x2_kernel, grid2, a, reinterpret_cast<cudaStream_t>(stream));
+  }
   const unsigned grid = static_cast<unsigned>((jobs + w8::kGlueWarps - 1) / w8::kGlueWarps);
   return launch_pdl_glue(w8::qkv_rows_kernel, grid, a, reinterpret_cast<cudaStream_t>(stream));
 }
