@@ -451,13 +451,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      // The leader's own warps release at CTA scope; the peer's P must be ordered at
-      // cluster scope before the leader's MMA reads it.
+      // P is TMEM data, complete (tcgen05.wait::st) and fenced above: the peer's warps
+      // arrive on the leader's barrier with no cluster-scope release of generic memory.
       if (lane == 0) {
         if (rank == 0)
           mbar_arrive(p_full(b));
         else
-          mbar_arrive_cluster(p_full_l0 + 8u * b);
+          mbar_arrive_tmem_handoff(p_full_l0 + 8u * b);
       }
     }
     if (ok) ok = mbar_wait_bounded(o_ready, 0, abort_flag, &g_attn_status);

@@ -266,6 +266,16 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
+// Arrive on an mbarrier in this CTA or the peer CTA of the pair when what the waiter needs
+// is TMEM that this thread's tcgen05 loads or stores touched: tcgen05.wait has completed
+// them and tcgen05.fence::before_thread_sync orders them before the arrive, and the waiter
+// issues its tcgen05 operations after tcgen05.fence::after_thread_sync.  No generic memory
+// is handed over, so the arrive keeps the default CTA-scope release: a cluster-scope release
+// first drains this thread's outstanding memory operations (about 1000 cycles measured
+// here, on the critical path of every tile).
+__device__ __forceinline__ void mbar_arrive_tmem_handoff(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
 // TMA load into this CTA's shared memory whose completion is counted on `bar`, a
 // shared::cluster barrier address that may lie in the peer CTA of the pair.
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* m, uint32_t bar,

@@ -817,7 +817,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for<EPI>(), 
       if constexpr (EPI != kEpiI32) sxr = row0 + lane < args.m ? __ldg(args.sx + row0 + lane) : 0.f;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
       epilogue_segment<EPI>(args, &tm_c, sg, taddr, row0, nb * args.bn, sxr, stage_base, sbuf, lane,
-                            2 * epi_warps<EPI>(), part, [&] { mbar_arrive_cluster(tempty_leader0 + 8u * acc); });
+                            2 * epi_warps<EPI>(), part, [&] { mbar_arrive_tmem_handoff(tempty_leader0 + 8u * acc); });
     }
     if (lane == 0) bulk_wait_group<0>();  // every store of this warp has landed
   }
