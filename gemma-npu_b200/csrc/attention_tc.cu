@@ -393,9 +393,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         if (!interior) {
           const int hi = min(qpos, a.t - 1) - k0 - 64 * hv;  // valid keys: lo <= key <= hi
           const int lo = a.window > 0 ? qpos - a.window + 1 - k0 - 64 * hv : -1;
+          // The valid keys as one bit per column of each 32-column half, so that each
+          // element takes one bit test instead of two range compares.
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (c < lo || c > hi) sv[c >> 5][c & 31] = __float_as_uint(-INFINITY);
+          for (int j = 0; j < 2; ++j) {
+            const int l = max(lo - 32 * j, 0), h = min(hi - 32 * j, 31);
+            const uint32_t keep = h < l ? 0u : (0xFFFFFFFFu >> (31 - h)) & (0xFFFFFFFFu << l);
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (!((keep >> c) & 1u)) sv[j][c] = __float_as_uint(-INFINITY);
+          }
         }
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
