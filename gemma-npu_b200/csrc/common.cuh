@@ -262,10 +262,6 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
 }
-// Arrive on an mbarrier given by its shared::cluster address (possibly in the peer CTA).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
-}
 // Arrive on an mbarrier in this CTA or the peer CTA of the pair when what the waiter needs
 // is TMEM that this thread's tcgen05 loads or stores touched: tcgen05.wait has completed
 // them and tcgen05.fence::before_thread_sync orders them before the arrive, and the waiter
